@@ -1,0 +1,164 @@
+/*
+ * fftsparse_b200.h -- C ABI of the B200 (sm_100a) FFTSparse prefill hot path.
+ *
+ * The reference operator is `myattn_prefill` in attn_src/fft_attn/my_attn_v7.py
+ * (lines 454-792): block mean pooling, FFT lag correlation, stripe/diffuse head
+ * classification, four auxiliary block masks, and a call into the third-party
+ * `block_sparse_attn_func` CUDA kernel (my_attn_v7.py:775-786).  Every entry
+ * point below replaces one step of that function; `ffts_prefill` replaces the
+ * whole of it.
+ *
+ * Conventions
+ *   - All tensor arguments are DEVICE pointers with explicit element strides.
+ *     The caller owns every buffer (inputs, outputs and the workspace); the
+ *     library allocates nothing per call.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*); no entry
+ *     point synchronises the host with the device.
+ *   - Every entry point returns FFTS_OK (0) or a negative FFTS_E* code; the
+ *     message for the last failure on the calling thread is returned by
+ *     ffts_last_error_string().  No C++ exception crosses this boundary.
+ *   - dtype codes: FFTS_DTYPE_F32 = 0, FFTS_DTYPE_BF16 = 1.
+ *   - q is [B, H, L, D]; k and v are [B, Hkv, L, D] with H % Hkv == 0 (the
+ *     reference's callers pass Hkv == H, i.e. repeat_kv-expanded k/v,
+ *     eval/LongBench/pred.py:204-205; Hkv < H is accepted as GQA).
+ *   - Block masks are packed bits: word (b, h, i, w) bit t <=> key block
+ *     j = 32*w + t is kept for query block i.  Row stride is W = ceil(N/32).
+ *   - The first call on a device uploads the library's constant tables (FFT
+ *     twiddles and log10 weights) to that device with a synchronous copy; make
+ *     that first call (or ffts_init) before any stream capture.
+ */
+#ifndef FFTSPARSE_B200_H
+#define FFTSPARSE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFTS_OK              0
+#define FFTS_E_INVALID     (-1)  /* bad shape, stride, dtype or parameter  */
+#define FFTS_E_UNSUPPORTED (-2)  /* valid but not implemented (e.g. D)     */
+#define FFTS_E_CUDA        (-3)  /* a CUDA runtime call failed              */
+#define FFTS_E_WORKSPACE   (-4)  /* workspace too small or misaligned       */
+#define FFTS_E_DEVICE      (-5)  /* not an sm_100 device                    */
+
+#define FFTS_DTYPE_F32  0
+#define FFTS_DTYPE_BF16 1
+
+#define FFTS_SEL_THRESHOLD 0   /* correlation_selection_mode="threshold" */
+#define FFTS_SEL_TOPK      1   /* correlation_selection_mode="topk"      */
+
+#define FFTS_MAX_DIAG_SAMPLES 64
+
+/*
+ * Derived integer/float parameters of one mask selection.  They are computed
+ * on the host exactly as myattn_prefill derives them (my_attn_v7.py:532-540,
+ * 583-594, 626-634); fftsparse_b200/params.py fills this struct.
+ */
+typedef struct ffts_mask_params {
+  int32_t n_blocks;          /* N = ceil(L / block_size)                       */
+  int32_t block_size;
+  int32_t keep_sink;         /* :537                                           */
+  int32_t keep_recent;       /* :538                                           */
+  int32_t local_window;      /* :539-540                                       */
+  int32_t corr_on;           /* enable_correlation_mask and N > corr top-k :579 */
+  int32_t corr_mode;         /* FFTS_SEL_*                                      */
+  float   corr_threshold;    /* fp32(corr_threshold)          (:206-208)        */
+  float   corr_quantile;     /* fp32(1 - correlation_topk_ratio) (:199)         */
+  int32_t exclude_tau;       /* local_window + 1              (:137)            */
+  int32_t sink_tau_raw;      /* N - keep_sink - 5 (may be < 0) (:138)           */
+  int32_t remote_start;      /* max(local_window, keep_recent-1)+1 (:183-184)   */
+  int32_t n_diag_samples;    /* length of diag_taus                             */
+  int32_t diag_taus[FFTS_MAX_DIAG_SAMPLES]; /* sampled lags (:325-334)          */
+  int32_t stripe_all_diffuse;/* remote_start >= N-1 (:318-321)                  */
+  float   stripe_threshold;  /* fp32(stripe_threshold)         (:363)           */
+  float   qk_topk_ratio;     /* fp32(qk_topk_ratio)            (:271-272)       */
+  int32_t col_on;            /* enable_column_mask and N > 1   (:622)           */
+  int32_t col_start;         /* (:626-634, :429-430)                            */
+  int32_t col_end;
+  int32_t col_topk;          /* (:436-437)                                      */
+  int32_t last_on;           /* enable_last_block_mask         (:558)           */
+  int32_t last_topk;         /* min(128, N)                    (:65)            */
+} ffts_mask_params;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int32_t ffts_version(void);
+
+/* Message for the last error returned on this thread ("" if none). */
+const char *ffts_last_error_string(void);
+
+/* Upload the constant tables to `device` (idempotent, synchronous). */
+int32_t ffts_init(int32_t device);
+
+/*
+ * Block mean pooling.  Replaces block_mean_pool (my_attn_v7.py:105-114) as
+ * called at :554-555: out[b, h, n, d] = mean over the block_size tokens of
+ * block n (the partial last block is zero-padded and still divided by
+ * block_size), rounded to the input dtype.  out is contiguous [B, H, N, D].
+ */
+int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L,
+                  int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_l,
+                  int32_t block_size, void *out, void *stream);
+
+/* Bytes of device workspace ffts_block_mask / ffts_prefill need. */
+int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
+
+/*
+ * Block-mask selection from pooled blocks.  Replaces my_attn_v7.py:546-641:
+ * create_deterministic_block_mask (:74-98), create_last_block_query_mask
+ * (:54-72), batch_fft_cross_correlation (:117-157),
+ * create_correlation_block_mask (:160-227), compute_block_scores (:234-249),
+ * compute_stripe_variance (:301-383), create_qk_topk_block_mask (:256-294),
+ * create_column_block_mask (:390-447) and their union.
+ *
+ *   qb, kb      pooled blocks, contiguous [B, H, N, D] and [B, Hkv, N, D]
+ *   mask_bits   out: uint32 [B, H, N, W]
+ *   row_count   out: int32 [B, H, N] (number of kept blocks per row), or NULL
+ *   corr        out: fp32 [B, H, N] final lag scores (corr_causal), or NULL
+ *   corr_sum    out: fp32 [B, H, N] raw lag sums (corr_causal_sum), or NULL
+ *   is_stripe   out: uint8 [B, H] (1 = stripe head), or NULL
+ *   stripe_var  out: fp32 [B, H] mean normalised diff variance, or NULL
+ *   workspace   >= ffts_mask_workspace_bytes(...) bytes, 256-byte aligned
+ */
+int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B,
+                        int64_t H, int64_t Hkv, int64_t D,
+                        const ffts_mask_params *params, uint32_t *mask_bits,
+                        int32_t *row_count, float *corr, float *corr_sum,
+                        uint8_t *is_stripe, float *stripe_var, void *workspace,
+                        int64_t workspace_bytes, void *stream);
+
+/*
+ * Expand packed bits to the reference's bool block mask [B, H, N, N] (uint8),
+ * i.e. the `base_blockmask` argument at my_attn_v7.py:780.
+ */
+int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_t N,
+                         uint8_t *out, void *stream);
+
+/*
+ * Block-sparse causal attention forward (bf16 in, fp32 accumulate, bf16 out).
+ * Replaces block_sparse_attn_func (my_attn_v7.py:775-786; package
+ * block_sparse_attn 0.0.2) with head_mask_type all 1 (:772), p_dropout 0,
+ * scale 1/sqrt(D).  Query row t of block i attends to key s of block j iff
+ * bit (i, j) is set and (not causal or s <= t).  Rows with no kept key
+ * produce zeros.  out[b, t, h, :] is written at
+ * out + b*out_stride_b + t*out_stride_l + h*out_stride_h (the reference's
+ * [1, L, H*D] return layout, :789-790, when strides are (L*H*D, H*D, D)).
+ * D must be 128; block_size 32, 64 or 128; q/k/v strides multiples of 8
+ * elements with unit stride in D.
+ */
+int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B,
+                             int64_t H, int64_t Hkv, int64_t L, int64_t D,
+                             const int64_t *q_strides /* b,h,l */,
+                             const int64_t *k_strides /* b,h,l */,
+                             const int64_t *v_strides /* b,h,l */,
+                             const uint32_t *mask_bits, int32_t block_size,
+                             int32_t causal, void *out,
+                             const int64_t *out_strides /* b,h,l */,
+                             int32_t *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFTSPARSE_B200_H */
