@@ -1,0 +1,24 @@
+"""fftsparse_b200: the FFTSparse prefill hot path, B200-native (sm_100a).
+
+Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
+
+  myattn_prefill(q, k, v, layer_idx, ...)   drop-in for the reference operator
+  fft_block_mask(q, k, ...)                 the selected block mask + statistics
+  sparse_attention(q, k, v, bits, bs)       block-sparse attention on packed bits
+  pool_blocks(x, bs)                        block mean pooling
+  derive_mask_params(L, ...)                host-side parameter derivation
+  dist.sharded_prefill(...)                 KV-group sharded prefill over NCCL
+"""
+from .params import derive_mask_params, MaskParams  # noqa: F401
+from .prefill import (  # noqa: F401
+    AttentionCache,
+    BlockMask,
+    _attention_cache,
+    fft_block_mask,
+    myattn_prefill,
+    pool_blocks,
+    sparse_attention,
+)
+from ._lib import load as load_library, LIB_PATH  # noqa: F401
+
+__version__ = "0.1.0"

@@ -1,0 +1,81 @@
+"""ctypes binding of libfftsparse_b200.so (the C ABI in include/fftsparse_b200.h).
+
+The library is required: importing the operators without it raises, and there
+is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfftsparse_b200.so")
+
+FFTS_OK = 0
+FFTS_E_INVALID = -1
+FFTS_E_UNSUPPORTED = -2
+FFTS_E_CUDA = -3
+FFTS_E_WORKSPACE = -4
+FFTS_E_DEVICE = -5
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+# (name, restype, argtypes) of every export declared in include/fftsparse_b200.h
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+EXPORTS = {
+    "ffts_version": (_I32, []),
+    "ffts_last_error_string": (ctypes.c_char_p, []),
+    "ffts_init": (_I32, [_I32]),
+    "ffts_pool": (_I32, [_P, _I32, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _P, _P]),
+    "ffts_mask_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64]),
+    "ffts_block_mask": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
+                               _I64, _P]),
+    "ffts_unpack_mask": (_I32, [_P, _I64, _I64, _I64, _P, _P]),
+    "ffts_sparse_attn_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I32,
+                                    _I32, _P, _P, _P, _P]),
+}
+
+_lib = None
+
+
+class FFTSparseError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{message} [ffts code {code}]")
+        self.code = code
+
+
+def load(path: str = LIB_PATH):
+    """Load (once) and return the ctypes handle; raises if the library is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(
+            f"libfftsparse_b200.so not found at {path}; build it with "
+            "`python -m fftsparse_b200.build` (nvcc, sm_100a). There is no CPU fallback.")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc == FFTS_OK:
+        return
+    msg = load().ffts_last_error_string().decode(errors="replace")
+    if rc == FFTS_E_INVALID:
+        raise ValueError(msg)
+    if rc == FFTS_E_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise FFTSparseError(rc, msg)
+
+
+def i64_array(values):
+    arr = (ctypes.c_int64 * len(values))(*[int(v) for v in values])
+    return arr

@@ -1,0 +1,638 @@
+// attn_fwd.cu -- block-sparse causal attention forward on sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces the third-party block_sparse_attn_func (block_sparse_attn 0.0.2) as
+// myattn_prefill calls it (attn_src/fft_attn/my_attn_v7.py:775-786): bf16
+// q/k/v, fp32 accumulation, scale 1/sqrt(D), causal, head h uses mask plane h
+// (head_mask_type all 1, :772), no dropout.  It reads q/k/v in their
+// [B, H, L, D] layout through 4-D TMA descriptors (the reference copies them to
+// [L, H, D] first, :528-530) and writes the output directly in the [B, L, H, D]
+// layout the reference returns (:789-790).
+//
+// One CTA computes one 128-row query tile of one head:
+//   warp 4      TMA producer: Q once, then K and V tiles of every selected
+//               128-column key tile into a two-stage ring (no multicast).
+//   warp 5      MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
+//               accumulator, O += P V into a TMEM accumulator; completion is
+//               signalled with tcgen05.commit on mbarriers.
+//   warps 0-3   softmax: thread r owns query row r (TMEM lane r); reads S with
+//               tcgen05.ld, applies the causal / ragged / sub-block masks, keeps
+//               the running max and sum, rescales O in TMEM when the max moves,
+//               writes P (bf16, 128B-swizzled K-major) to shared memory for the
+//               PV MMA, and finally normalises O and stores it.
+// Unselected key tiles are never loaded.  Every mbarrier wait is bounded: on a
+// time-out the CTA records an error status, stops issuing work, waits (bounded)
+// for its own TMA copies and MMAs in flight, frees TMEM and exits.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "ffts_common.cuh"
+
+namespace ffts {
+namespace attn {
+
+constexpr int kBM = 128;       // query rows per tile
+constexpr int kBN = 128;       // key columns per tile
+constexpr int kD = 128;        // head dim
+constexpr int kStages = 2;     // K/V ring depth
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kTileBytes = kBM * kD * 2;     // 32 KB (two 16 KB swizzle boxes)
+constexpr int kHalfBytes = kTileBytes / 2;   // one [128 rows][64 cols] box
+constexpr int kMaxTiles = 4096;              // key tiles per row of tiles
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s bound on any single wait
+
+// status codes written to the caller's status word
+constexpr int kErrTimeoutProducer = 1;
+constexpr int kErrTimeoutMma = 2;
+constexpr int kErrTimeoutSoftmax = 3;
+
+struct SmemLayout {
+  // offsets from the 1024-byte aligned base
+  static constexpr int q = 0;
+  static constexpr int k = q + kTileBytes;
+  static constexpr int v = k + kStages * kTileBytes;
+  static constexpr int p = v + kStages * kTileBytes;
+  static constexpr int bars = p + kTileBytes;  // 64 bytes of mbarriers each 8 B
+  static constexpr int nbars = 1 + 4 * kStages + 2 + 2 + 2;
+  static constexpr int tmem_slot = bars + nbars * 8;
+  static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
+  static constexpr int list = misc + 16;        // uint16 tile list
+  static constexpr int end = list + kMaxTiles * 2;
+  static constexpr int bytes = end + 1024;      // + alignment slack
+};
+
+// barrier indices
+constexpr int BQ = 0;
+constexpr int BKF = 1;                 // + stage
+constexpr int BVF = BKF + kStages;     // + stage
+constexpr int BKE = BVF + kStages;     // + stage
+constexpr int BVE = BKE + kStages;     // + stage
+constexpr int BSF = BVE + kStages;     // + s buffer
+constexpr int BSE = BSF + 2;           // + s buffer
+constexpr int BOF = BSE + 2;
+constexpr int BPF = BOF + 1;
+constexpr int BDRAIN = BPF + 1;
+
+// ------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false on time-out or when another role has aborted the CTA.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format).
+// SWIZZLE_128B; lbo/sbo in bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3fffu);
+  d |= uint64_t((lbo >> 4) & 0x3fffu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3fffu) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version for sm_100
+  d |= uint64_t(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, bf16 x bf16 -> fp32, M = 128, N = 128.
+constexpr uint32_t idesc_bf16(bool b_mn_major) {
+  return (1u << 4)                        // D format: f32
+         | (1u << 7)                      // A format: bf16
+         | (1u << 10)                     // B format: bf16
+         | (b_mn_major ? (1u << 16) : 0u) // B major-ness
+         | (uint32_t(kBN >> 3) << 17)     // N
+         | (uint32_t(kBM >> 4) << 24);    // M
+}
+
+struct Params {
+  int B, H, Hkv, L, bs, causal;
+  int nq;         // query tiles per head
+  int nblk;       // mask blocks per row (N)
+  int W;          // mask words per row
+  const uint32_t *bits;
+  __nv_bfloat16 *out;
+  int64_t os_b, os_h, os_l;  // output strides (elements)
+  float scale_log2;
+  int *status;
+};
+
+// Tile bits of 32 consecutive key tiles [32*tw, 32*tw+32) for mask row `mrow`
+// when each 128-wide tile covers `sub` mask blocks.
+__device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw, int sub) {
+  if (sub == 1) return tw < W ? row[tw] : 0u;
+  uint32_t out = 0;
+  for (int t = 0; t < 32; ++t) {
+    const int blk0 = (tw * 32 + t) * sub;
+    const int w = blk0 >> 5;
+    if (w >= W) break;
+    const uint32_t grp = (row[w] >> (blk0 & 31)) & ((1u << sub) - 1u);
+    out |= uint32_t(grp != 0) << t;
+  }
+  return out;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    sparse_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, Params prm) {
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + SmemLayout::bars;
+  auto bar = [&](int i) { return bar0 + 8u * uint32_t(i); };
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + SmemLayout::misc);
+  int *ntiles_sh = reinterpret_cast<int *>(smem + SmemLayout::misc + 4);
+  uint16_t *list = reinterpret_cast<uint16_t *>(smem + SmemLayout::list);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SmemLayout::tmem_slot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // ---- tile coordinates: (b, kv head, query tile descending, head in group)
+  const int G = prm.H / prm.Hkv;
+  int x = blockIdx.x;
+  const int hg = x % G;
+  x /= G;
+  const int qt = prm.nq - 1 - (x % prm.nq);
+  x /= prm.nq;
+  const int kvh = x % prm.Hkv;
+  const int b = x / prm.Hkv;
+  const int h = kvh * G + hg;
+  const int sub = kBM / prm.bs;  // mask blocks per tile edge
+
+  // ---- setup: barriers, TMEM, tile list
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(bar(BQ), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(BKF + s), 1);
+      mbar_init(bar(BVF + s), 1);
+      mbar_init(bar(BKE + s), 1);
+      mbar_init(bar(BVE + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(BSF + s), 1);
+      mbar_init(bar(BSE + s), 128);
+    }
+    mbar_init(bar(BOF), 1);
+    mbar_init(bar(BPF), 128);
+    mbar_init(bar(BDRAIN), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_map(&tm_q);
+    prefetch_map(&tm_k);
+    prefetch_map(&tm_v);
+  }
+  // Key tiles to visit: OR of the sub x sub mask blocks of each tile, causal cut.
+  const int nkv_all = (prm.L + kBN - 1) / kBN;
+  const int nkv = prm.causal ? min(qt + 1, nkv_all) : nkv_all;
+  const int TW = (nkv + 31) / 32;
+  if (warp == 0) {
+    int base = 0;
+    for (int c = 0; c < TW; c += 32) {
+      const int tw = c + lane;
+      uint32_t word = 0;
+      if (tw < TW) {
+        for (int s = 0; s < sub; ++s) {
+          const int mrow = qt * sub + s;
+          if (mrow < prm.nblk) {
+            const uint32_t *row = prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + mrow) * prm.W;
+            word |= tile_word(row, prm.W, tw, sub);
+          }
+        }
+        const int lim = nkv - tw * 32;  // tiles valid in this word
+        if (lim < 32) word &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
+      }
+      const int cntw = __popc(word);
+      int incl = cntw;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      int pos = base + incl - cntw;
+      while (word) {
+        const int t = __ffs(word) - 1;
+        word &= word - 1;
+        list[pos++] = uint16_t(tw * 32 + t);
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) *ntiles_sh = base;
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int ntiles = *ntiles_sh;
+  const uint32_t tm_s0 = tmem, tm_o = tmem + 256;
+
+  if (warp == 4) {
+    // ================================================================ TMA producer
+    if (lane == 0 && ntiles > 0) {
+      int issued_k = 0, issued_v = 0;
+      bool ok = true;
+      mbar_arrive_tx(bar(BQ), kTileBytes);
+      tma_load_4d(sbase + SmemLayout::q, &tm_q, bar(BQ), 0, qt * kBM, h, b);
+      tma_load_4d(sbase + SmemLayout::q + kHalfBytes, &tm_q, bar(BQ), 64, qt * kBM, h, b);
+      for (int n = 0; n < ntiles && ok; ++n) {
+        const int s = n % kStages;
+        const uint32_t par = ((n / kStages) & 1) ^ 1;
+        const int j = list[n];
+        if (!mbar_wait(bar(BKE + s), par, abort_flag)) { ok = false; break; }
+        mbar_arrive_tx(bar(BKF + s), kTileBytes);
+        const uint32_t kd = sbase + SmemLayout::k + s * kTileBytes;
+        tma_load_4d(kd, &tm_k, bar(BKF + s), 0, j * kBN, kvh, b);
+        tma_load_4d(kd + kHalfBytes, &tm_k, bar(BKF + s), 64, j * kBN, kvh, b);
+        ++issued_k;
+        if (!mbar_wait(bar(BVE + s), par, abort_flag)) { ok = false; break; }
+        mbar_arrive_tx(bar(BVF + s), kTileBytes);
+        const uint32_t vd = sbase + SmemLayout::v + s * kTileBytes;
+        tma_load_4d(vd, &tm_v, bar(BVF + s), 0, j * kBN, kvh, b);
+        tma_load_4d(vd + kHalfBytes, &tm_v, bar(BVF + s), 64, j * kBN, kvh, b);
+        ++issued_v;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(prm.status, 0, kErrTimeoutProducer);
+        // wait (bounded, ignoring the abort flag) for the copies this thread issued
+        volatile int never = 0;
+        mbar_wait(bar(BQ), 0, &never);
+        for (int n = max(0, issued_k - kStages); n < issued_k; ++n)
+          mbar_wait(bar(BKF + n % kStages), (n / kStages) & 1, &never);
+        for (int n = max(0, issued_v - kStages); n < issued_v; ++n)
+          mbar_wait(bar(BVF + n % kStages), (n / kStages) & 1, &never);
+      }
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t idS = idesc_bf16(false), idPV = idesc_bf16(true);
+      bool ok = mbar_wait(bar(BQ), 0, abort_flag);
+      fence_after();
+      auto issue_pv = [&](int m) -> bool {
+        const int s = m % kStages;
+        if (!mbar_wait(bar(BVF + s), (m / kStages) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
+        fence_after();
+        const uint32_t vb = sbase + SmemLayout::v + s * kTileBytes;
+        const uint32_t pb = sbase + SmemLayout::p;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = smem_desc(pb + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc(vb + kk * 2048, kHalfBytes, 1024);
+          umma_f16(tm_o, ad, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(BOF));
+        umma_commit(bar(BVE + s));
+        return true;
+      };
+      for (int n = 0; n < ntiles && ok; ++n) {
+        const int s = n % kStages, sb = n & 1;
+        ok = mbar_wait(bar(BKF + s), (n / kStages) & 1, abort_flag);
+        if (ok && n >= 2) ok = mbar_wait(bar(BSE + sb), ((n >> 1) - 1) & 1, abort_flag);
+        if (!ok) break;
+        fence_after();
+        const uint32_t kb = sbase + SmemLayout::k + s * kTileBytes;
+        const uint32_t qb = sbase + SmemLayout::q;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          umma_f16(tm_s0 + sb * 128, smem_desc(qb + off, 16, 1024), smem_desc(kb + off, 16, 1024), idS,
+                   kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar(BSF + sb));
+        umma_commit(bar(BKE + s));
+        if (n >= 1) ok = issue_pv(n - 1);
+      }
+      if (ok) ok = issue_pv(ntiles - 1);
+      if (!ok) {
+        *abort_flag = 1;
+        atomicCAS(prm.status, 0, kErrTimeoutMma);
+      }
+      // drain: wait (bounded) until every MMA this thread issued has completed
+      umma_commit(bar(BDRAIN));
+      volatile int never = 0;
+      mbar_wait(bar(BDRAIN), 0, &never);
+    }
+  } else {
+    // ================================================================ softmax (warps 0-3)
+    const int r = threadIdx.x;  // query row within the tile == TMEM lane
+    const int row_g = qt * kBM + r;
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    const int mrow = qt * sub + r / prm.bs;
+    const uint32_t *rowbits =
+        prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + min(mrow, prm.nblk - 1)) * prm.W;
+    uint8_t *pbase = smem + SmemLayout::p;
+    for (int n = 0; n < ntiles; ++n) {
+      const int sb = n & 1;
+      const int j = list[n];
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
+      fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tm_s0 + sb * 128 + lane_off + c * 32, s + c * 32);
+      tmem_wait_ld();
+      fence_before();
+      mbar_arrive(bar(BSE + sb));
+      // masks: causal diagonal, ragged end, sub-block selection
+      const int col0 = j * kBN;
+      int lim = prm.L - col0;                     // columns < lim are in range
+      if (prm.causal && j == qt) lim = min(lim, r + 1);
+      uint32_t subm = 0xffffffffu;
+      if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const bool keep = c < lim && ((subm >> (c / prm.bs)) & 1u);
+        s[c] = keep ? s[c] : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+      const float alpha = fast_exp2((m_run - m_use) * prm.scale_log2);
+      const float moff = m_use * prm.scale_log2;
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        s[c] = fast_exp2(fmaf(s[c], prm.scale_log2, -moff));
+        rs += s[c];
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      if (n >= 1) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(BOF), (n - 1) & 1, abort_flag))) { ok = false; break; }
+        fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(tm_o + lane_off + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(tm_o + lane_off + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row r -> shared memory, K-major with the 128-byte swizzle
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(s[ch * 8 + 2 * e], s[ch * 8 + 2 * e + 1]);
+          w[e] = *reinterpret_cast<const uint32_t *>(&pr);
+        }
+        const int half = ch >> 3, c16 = ch & 7;
+        uint8_t *dst = pbase + half * kHalfBytes + r * 128 + ((c16 ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async();
+      fence_before();
+      mbar_arrive(bar(BPF));
+    }
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(BOF), (ntiles - 1) & 1, abort_flag));
+    if (!ok) {
+      *abort_flag = 1;
+      atomicCAS(prm.status, 0, kErrTimeoutSoftmax);
+    }
+    fence_after();
+    // epilogue: O / l -> bf16 -> out[b, row, h, :]
+    const bool store = row_g < prm.L;
+    __nv_bfloat16 *dst = prm.out + int64_t(b) * prm.os_b + int64_t(row_g) * prm.os_l + int64_t(h) * prm.os_h;
+    const float inv_l = (ok && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      if (ntiles > 0 && ok) {
+        tmem_ld32(tm_o + lane_off + c * 32, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0.0f;
+      }
+      if (store) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 pr =
+                __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv_l, o[q4 * 8 + 2 * e + 1] * inv_l);
+            w[e] = *reinterpret_cast<const uint32_t *>(&pr);
+          }
+          *reinterpret_cast<uint4 *>(dst + c * 32 + q4 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+
+  // ---- teardown
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 5) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
+// ----------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+static int make_map(CUtensorMap *map, const void *base, int64_t L, int64_t Hx, int64_t B, const int64_t *st) {
+  auto enc = get_encode();
+  if (!enc) {
+    set_error(FFTS_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    return FFTS_E_CUDA;
+  }
+  cuuint64_t dims[4] = {cuuint64_t(kD), cuuint64_t(L), cuuint64_t(Hx), cuuint64_t(B)};
+  cuuint64_t strides[3] = {cuuint64_t(st[2]) * 2, cuuint64_t(st[1]) * 2, cuuint64_t(st[0]) * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error(FFTS_E_INVALID, "cuTensorMapEncodeTiled failed (%d): check 16-byte aligned base and strides", int(r));
+    return FFTS_E_INVALID;
+  }
+  return FFTS_OK;
+}
+
+__device__ int g_attn_status_sink;
+
+}  // namespace attn
+
+int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv, int64_t L,
+                    int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs, const uint32_t *bits, int bs,
+                    int causal, void *out, const int64_t *os, int32_t *status, cudaStream_t stream) {
+  using namespace attn;
+  FFTS_REQUIRE(q && k && v && bits && out && qs && ks && vs && os, "sparse_attn: NULL argument");
+  FFTS_REQUIRE(D == kD, "sparse_attn: head_dim must be 128 (got %lld)", (long long)D);
+  FFTS_REQUIRE(bs == 32 || bs == 64 || bs == 128, "sparse_attn: block_size must be 32, 64 or 128 (got %d)", bs);
+  FFTS_REQUIRE(B >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0 && L >= 1, "sparse_attn: bad shape");
+  const int64_t nblk = ceil_div(L, bs);
+  const int64_t nq = ceil_div(L, kBM);
+  FFTS_REQUIRE(nblk <= kMaxBlocks && nq <= kMaxTiles, "sparse_attn: sequence too long for the tile list");
+  FFTS_REQUIRE(L < (int64_t(1) << 31) && B * H * nq < (int64_t(1) << 31), "sparse_attn: grid too large");
+  for (const int64_t *st : {qs, ks, vs})
+    FFTS_REQUIRE(st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0 && st[2] >= D,
+                 "sparse_attn: q/k/v strides must be multiples of 8 elements (16 bytes)");
+  FFTS_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(k) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+               "sparse_attn: tensors must be 16-byte aligned");
+  FFTS_REQUIRE(os[0] % 8 == 0 && os[1] % 8 == 0 && os[2] % 8 == 0, "sparse_attn: output strides must be 16-byte multiples");
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, L, H, B, qs);
+  if (!rc) rc = make_map(&mk, k, L, Hkv, B, ks);
+  if (!rc) rc = make_map(&mv, v, L, Hkv, B, vs);
+  if (rc) return rc;
+  Params p{};
+  p.B = int(B); p.H = int(H); p.Hkv = int(Hkv); p.L = int(L); p.bs = bs; p.causal = causal ? 1 : 0;
+  p.nq = int(nq); p.nblk = int(nblk); p.W = int(ceil_div(nblk, 32));
+  p.bits = bits;
+  p.out = static_cast<__nv_bfloat16 *>(out);
+  p.os_b = os[0]; p.os_h = os[1]; p.os_l = os[2];
+  p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
+  if (status) {
+    p.status = status;
+  } else {
+    void *sink = nullptr;
+    FFTS_CUDA(cudaGetSymbolAddress(&sink, g_attn_status_sink));
+    p.status = static_cast<int *>(sink);
+  }
+  FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes));
+  const unsigned grid = unsigned(B * H * nq);
+  sparse_attn_kernel<<<grid, kThreads, SmemLayout::bytes, stream>>>(mq, mk, mv, p);
+  FFTS_CUDA(cudaGetLastError());
+  return FFTS_OK;
+}
+
+}  // namespace ffts

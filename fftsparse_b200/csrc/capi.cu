@@ -1,0 +1,124 @@
+// capi.cu -- the extern "C" boundary of libfftsparse_b200.so.
+//
+// Each export validates its arguments, enqueues kernels on the caller's stream
+// and returns FFTS_OK or a negative FFTS_E* code; the message of the last
+// failure on the calling thread is kept for ffts_last_error_string().
+
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "ffts_common.cuh"
+
+namespace ffts {
+
+static thread_local std::string g_last_error;
+
+void set_error(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = std::string(buf) + " (code " + std::to_string(code) + ")";
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+  set_error(FFTS_E_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
+  return FFTS_E_CUDA;
+}
+
+int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t sb,
+                int64_t sh, int64_t sl, int bs, void *out, cudaStream_t stream);
+int64_t mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
+int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+               const ffts_mask_params *params, uint32_t *bits, int32_t *row_count, float *corr,
+               float *csum, uint8_t *is_stripe, float *svar, void *workspace, int64_t ws_bytes,
+               cudaStream_t stream);
+int unpack_mask(const uint32_t *bits, int64_t B, int64_t H, int64_t N, uint8_t *out, cudaStream_t stream);
+int ensure_tables();
+int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
+                    int64_t L, int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs,
+                    const uint32_t *bits, int bs, int causal, void *out, const int64_t *os,
+                    int32_t *status, cudaStream_t stream);
+
+static int check_device() {
+  int dev = 0;
+  FFTS_CUDA(cudaGetDevice(&dev));
+  int major = 0;
+  FFTS_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  if (major != 10) {
+    set_error(FFTS_E_DEVICE, "device %d has compute capability %d.x; this library targets sm_100a", dev, major);
+    return FFTS_E_DEVICE;
+  }
+  return FFTS_OK;
+}
+
+}  // namespace ffts
+
+using namespace ffts;
+
+extern "C" {
+
+int32_t ffts_version(void) { return 100; }
+
+const char *ffts_last_error_string(void) { return g_last_error.c_str(); }
+
+int32_t ffts_init(int32_t device) {
+  g_last_error.clear();
+  int prev = 0;
+  FFTS_CUDA(cudaGetDevice(&prev));
+  if (device != prev) FFTS_CUDA(cudaSetDevice(device));
+  int rc = check_device();
+  if (rc == FFTS_OK) rc = ensure_tables();
+  if (device != prev) cudaSetDevice(prev);
+  return rc;
+}
+
+int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L, int64_t D,
+                  int64_t stride_b, int64_t stride_h, int64_t stride_l, int32_t block_size, void *out,
+                  void *stream) {
+  g_last_error.clear();
+  FFTS_REQUIRE(x != nullptr && out != nullptr, "ffts_pool: NULL pointer");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_pool(x, dtype, B, H, L, D, stride_b, stride_h, stride_l, block_size, out,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D) {
+  if (B <= 0 || H <= 0 || N <= 0 || D <= 0) return 0;
+  return mask_workspace_bytes(B, H, N, D);
+}
+
+int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B, int64_t H, int64_t Hkv,
+                        int64_t D, const ffts_mask_params *params, uint32_t *mask_bits, int32_t *row_count,
+                        float *corr, float *corr_sum, uint8_t *is_stripe, float *stripe_var, void *workspace,
+                        int64_t workspace_bytes, void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return block_mask(qb, kb, dtype, B, H, Hkv, D, params, mask_bits, row_count, corr, corr_sum, is_stripe,
+                    stripe_var, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_t N, uint8_t *out,
+                         void *stream) {
+  g_last_error.clear();
+  return unpack_mask(mask_bits, B, H, N, out, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
+                             int64_t L, int64_t D, const int64_t *q_strides, const int64_t *k_strides,
+                             const int64_t *v_strides, const uint32_t *mask_bits, int32_t block_size,
+                             int32_t causal, void *out, const int64_t *out_strides, int32_t *status,
+                             void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
+                         causal, out, out_strides, status, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

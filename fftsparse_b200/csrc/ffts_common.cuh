@@ -1,0 +1,101 @@
+// ffts_common.cuh -- helpers shared by the FFTSparse sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/fftsparse_b200.h"
+
+namespace ffts {
+
+// ------------------------------------------------------------ error state
+void set_error(int code, const char *fmt, ...);
+int cuda_status(cudaError_t e, const char *what);
+
+#define FFTS_REQUIRE(cond, ...)                          \
+  do {                                                   \
+    if (!(cond)) {                                       \
+      ::ffts::set_error(FFTS_E_INVALID, __VA_ARGS__);    \
+      return FFTS_E_INVALID;                             \
+    }                                                    \
+  } while (0)
+
+#define FFTS_CUDA(call)                                           \
+  do {                                                            \
+    cudaError_t _e = (call);                                      \
+    if (_e != cudaSuccess) return ::ffts::cuda_status(_e, #call); \
+  } while (0)
+
+// ------------------------------------------------------- element helpers
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static constexpr int kVec = 4;  // elements per 16-byte vector
+  __device__ static inline float to_f32(float x) { return x; }
+  __device__ static inline float from_f32(float x) { return x; }
+  // value as stored in the dtype, returned as fp32 (identity for fp32)
+  __device__ static inline float round_f32(float x) { return x; }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ static inline float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ static inline __nv_bfloat16 from_f32(float x) { return __float2bfloat16_rn(x); }
+  __device__ static inline float round_f32(float x) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  }
+};
+
+// Load 16 bytes and widen to fp32.
+template <typename T>
+__device__ inline void load_vec_f32(const T *p, float *out);
+
+template <>
+__device__ inline void load_vec_f32<float>(const float *p, float *out) {
+  const float4 v = *reinterpret_cast<const float4 *>(p);
+  out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+}
+
+template <>
+__device__ inline void load_vec_f32<__nv_bfloat16>(const __nv_bfloat16 *p, float *out) {
+  const uint4 v = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+// Monotone 32-bit key of a float: larger value -> larger key; -0 maps to +0.
+__device__ __forceinline__ uint32_t f32_key(float f) {
+  if (f == 0.0f) f = 0.0f;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float key_f32(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+__host__ __device__ __forceinline__ int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+__host__ __device__ __forceinline__ int ilog2_ceil(int64_t m) {
+  int r = 0;
+  while ((int64_t(1) << r) < m) ++r;
+  return r;
+}
+
+constexpr int kMaxBlocks = 4096;        // N limit (FFT size <= 8192)
+constexpr int kMaxFFT = 8192;           // largest FFT length
+constexpr int kDChunk = 8;              // channels per partial-spectrum CTA
+constexpr int kLanes = 256;             // canonical reduction lanes
+
+}  // namespace ffts

@@ -1,0 +1,855 @@
+// mask.cu -- FFTSparse block-mask selection on sm_100a.
+//
+// Replaces the selection half of myattn_prefill (attn_src/fft_attn/my_attn_v7.py
+// :532-641) with four kernels that keep every decision on the device (the
+// reference syncs the host at :273 and :597 and loops over sampled diagonals on
+// the host at :342-357):
+//
+//   fft_partial_kernel   per (b, h, 8-channel chunk): zero-padded FFT of
+//                        z = q + i k per channel (warp-shuffle butterflies for
+//                        spans < 32, shared-memory butterflies above), cross
+//                        spectrum Q conj(K) summed over the chunk's channels.
+//                        (batch_fft_cross_correlation, :117-131)
+//   corr_select_kernel   per (b, h): sum of chunk spectra, one inverse FFT,
+//                        the reference's post-processing (:132-155), and the
+//                        lag selection by normalised threshold or quantile
+//                        (create_correlation_block_mask, :195-208).
+//   head_stats_kernel    per (b, h): stripe statistic over sampled diagonals
+//                        (compute_stripe_variance, :301-383), hot key columns
+//                        (create_column_block_mask, :390-447) and the last
+//                        query row's top-k (create_last_block_query_mask, :54-72).
+//   mask_build_kernel    per (b, h, row tile): per-row QK top-k for diffuse
+//                        heads (create_qk_topk_block_mask, :256-294) and the
+//                        union with the prior, Toeplitz lag, column and last-row
+//                        masks (:74-98, :212-225, :606-641) into packed bits.
+//
+// Arithmetic is the canonical one restated by oracle/ffts_oracle.c: fp32 FFT
+// butterflies with no contraction (__fmul_rn/__fadd_rn), exact-product fp64
+// dot products for block scores, fp64 reductions in a fixed 256-lane order, and
+// top-k ties broken by lowest block index.
+
+#include <math.h>
+#include <stdarg.h>
+
+#include <mutex>
+#include <vector>
+
+#include "ffts_common.cuh"
+
+namespace ffts {
+
+// ---------------------------------------------------------------- tables
+// Forward twiddles of the largest FFT: g_twiddle[j] = (cos a, -sin a) with
+// a = 2*pi*j / kMaxFFT; an FFT of length M uses entry j * (kMaxFFT / M), which is
+// bit-identical to evaluating a = 2*pi*j / M directly (power-of-two scaling).
+__device__ float2 g_twiddle[kMaxFFT / 2];
+// g_log10[n] = (float)log10(n), n <= kMaxBlocks
+__device__ float g_log10[kMaxBlocks + 1];
+
+static std::mutex g_table_mutex;
+static std::vector<int> g_table_ready;
+
+int ensure_tables() {
+  int dev = 0;
+  FFTS_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(g_table_mutex);
+  if (dev < int(g_table_ready.size()) && g_table_ready[dev]) return FFTS_OK;
+  std::vector<float2> tw(kMaxFFT / 2);
+  for (int j = 0; j < kMaxFFT / 2; ++j) {
+    const double a = (2.0 * M_PI * (double)j) / (double)kMaxFFT;
+    tw[j] = make_float2((float)cos(a), (float)(-sin(a)));
+  }
+  std::vector<float> lg(kMaxBlocks + 1);
+  lg[0] = -INFINITY;
+  for (int n = 1; n <= kMaxBlocks; ++n) lg[n] = (float)log10((double)n);
+  FFTS_CUDA(cudaMemcpyToSymbol(g_twiddle, tw.data(), tw.size() * sizeof(float2)));
+  FFTS_CUDA(cudaMemcpyToSymbol(g_log10, lg.data(), lg.size() * sizeof(float)));
+  if (dev >= int(g_table_ready.size())) g_table_ready.resize(dev + 1, 0);
+  g_table_ready[dev] = 1;
+  return FFTS_OK;
+}
+
+// ------------------------------------------------------------------- FFT
+__device__ __forceinline__ uint32_t bitrev(uint32_t x, int bits) { return __brev(x) >> (32 - bits); }
+
+// Spans h = 1..16 of a radix-2 DIT on a warp-held 32-element segment
+// (lane = index bits 0..4).  The upper element of each pair forms t = w*b and
+// sends it; the lower sends a; the lower keeps a + t, the upper a - t.
+__device__ __forceinline__ void fft_warp_stages(float &re, float &im, int lane, int M,
+                                                const float2 *tw, bool inverse) {
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+    const bool upper = lane & h;
+    float sr = re, si = im;
+    if (upper) {
+      float2 w = tw[(lane & (h - 1)) * (M / (2 * h))];
+      if (inverse) w.y = -w.y;
+      const float p1 = __fmul_rn(w.x, re), p2 = __fmul_rn(w.y, im);
+      const float p3 = __fmul_rn(w.x, im), p4 = __fmul_rn(w.y, re);
+      sr = __fsub_rn(p1, p2);
+      si = __fadd_rn(p3, p4);
+    }
+    const float rr = __shfl_xor_sync(0xffffffffu, sr, h);
+    const float ri = __shfl_xor_sync(0xffffffffu, si, h);
+    if (upper) {
+      re = __fsub_rn(rr, sr);
+      im = __fsub_rn(ri, si);
+    } else {
+      re = __fadd_rn(sr, rr);
+      im = __fadd_rn(si, ri);
+    }
+  }
+}
+
+// nfft independent length-M transforms stored back to back in x (input in
+// bit-reversed order, output in natural order).  All threads of the CTA call.
+__device__ void fft_block(float2 *x, int M, int nfft, const float2 *tw, bool inverse) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int nseg = nfft * (M >> 5);
+  for (int seg = warp; seg < nseg; seg += nwarps) {
+    float2 v = x[seg * 32 + lane];
+    fft_warp_stages(v.x, v.y, lane, M, tw, inverse);
+    x[seg * 32 + lane] = v;
+  }
+  __syncthreads();
+  const int half = M >> 1;
+  const int lh = ilog2_ceil(half);
+  for (int h = 32; h < M; h <<= 1) {
+    const int lgh = ilog2_ceil(h);
+    const int step = M / (2 * h);
+    for (int b = threadIdx.x; b < nfft * half; b += blockDim.x) {
+      const int f = b >> lh, bb = b & (half - 1);
+      const int g = bb >> lgh, k = bb & (h - 1);
+      float2 *X = x + f * M;
+      const int ia = g * 2 * h + k, ib = ia + h;
+      float2 w = tw[k * step];
+      if (inverse) w.y = -w.y;
+      const float2 bv = X[ib], av = X[ia];
+      const float p1 = __fmul_rn(w.x, bv.x), p2 = __fmul_rn(w.y, bv.y);
+      const float p3 = __fmul_rn(w.x, bv.y), p4 = __fmul_rn(w.y, bv.x);
+      const float tr = __fsub_rn(p1, p2), ti = __fadd_rn(p3, p4);
+      X[ia] = make_float2(__fadd_rn(av.x, tr), __fadd_rn(av.y, ti));
+      X[ib] = make_float2(__fsub_rn(av.x, tr), __fsub_rn(av.y, ti));
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) fft_partial_kernel(const T *__restrict__ qb,
+                                                          const T *__restrict__ kb, int H, int Hkv,
+                                                          int N, int D, int M, int nf,
+                                                          float2 *__restrict__ partial) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float2 *tw = reinterpret_cast<float2 *>(smem_raw);  // [M/2]
+  float2 *acc = tw + M / 2;                            // [M/2 + 1]
+  float2 *buf = acc + (M / 2 + 1) + 1;                 // [nf][M] (16-byte aligned)
+  const int F = M / 2 + 1;
+  const int bits = ilog2_ceil(M);
+  const int chunk = blockIdx.x, nchunk = gridDim.x;
+  const int bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const T *q = qb + int64_t(bh) * N * D;
+  const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
+  const int stride = kMaxFFT / M;
+  for (int j = threadIdx.x; j < M / 2; j += blockDim.x) tw[j] = g_twiddle[j * stride];
+  for (int f = threadIdx.x; f < F; f += blockDim.x) acc[f] = make_float2(0.0f, 0.0f);
+  const int d_lo = chunk * kDChunk, d_hi = min(D, d_lo + kDChunk);
+  for (int d0 = d_lo; d0 < d_hi; d0 += nf) {
+    const int nb = min(nf, d_hi - d0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nb * M; e += blockDim.x) {
+      const int fi = e / M, t = e - fi * M;
+      float2 z = make_float2(0.0f, 0.0f);
+      if (t < N) z = make_float2(Elem<T>::to_f32(q[int64_t(t) * D + d0 + fi]),
+                                 Elem<T>::to_f32(k[int64_t(t) * D + d0 + fi]));
+      buf[fi * M + bitrev(t, bits)] = z;
+    }
+    __syncthreads();
+    fft_block(buf, M, nb, tw, false);
+    for (int f = threadIdx.x; f < F; f += blockDim.x) {
+      float2 a2 = acc[f];
+      const int g = (M - f) & (M - 1);
+      for (int fi = 0; fi < nb; ++fi) {
+        const float2 A = buf[fi * M + f], Bv = buf[fi * M + g];
+        const float qr = __fmul_rn(0.5f, __fadd_rn(A.x, Bv.x));
+        const float qi = __fmul_rn(0.5f, __fsub_rn(A.y, Bv.y));
+        const float kr = __fmul_rn(0.5f, __fadd_rn(A.y, Bv.y));
+        const float ki = __fmul_rn(0.5f, __fsub_rn(Bv.x, A.x));
+        const float cr = __fadd_rn(__fmul_rn(qr, kr), __fmul_rn(qi, ki));
+        const float ci = __fsub_rn(__fmul_rn(qi, kr), __fmul_rn(qr, ki));
+        a2.x = __fadd_rn(a2.x, cr);
+        a2.y = __fadd_rn(a2.y, ci);
+      }
+      acc[f] = a2;
+    }
+  }
+  __syncthreads();
+  float2 *out = partial + (int64_t(bh) * nchunk + chunk) * F;
+  for (int f = threadIdx.x; f < F; f += blockDim.x) out[f] = acc[f];
+}
+
+// ------------------------------------------------------- block selection
+// Ascending-rank selection of 32-bit keys (keys[0..n)) by 8-bit radix passes.
+__device__ uint32_t block_select_rank(const uint32_t *keys, int n, int rank, int *hist, int *bc) {
+  uint32_t prefix = 0, mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t kk = keys[i];
+      if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int c = 0, dsel = 255;
+      for (int d = 0; d < 256; ++d) {
+        if (c + hist[d] > rank) { dsel = d; break; }
+        c += hist[d];
+      }
+      bc[0] = dsel;
+      bc[1] = c;
+    }
+    __syncthreads();
+    rank -= bc[1];
+    prefix |= uint32_t(bc[0]) << shift;
+    mask |= 0xffu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Set in `words` (pre-zeroed, indexed by absolute position) the bits of the k
+// largest keys among keys[lo..hi); ties are broken by lowest index.
+__device__ void block_topk_bits(const uint32_t *keys, int lo, int hi, int k, uint32_t *words,
+                                int *hist, int *bc) {
+  const int n = hi - lo;
+  if (n <= 0 || k <= 0) return;
+  if (k >= n) {
+    for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) atomicOr(&words[j >> 5], 1u << (j & 31));
+    __syncthreads();
+    return;
+  }
+  const uint32_t T = block_select_rank(keys + lo, n, n - k, hist, bc);
+  // number of keys strictly greater than T
+  if (threadIdx.x == 0) bc[2] = 0;
+  __syncthreads();
+  int local = 0;
+  for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) local += keys[j] > T;
+  for (int o = 16; o; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(&bc[2], local);
+  __syncthreads();
+  const int need = k - bc[2];
+  // walk indices in order; equal keys take the first `need` slots
+  int *wsum = hist;  // reuse: per-warp counts
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int base = 0;
+  for (int c = lo; c < hi; c += blockDim.x) {
+    const int j = c + threadIdx.x;
+    const bool in = j < hi;
+    const bool eq = in && keys[j] == T;
+    const unsigned bal = __ballot_sync(0xffffffffu, eq);
+    __syncthreads();
+    if (lane == 0) wsum[warp] = __popc(bal);
+    __syncthreads();
+    int before = base;
+    for (int w = 0; w < warp; ++w) before += wsum[w];
+    before += __popc(bal & ((1u << lane) - 1));
+    int tot = 0;
+    for (int w = 0; w < nw; ++w) tot += wsum[w];
+    if (in && (keys[j] > T || (eq && before < need))) atomicOr(&words[j >> 5], 1u << (j & 31));
+    base += tot;
+  }
+  __syncthreads();
+}
+
+// -------------------------------------------------- correlation + lag select
+__global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restrict__ partial,
+                                                          int nchunk, int N, int M,
+                                                          ffts_mask_params p,
+                                                          float *__restrict__ corr_out,
+                                                          float *__restrict__ csum_out,
+                                                          uint32_t *__restrict__ tausel) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float2 *tw = reinterpret_cast<float2 *>(smem_raw);  // [M/2]
+  float2 *X = tw + M / 2;                             // [M]
+  float *corr = reinterpret_cast<float *>(X + M);     // [N]
+  uint32_t *keys = reinterpret_cast<uint32_t *>(corr + N);  // [N]
+  __shared__ int hist[256];
+  __shared__ int bc[4];
+  __shared__ float red[32];
+  const int bh = blockIdx.x;
+  const int F = M / 2 + 1;
+  const int bits = ilog2_ceil(M);
+  const int W = (N + 31) / 32;
+  const int stride = kMaxFFT / M;
+  for (int j = threadIdx.x; j < M / 2; j += blockDim.x) tw[j] = g_twiddle[j * stride];
+  const float2 *part = partial + int64_t(bh) * nchunk * F;
+  for (int f = threadIdx.x; f < F; f += blockDim.x) {
+    float2 s = make_float2(0.0f, 0.0f);
+    for (int c = 0; c < nchunk; ++c) {
+      const float2 v = part[int64_t(c) * F + f];
+      s.x = __fadd_rn(s.x, v.x);
+      s.y = __fadd_rn(s.y, v.y);
+    }
+    X[bitrev(f, bits)] = s;
+    if (f > 0 && f < M / 2) X[bitrev(M - f, bits)] = make_float2(s.x, -s.y);
+  }
+  __syncthreads();
+  fft_block(X, M, 1, tw, true);
+  const float invM = 1.0f / (float)M;
+  const int ex = p.exclude_tau, sraw = p.sink_tau_raw;
+  const int s0 = sraw >= 0 ? sraw : max(0, N + sraw);
+  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+    const float cs = __fmul_rn(X[t].x, invM);
+    if (csum_out) csum_out[int64_t(bh) * N + t] = cs;
+    float c = __fdiv_rn(cs, (float)(N - t));
+    if (t < ex || t >= s0) c = 0.0f;
+    corr[t] = c;
+  }
+  __syncthreads();
+  if (ex < sraw) {
+    float mn = INFINITY;
+    for (int t = ex + threadIdx.x; t < sraw; t += blockDim.x) mn = fminf(mn, corr[t]);
+    for (int o = 16; o; o >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mn;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float m2 = red[0];
+      for (int w = 1; w < int(blockDim.x >> 5); ++w) m2 = fminf(m2, red[w]);
+      red[0] = m2;
+    }
+    __syncthreads();
+    mn = red[0];
+    const float lden0 = g_log10[N - ex];
+    const float lden = lden0 > 1e-6f ? lden0 : 1e-6f;
+    for (int t = ex + threadIdx.x; t < sraw; t += blockDim.x) {
+      const float w = __fdiv_rn(g_log10[N - t], lden);
+      corr[t] = __fmul_rn(__fsub_rn(corr[t], mn), w);
+    }
+    __syncthreads();
+  }
+  if (corr_out)
+    for (int t = threadIdx.x; t < N; t += blockDim.x) corr_out[int64_t(bh) * N + t] = corr[t];
+
+  // lag selection over the remote range [rs, N)
+  const int rs = p.remote_start, nr = N - rs;
+  float thr = 0.0f;
+  bool by_ratio = false;
+  float mx = 0.0f;
+  if (nr > 0) {
+    if (p.corr_mode == FFTS_SEL_TOPK) {
+      for (int t = threadIdx.x; t < nr; t += blockDim.x) keys[t] = f32_key(corr[rs + t]);
+      __syncthreads();
+      const float ranks = __fmul_rn(p.corr_quantile, (float)(nr - 1));
+      const int lo = (int)ranks;
+      const int hi = (int)ceilf(ranks);
+      const float w = __fsub_rn(ranks, (float)lo);
+      const float a = key_f32(block_select_rank(keys, nr, lo, hist, bc));
+      const float bb = hi == lo ? a : key_f32(block_select_rank(keys, nr, hi, hist, bc));
+      const float diff = __fsub_rn(bb, a);
+      thr = fabsf(w) < 0.5f ? __fmaf_rn(w, diff, a) : __fmaf_rn(-diff, __fsub_rn(1.0f, w), bb);
+    } else {
+      float m = -INFINITY;
+      for (int t = rs + threadIdx.x; t < N; t += blockDim.x) m = fmaxf(m, corr[t]);
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      __syncthreads();
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float m2 = red[0];
+        for (int w = 1; w < int(blockDim.x >> 5); ++w) m2 = fmaxf(m2, red[w]);
+        red[0] = m2;
+      }
+      __syncthreads();
+      mx = red[0] < 1e-6f ? 1e-6f : red[0];
+      by_ratio = true;
+      thr = p.corr_threshold;
+    }
+  }
+  __syncthreads();
+  uint32_t *out = tausel + int64_t(bh) * W;
+  for (int w = threadIdx.x; w < W; w += blockDim.x) {
+    uint32_t word = 0;
+    for (int b = 0; b < 32; ++b) {
+      const int t = w * 32 + b;
+      if (t >= rs && t < N) {
+        const float c = corr[t];
+        const bool on = by_ratio ? (__fdiv_rn(c, mx) >= thr) : (c >= thr);
+        word |= uint32_t(on) << b;
+      }
+    }
+    out[w] = word;
+  }
+}
+
+// --------------------------------------------------------- dot products
+template <typename T>
+__device__ __forceinline__ double dot64_rows(const T *a, const T *b, int D) {
+  constexpr int VEC = Elem<T>::kVec;
+  double acc = 0.0;
+  for (int d = 0; d < D; d += VEC) {
+    float av[VEC], bv[VEC];
+    load_vec_f32<T>(a + d, av);
+    load_vec_f32<T>(b + d, bv);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc = __fma_rn((double)av[e], (double)bv[e], acc);
+  }
+  return acc;
+}
+
+// 256-lane canonical reduction of per-thread partials (blockDim.x == 256).
+__device__ double lane_tree(double v, double *part) {
+  part[threadIdx.x] = v;
+  __syncthreads();
+  for (int s = kLanes / 2; s >= 1; s >>= 1) {
+    if (threadIdx.x < s) part[threadIdx.x] = __dadd_rn(part[threadIdx.x], part[threadIdx.x + s]);
+    __syncthreads();
+  }
+  const double r = part[0];
+  __syncthreads();
+  return r;
+}
+
+// ------------------------------------------------------------ head stats
+template <typename T>
+__global__ void __launch_bounds__(256) head_stats_kernel(const T *__restrict__ qb,
+                                                         const T *__restrict__ kb, int H, int Hkv,
+                                                         int D, ffts_mask_params p,
+                                                         int32_t *__restrict__ stripe_ws,
+                                                         uint8_t *__restrict__ is_stripe_out,
+                                                         float *__restrict__ stripe_var_out,
+                                                         uint32_t *__restrict__ colsel,
+                                                         uint32_t *__restrict__ lastsel) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int N = p.n_blocks;
+  const int W = (N + 31) / 32;
+  double *part = reinterpret_cast<double *>(smem_raw);      // [256]
+  double *pch = part + kLanes;                              // [32][D]
+  float *vals = reinterpret_cast<float *>(pch + 32 * D);    // [N]
+  uint32_t *keys = reinterpret_cast<uint32_t *>(vals + N);  // [N]
+  uint32_t *words = keys + N;                               // [W]
+  __shared__ int hist[256];
+  __shared__ int bc[4];
+  __shared__ int stripe_sh;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const T *q = qb + int64_t(bh) * N * D;
+  const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
+  const double sqrtD = sqrt((double)D);
+
+  // ---- stripe statistic
+  double total = 0.0;
+  float svar = INFINITY;
+  int stripe = 0;
+  if (p.corr_on && !p.stripe_all_diffuse) {
+    for (int s = 0; s < p.n_diag_samples; ++s) {
+      const int tau = p.diag_taus[s];
+      const int m = N - tau - 1, n = m - 1;
+      for (int t = threadIdx.x; t < m; t += blockDim.x)
+        vals[t] = __double2float_rn(__ddiv_rn(dot64_rows(q + int64_t(t + tau) * D, k + int64_t(t) * D, D), sqrtD));
+      __syncthreads();
+      double var;
+      if (n >= 2) {
+        double a = 0.0;
+        for (int e = threadIdx.x; e < n; e += blockDim.x)
+          a = __dadd_rn(a, (double)__fsub_rn(vals[e + 1], vals[e]));
+        const double mean = __ddiv_rn(lane_tree(a, part), (double)n);
+        a = 0.0;
+        for (int e = threadIdx.x; e < n; e += blockDim.x) {
+          const double dv = __dsub_rn((double)__fsub_rn(vals[e + 1], vals[e]), mean);
+          a = __dadd_rn(a, __dmul_rn(dv, dv));
+        }
+        var = __ddiv_rn(lane_tree(a, part), (double)(n - 1));
+      } else {
+        var = __longlong_as_double(0x7ff8000000000000ll);
+      }
+      double a = 0.0;
+      for (int e = threadIdx.x; e < m; e += blockDim.x) a = __dadd_rn(a, fabs((double)vals[e]));
+      const double sabs = lane_tree(a, part);
+      double mabs = m > 0 ? __ddiv_rn(sabs, (double)m) : __longlong_as_double(0x7ff8000000000000ll);
+      const double floor6 = (double)1e-6f;
+      if (mabs < floor6) mabs = floor6;
+      total = __dadd_rn(total, __ddiv_rn(var, mabs));
+    }
+    svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
+    stripe = svar <= p.stripe_threshold;
+  }
+  if (threadIdx.x == 0) {
+    stripe_ws[bh] = stripe;
+    if (is_stripe_out) is_stripe_out[bh] = (uint8_t)stripe;
+    if (stripe_var_out) stripe_var_out[bh] = svar;
+  }
+
+  // ---- hot key columns
+  const int col_apply = p.col_on && (!p.corr_on || stripe);
+  for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
+  __syncthreads();
+  if (col_apply && p.col_end > p.col_start) {
+    double P = 0.0;
+    for (int jhi = N - 1; jhi >= 0; jhi -= 32) {
+      const int jlo = max(0, jhi - 31);
+      if (threadIdx.x < D) {
+        for (int j = jhi; j >= jlo; --j) {
+          if (j <= N - 2) P = __dadd_rn(P, (double)Elem<T>::to_f32(q[int64_t(j) * D + threadIdx.x]));
+          pch[(jhi - j) * D + threadIdx.x] = P;
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x <= jhi - jlo) {
+        const int j = jhi - threadIdx.x;
+        double acc = 0.0;
+        for (int d = 0; d < D; ++d)
+          acc = __fma_rn(pch[threadIdx.x * D + d], (double)Elem<T>::to_f32(k[int64_t(j) * D + d]), acc);
+        const int cnt = max(1, N - j - 1);
+        vals[j] = __double2float_rn(__ddiv_rn(__ddiv_rn(acc, sqrtD), (double)cnt));
+      }
+      __syncthreads();
+    }
+    for (int j = threadIdx.x; j < N; j += blockDim.x) keys[j] = f32_key(vals[j]);
+    __syncthreads();
+    block_topk_bits(keys, p.col_start, p.col_end, p.col_topk, words, hist, bc);
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < W; w += blockDim.x) colsel[int64_t(bh) * W + w] = words[w];
+  __syncthreads();
+
+  // ---- last query row
+  for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
+  __syncthreads();
+  if (p.last_on) {
+    for (int j = threadIdx.x; j < N; j += blockDim.x) {
+      const double s = dot64_rows(q + int64_t(N - 1) * D, k + int64_t(j) * D, D);
+      keys[j] = f32_key(Elem<T>::round_f32(__double2float_rn(s)));
+    }
+    __syncthreads();
+    block_topk_bits(keys, 0, N, p.last_topk, words, hist, bc);
+  }
+  __syncthreads();
+  for (int w = threadIdx.x; w < W; w += blockDim.x) lastsel[int64_t(bh) * W + w] = words[w];
+  (void)stripe_sh;
+}
+
+// ------------------------------------------------------- warp selection
+__device__ uint32_t warp_select_rank(const uint32_t *keys, int n, int rank, int *hist) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = lane; i < 256; i += 32) hist[i] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint32_t kk = keys[i];
+      if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255], 1);
+    }
+    __syncwarp();
+    int c[8], s = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      c[e] = hist[lane * 8 + e];
+      s += c[e];
+    }
+    int incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const int excl = incl - s;
+    const unsigned ball = __ballot_sync(0xffffffffu, rank >= excl && rank < incl);
+    const int src = ball ? __ffs(ball) - 1 : 31;
+    int dsel = 255, below = excl;
+    if (lane == src) {
+      int cc = excl;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (cc + c[e] > rank) { dsel = lane * 8 + e; below = cc; break; }
+        cc += c[e];
+      }
+    }
+    dsel = __shfl_sync(0xffffffffu, dsel, src);
+    below = __shfl_sync(0xffffffffu, below, src);
+    rank -= below;
+    prefix |= uint32_t(dsel) << shift;
+    mask |= 0xffu << shift;
+    __syncwarp();
+  }
+  return prefix;
+}
+
+// k largest of keys[0..n) (ties: lowest index) OR-ed into words[] (warp-local).
+__device__ void warp_topk_bits(const uint32_t *keys, int n, int k, uint32_t *words, int *hist) {
+  const int lane = threadIdx.x & 31;
+  if (k >= n) {
+    for (int j = lane; j < n; j += 32) atomicOr(&words[j >> 5], 1u << (j & 31));
+    __syncwarp();
+    return;
+  }
+  const uint32_t T = warp_select_rank(keys, n, n - k, hist);
+  int gt = 0;
+  for (int j = lane; j < n; j += 32) gt += keys[j] > T;
+  for (int o = 16; o; o >>= 1) gt += __shfl_xor_sync(0xffffffffu, gt, o);
+  const int need = k - gt;
+  int base = 0;
+  for (int c = 0; c < n; c += 32) {
+    const int j = c + lane;
+    const bool in = j < n;
+    const uint32_t kk = in ? keys[j] : 0u;
+    const bool eq = in && kk == T;
+    const unsigned bal = __ballot_sync(0xffffffffu, eq);
+    const int before = base + __popc(bal & ((1u << lane) - 1));
+    if (in && (kk > T || (eq && before < need))) atomicOr(&words[j >> 5], 1u << (j & 31));
+    base += __popc(bal);
+  }
+  __syncwarp();
+}
+
+// ------------------------------------------------------------ mask build
+template <typename T>
+__global__ void __launch_bounds__(256) mask_build_kernel(const T *__restrict__ qb,
+                                                         const T *__restrict__ kb, int H, int Hkv,
+                                                         int D, ffts_mask_params p, int R,
+                                                         const int32_t *__restrict__ stripe_ws,
+                                                         const uint32_t *__restrict__ tausel,
+                                                         const uint32_t *__restrict__ colsel,
+                                                         const uint32_t *__restrict__ lastsel,
+                                                         uint32_t *__restrict__ bits,
+                                                         int32_t *__restrict__ row_count) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int VEC = Elem<T>::kVec;
+  constexpr int RMAX = 16;
+  const int N = p.n_blocks;
+  const int W = (N + 31) / 32;
+  double *qrow = reinterpret_cast<double *>(smem_raw);        // [R][D]
+  uint32_t *keys = reinterpret_cast<uint32_t *>(qrow + R * D);  // [R][N]
+  uint32_t *rowbits = keys + R * N;                           // [R][W]
+  int *hist = reinterpret_cast<int *>(rowbits + R * W);       // [8][256]
+  int *cnt = hist + 8 * 256;                                  // [R]
+  const int bh = blockIdx.y;
+  const int i0 = blockIdx.x * R;
+  const int rows = min(R, N - i0);
+  const int b = bh / H, h = bh % H;
+  const int stripe = stripe_ws[bh];
+  const bool diffuse = p.corr_on && !stripe;
+  const int col_apply = p.col_on && (!p.corr_on || stripe);
+  for (int e = threadIdx.x; e < R * W; e += blockDim.x) rowbits[e] = 0;
+  for (int e = threadIdx.x; e < R; e += blockDim.x) cnt[e] = 0;
+
+  if (diffuse) {
+    const T *q = qb + int64_t(bh) * N * D;
+    const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
+    for (int e = threadIdx.x; e < rows * D; e += blockDim.x)
+      qrow[e] = (double)Elem<T>::to_f32(q[int64_t(i0) * D + e]);
+    __syncthreads();
+    const double sqrtD = sqrt((double)D);
+    const int jmax = i0 + rows;  // columns 0 .. i0+rows-1
+    for (int j = threadIdx.x; j < jmax; j += blockDim.x) {
+      double acc[RMAX];
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) acc[r] = 0.0;
+      const T *kr = k + int64_t(j) * D;
+      for (int d = 0; d < D; d += VEC) {
+        float kv[VEC];
+        load_vec_f32<T>(kr + d, kv);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const double kd = (double)kv[e];
+#pragma unroll
+          for (int r = 0; r < RMAX; ++r)
+            if (r < rows) acc[r] = __fma_rn(qrow[r * D + d + e], kd, acc[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r)
+        if (r < rows) keys[r * N + j] = f32_key(__double2float_rn(__ddiv_rn(acc[r], sqrtD)));
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5;
+    for (int r = warp; r < rows; r += blockDim.x >> 5) {
+      const int i = i0 + r;
+      const float kf = __fmul_rn((float)(i + 1), p.qk_topk_ratio);
+      int ki = (int)kf;
+      if (ki < 1) ki = 1;
+      warp_topk_bits(keys + r * N, i + 1, ki, rowbits + r * W, hist + warp * 256);
+    }
+  }
+  __syncthreads();
+
+  const uint32_t *ts = tausel + int64_t(bh) * W;
+  const uint32_t *cs = colsel + int64_t(bh) * W;
+  const uint32_t *ls = lastsel + int64_t(bh) * W;
+  for (int e = threadIdx.x; e < rows * W; e += blockDim.x) {
+    const int r = e / W, w = e - r * W;
+    const int i = i0 + r;
+    uint32_t word = 0;
+    const uint32_t cw = col_apply ? cs[w] : 0u;
+    const uint32_t lw = (p.last_on && i == N - 1) ? ls[w] : 0u;
+    const uint32_t dw = diffuse ? rowbits[r * W + w] : 0u;
+    for (int t = 0; t < 32; ++t) {
+      const int j = w * 32 + t;
+      if (j > i) break;
+      const int tau = i - j;
+      bool on = j < p.keep_sink || j >= N - p.keep_recent || tau <= p.local_window;
+      if (p.corr_on && stripe)
+        on |= tau >= p.remote_start && ((ts[tau >> 5] >> (tau & 31)) & 1u) && j >= p.keep_sink;
+      on |= (dw >> t) & 1u;
+      on |= (cw >> t) & 1u;
+      on |= (lw >> t) & 1u;
+      word |= uint32_t(on) << t;
+    }
+    bits[(int64_t(bh) * N + i) * W + w] = word;
+    atomicAdd(&cnt[r], __popc(word));
+  }
+  __syncthreads();
+  if (row_count)
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) row_count[int64_t(bh) * N + i0 + r] = cnt[r];
+}
+
+__global__ void unpack_kernel(const uint32_t *__restrict__ bits, int64_t rows, int64_t N,
+                              uint8_t *__restrict__ out) {
+  const int64_t W = (N + 31) / 32;
+  const int64_t total = rows * N;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / N, j = e - r * N;
+    out[e] = (bits[r * W + (j >> 5)] >> (j & 31)) & 1u;
+  }
+}
+
+// ------------------------------------------------------------- host side
+struct MaskWorkspace {
+  float2 *partial;
+  uint32_t *tausel, *colsel, *lastsel;
+  int32_t *stripe;
+  int64_t bytes;
+};
+
+static inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+
+static MaskWorkspace carve(void *ws, int64_t B, int64_t H, int64_t N, int64_t D) {
+  MaskWorkspace m{};
+  const int M = 1 << ilog2_ceil(2 * N);
+  const int64_t F = M / 2 + 1;
+  const int64_t nchunk = ceil_div(D, kDChunk);
+  const int64_t W = ceil_div(N, 32);
+  char *p = static_cast<char *>(ws);
+  int64_t off = 0;
+  m.partial = reinterpret_cast<float2 *>(p + off);
+  off += align256(B * H * nchunk * F * int64_t(sizeof(float2)));
+  m.tausel = reinterpret_cast<uint32_t *>(p + off);
+  off += align256(B * H * W * 4);
+  m.colsel = reinterpret_cast<uint32_t *>(p + off);
+  off += align256(B * H * W * 4);
+  m.lastsel = reinterpret_cast<uint32_t *>(p + off);
+  off += align256(B * H * W * 4);
+  m.stripe = reinterpret_cast<int32_t *>(p + off);
+  off += align256(B * H * 4);
+  m.bytes = off;
+  return m;
+}
+
+int64_t mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D) {
+  return carve(nullptr, B, H, N, D).bytes;
+}
+
+template <typename T>
+static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+                          const ffts_mask_params &p, uint32_t *bits, int32_t *row_count, float *corr,
+                          float *csum, uint8_t *is_stripe, float *svar, const MaskWorkspace &ws,
+                          cudaStream_t stream) {
+  const int N = p.n_blocks;
+  const int M = 1 << ilog2_ceil(2 * int64_t(N));
+  const int F = M / 2 + 1;
+  const int nchunk = int(ceil_div(D, kDChunk));
+  const int W = int(ceil_div(N, 32));
+  const unsigned BH = unsigned(B * H);
+  if (p.corr_on) {
+    // FFT partial spectra
+    const size_t fixed = size_t(M / 2 + F + 1) * sizeof(float2);
+    int nf = kDChunk;
+    while (nf > 1 && fixed + size_t(nf) * M * sizeof(float2) > 200 * 1024) nf >>= 1;
+    const size_t smem1 = fixed + size_t(nf) * M * sizeof(float2);
+    FFTS_CUDA(cudaFuncSetAttribute(fft_partial_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
+    fft_partial_kernel<T><<<dim3(nchunk, BH), 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), N, int(D), M, nf, ws.partial);
+    FFTS_CUDA(cudaGetLastError());
+    const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
+    FFTS_CUDA(cudaFuncSetAttribute(corr_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2)));
+    corr_select_kernel<<<BH, 512, smem2, stream>>>(ws.partial, nchunk, N, M, p, corr, csum, ws.tausel);
+    FFTS_CUDA(cudaGetLastError());
+  } else {
+    FFTS_CUDA(cudaMemsetAsync(ws.tausel, 0, size_t(BH) * W * 4, stream));
+    if (corr) FFTS_CUDA(cudaMemsetAsync(corr, 0, size_t(BH) * N * 4, stream));
+    if (csum) FFTS_CUDA(cudaMemsetAsync(csum, 0, size_t(BH) * N * 4, stream));
+  }
+  const size_t smem3 = size_t(kLanes) * 8 + size_t(32) * D * 8 + size_t(N) * 8 + size_t(W) * 4;
+  FFTS_CUDA(cudaFuncSetAttribute(head_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3)));
+  head_stats_kernel<T><<<BH, 256, smem3, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, ws.stripe, is_stripe, svar,
+                                                   ws.colsel, ws.lastsel);
+  FFTS_CUDA(cudaGetLastError());
+  const int R = N <= 1024 ? 16 : max(1, 16384 / N);
+  const size_t smem4 = size_t(R) * D * 8 + size_t(R) * N * 4 + size_t(R) * W * 4 + 8 * 256 * 4 + size_t(R) * 4;
+  FFTS_CUDA(cudaFuncSetAttribute(mask_build_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem4)));
+  mask_build_kernel<T><<<dim3(unsigned(ceil_div(N, R)), BH), 256, smem4, stream>>>(
+      qb, kb, int(H), int(Hkv), int(D), p, R, ws.stripe, ws.tausel, ws.colsel, ws.lastsel, bits, row_count);
+  FFTS_CUDA(cudaGetLastError());
+  return FFTS_OK;
+}
+
+int validate_params(const ffts_mask_params &p, int64_t D) {
+  const int N = p.n_blocks;
+  FFTS_REQUIRE(N >= 1 && N <= kMaxBlocks, "n_blocks %d outside [1, %d]", N, kMaxBlocks);
+  FFTS_REQUIRE(!p.corr_on || N >= 10, "the correlation mask needs at least 10 blocks (got %d)", N);
+  FFTS_REQUIRE(p.n_diag_samples >= 0 && p.n_diag_samples <= FFTS_MAX_DIAG_SAMPLES, "bad n_diag_samples");
+  for (int s = 0; s < p.n_diag_samples; ++s)
+    FFTS_REQUIRE(p.diag_taus[s] >= 0 && p.diag_taus[s] < N, "sampled lag %d outside [0, N)", p.diag_taus[s]);
+  FFTS_REQUIRE(!p.corr_on || p.stripe_all_diffuse || p.n_diag_samples >= 1, "no sampled diagonals");
+  FFTS_REQUIRE(!p.corr_on || (p.remote_start >= 1 && p.remote_start < N), "remote_start outside [1, N)");
+  FFTS_REQUIRE(p.exclude_tau >= 0, "exclude_tau < 0");
+  FFTS_REQUIRE(p.corr_mode == FFTS_SEL_TOPK || p.corr_mode == FFTS_SEL_THRESHOLD, "bad corr_mode");
+  FFTS_REQUIRE(!p.col_on || p.col_end <= p.col_start || (p.col_start >= 0 && p.col_end <= N && p.col_topk >= 1),
+               "bad column range");
+  FFTS_REQUIRE(!p.last_on || (p.last_topk >= 1 && p.last_topk <= N), "bad last_topk");
+  FFTS_REQUIRE(D >= 8 && D <= 256 && D % 8 == 0, "head_dim %lld unsupported for selection", (long long)D);
+  return FFTS_OK;
+}
+
+int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
+               const ffts_mask_params *params, uint32_t *bits, int32_t *row_count, float *corr,
+               float *csum, uint8_t *is_stripe, float *svar, void *workspace, int64_t ws_bytes,
+               cudaStream_t stream) {
+  FFTS_REQUIRE(params != nullptr, "params is NULL");
+  const ffts_mask_params &p = *params;
+  int rc = validate_params(p, D);
+  if (rc) return rc;
+  FFTS_REQUIRE(dtype == FFTS_DTYPE_F32 || dtype == FFTS_DTYPE_BF16, "unsupported dtype %d", dtype);
+  FFTS_REQUIRE(B >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0, "bad head counts H=%lld Hkv=%lld",
+               (long long)H, (long long)Hkv);
+  FFTS_REQUIRE(B * H <= 65535, "B*H too large");
+  FFTS_REQUIRE(qb && kb && bits, "NULL tensor pointer");
+  FFTS_REQUIRE((reinterpret_cast<uintptr_t>(qb) & 15) == 0 && (reinterpret_cast<uintptr_t>(kb) & 15) == 0,
+               "pooled inputs must be 16-byte aligned");
+  const int64_t need = mask_workspace_bytes(B, H, p.n_blocks, D);
+  if (workspace == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
+    set_error(FFTS_E_WORKSPACE, "workspace needs %lld bytes, 256-byte aligned (got %lld)", (long long)need,
+              (long long)ws_bytes);
+    return FFTS_E_WORKSPACE;
+  }
+  rc = ensure_tables();
+  if (rc) return rc;
+  const MaskWorkspace ws = carve(workspace, B, H, p.n_blocks, D);
+  if (dtype == FFTS_DTYPE_BF16)
+    return run_block_mask(static_cast<const __nv_bfloat16 *>(qb), static_cast<const __nv_bfloat16 *>(kb), B, H,
+                          Hkv, D, p, bits, row_count, corr, csum, is_stripe, svar, ws, stream);
+  return run_block_mask(static_cast<const float *>(qb), static_cast<const float *>(kb), B, H, Hkv, D, p, bits,
+                        row_count, corr, csum, is_stripe, svar, ws, stream);
+}
+
+int unpack_mask(const uint32_t *bits, int64_t B, int64_t H, int64_t N, uint8_t *out, cudaStream_t stream) {
+  FFTS_REQUIRE(bits && out && B > 0 && H > 0 && N > 0, "bad unpack arguments");
+  const int64_t total = B * H * N * N;
+  const int blocks = int(std::min<int64_t>(ceil_div(total, 256), 148 * 16));
+  unpack_kernel<<<blocks, 256, 0, stream>>>(bits, B * H * N, N, out);
+  FFTS_CUDA(cudaGetLastError());
+  return FFTS_OK;
+}
+
+}  // namespace ffts

@@ -1,0 +1,280 @@
+"""The FFTSparse prefill operator on B200.
+
+``myattn_prefill`` keeps the signature, argument meaning, return layout and
+error behaviour of the reference's ``myattn_prefill``
+(attn_src/fft_attn/my_attn_v7.py:454-792) so that it drops into the model
+patching code that calls it (eval/LongBench/pred.py:216,
+eval/RULER/pred.py:89, eval/LVEval/pred.py:277,
+eval/InfiniteBench/src/pred_infinitebench.py:336,
+eval/efficiency/benchmark_attention_multilayer.py:308).
+
+Every step runs in libfftsparse_b200.so on the current CUDA stream with no
+host synchronisation:
+
+  ffts_pool            block mean pooling of q and k          (ref :552-555)
+  ffts_block_mask      the union of all block masks           (ref :532-641)
+  ffts_sparse_attn_fwd block-sparse causal attention          (ref :763-786)
+
+``fft_block_mask`` additionally exposes the selected block mask (the
+reference's ``base_blockmask``) and the intermediate statistics.
+"""
+from __future__ import annotations
+
+import sys
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .params import derive_mask_params, MaskParams
+
+__all__ = ["myattn_prefill", "fft_block_mask", "sparse_attention", "pool_blocks", "BlockMask",
+           "AttentionCache", "_attention_cache"]
+
+
+class AttentionCache:
+    """Kept for interface parity with my_attn_v7.py:23-47 (cu_seqlens and
+    head_mask_type caches).  The B200 kernels need neither, so the cache is
+    never consulted on the hot path."""
+
+    def __init__(self):
+        self._cu_seqlens = {}
+        self._head_mask_type = {}
+
+    def get_cu_seqlens(self, seq_len, device):
+        key = (seq_len, str(device))
+        if key not in self._cu_seqlens:
+            self._cu_seqlens[key] = torch.tensor([0, seq_len], dtype=torch.int32, device=device)
+        return self._cu_seqlens[key]
+
+    def get_head_mask_type(self, num_heads, device):
+        key = (num_heads, str(device))
+        if key not in self._head_mask_type:
+            self._head_mask_type[key] = torch.tensor([1] * num_heads, dtype=torch.int32, device=device)
+        return self._head_mask_type[key]
+
+
+_attention_cache = AttentionCache()
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_4d(name: str, t: torch.Tensor):
+    if t.dim() != 4:
+        raise ValueError(f"{name} must be [B, H, L, D], got shape {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must be contiguous in the head dimension")
+
+
+def pool_blocks(x: torch.Tensor, block_size: int) -> torch.Tensor:
+    """Block mean of x [B, H, L, D] (ffts_pool) -> contiguous [B, H, N, D] in x.dtype."""
+    _check_4d("x", x)
+    if x.dtype not in _DTYPES:
+        raise TypeError(f"pooling supports float32 and bfloat16, got {x.dtype}")
+    lib = _lib.load()
+    B, H, L, D = x.shape
+    N = (L + block_size - 1) // block_size
+    out = torch.empty(B, H, N, D, dtype=x.dtype, device=x.device)
+    _lib.check(lib.ffts_pool(x.data_ptr(), _DTYPES[x.dtype], B, H, L, D, x.stride(0), x.stride(1),
+                             x.stride(2), block_size, out.data_ptr(), _stream_ptr(x.device)))
+    return out
+
+
+@dataclass
+class BlockMask:
+    """Result of the block-mask selection for a [B, H, L, D] prefill."""
+
+    bits: torch.Tensor          # int32 [B, H, N, W] packed (bit j of row i = key block j kept)
+    row_count: torch.Tensor     # int32 [B, H, N]
+    corr: torch.Tensor          # fp32 [B, H, N] lag scores (corr_causal)
+    corr_sum: torch.Tensor      # fp32 [B, H, N] raw lag sums (corr_causal_sum)
+    is_stripe: torch.Tensor     # uint8 [B, H]
+    stripe_var: torch.Tensor    # fp32 [B, H]
+    params: MaskParams
+    q_pooled: torch.Tensor
+    k_pooled: torch.Tensor
+
+    @property
+    def n_blocks(self) -> int:
+        return self.params.n_blocks
+
+    def dense(self) -> torch.Tensor:
+        """bool [B, H, N, N], the reference's ``base_blockmask`` layout."""
+        lib = _lib.load()
+        B, H, N, _ = self.bits.shape
+        out = torch.empty(B, H, N, N, dtype=torch.uint8, device=self.bits.device)
+        _lib.check(lib.ffts_unpack_mask(self.bits.data_ptr(), B, H, N, out.data_ptr(),
+                                        _stream_ptr(self.bits.device)))
+        return out.view(torch.bool)
+
+    def csr(self):
+        """(row_ptr int64 [B*H*N+1], col_idx int32 [nnz]) with ascending columns per row."""
+        dense = self.dense().reshape(-1, self.n_blocks)
+        row_ptr = torch.zeros(dense.shape[0] + 1, dtype=torch.int64, device=dense.device)
+        row_ptr[1:] = torch.cumsum(self.row_count.reshape(-1).to(torch.int64), 0)
+        col_idx = dense.nonzero()[:, 1].to(torch.int32)
+        return row_ptr, col_idx
+
+    def density(self) -> float:
+        """Kept fraction of the causal block pairs."""
+        N = self.n_blocks
+        causal = N * (N + 1) // 2
+        return float(self.row_count.sum()) / (causal * self.row_count.shape[0] * self.row_count.shape[1])
+
+
+def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, block_size: int = 128,
+                   params: Optional[MaskParams] = None, **kwargs) -> BlockMask:
+    """Select the FFTSparse block mask for q [B, H, L, D] and k [B, Hkv, L, D].
+
+    ``kwargs`` are the mask arguments of myattn_prefill (sink_ratio,
+    recent_ratio, local_span_ratio, enable_correlation_mask,
+    correlation_selection_mode, ...).
+    """
+    q, k = query_states, key_states
+    _check_4d("query_states", q)
+    _check_4d("key_states", k)
+    if q.dtype != k.dtype:
+        raise TypeError("query and key dtypes differ")
+    if q.dtype not in _DTYPES:
+        raise TypeError(f"mask selection supports float32 and bfloat16, got {q.dtype}")
+    B, H, L, D = q.shape
+    Hkv = k.shape[1]
+    if k.shape[0] != B or k.shape[2] != L or k.shape[3] != D or H % Hkv:
+        raise ValueError(f"key_states {tuple(k.shape)} incompatible with query_states {tuple(q.shape)}")
+    if params is None:
+        params = derive_mask_params(L, block_size=block_size, **kwargs)
+    lib = _lib.load()
+    qb = pool_blocks(q, params.block_size)
+    kb = pool_blocks(k, params.block_size)
+    N = params.n_blocks
+    W = (N + 31) // 32
+    dev = q.device
+    bits = torch.empty(B, H, N, W, dtype=torch.int32, device=dev)
+    row_count = torch.empty(B, H, N, dtype=torch.int32, device=dev)
+    corr = torch.empty(B, H, N, dtype=torch.float32, device=dev)
+    corr_sum = torch.empty(B, H, N, dtype=torch.float32, device=dev)
+    is_stripe = torch.empty(B, H, dtype=torch.uint8, device=dev)
+    stripe_var = torch.empty(B, H, dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.ffts_mask_workspace_bytes(B, H, N, D))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    cp = params.to_c()
+    _lib.check(lib.ffts_block_mask(qb.data_ptr(), kb.data_ptr(), _DTYPES[q.dtype], B, H, Hkv, D,
+                                   _lib.ctypes.addressof(cp), bits.data_ptr(), row_count.data_ptr(),
+                                   corr.data_ptr(), corr_sum.data_ptr(), is_stripe.data_ptr(),
+                                   stripe_var.data_ptr(), ws.data_ptr(), ws_bytes, _stream_ptr(dev)))
+    return BlockMask(bits, row_count, corr, corr_sum, is_stripe, stripe_var, params, qb, kb)
+
+
+def _dense_causal_bits(B: int, H: int, N: int, device) -> torch.Tensor:
+    W = (N + 31) // 32
+    return torch.full((B, H, N, W), -1, dtype=torch.int32, device=device)
+
+
+def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: torch.Tensor,
+                     block_size: int, causal: bool = True, out: Optional[torch.Tensor] = None,
+                     status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Block-sparse attention (ffts_sparse_attn_fwd).
+
+    q [B, H, L, D], k/v [B, Hkv, L, D] bf16; bits [B, H, N, W] packed mask.
+    Returns (or fills) ``out`` of shape [B, L, H, D] bf16.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_4d(name, t)
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"block-sparse attention supports bfloat16 inputs only (got {name} {t.dtype})")
+    B, H, L, D = q.shape
+    Hkv = k.shape[1]
+    if out is None:
+        out = torch.empty(B, L, H, D, dtype=torch.bfloat16, device=q.device)
+    lib = _lib.load()
+    qs = _lib.i64_array([q.stride(0), q.stride(1), q.stride(2)])
+    ks = _lib.i64_array([k.stride(0), k.stride(1), k.stride(2)])
+    vs = _lib.i64_array([v.stride(0), v.stride(1), v.stride(2)])
+    os_ = _lib.i64_array([out.stride(0), out.stride(2), out.stride(1)])
+    _lib.check(lib.ffts_sparse_attn_fwd(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
+        block_size, int(bool(causal)), out.data_ptr(), os_,
+        status.data_ptr() if status is not None else None, _stream_ptr(q.device)))
+    return out
+
+
+def myattn_prefill(
+        query_states,
+        key_states,
+        value_states,
+        layer_idx,
+        block_size=128,
+        is_causal=True,
+        is_visual=False,
+        sink_ratio=0.1,
+        recent_ratio=0.1,
+        local_span_ratio=0.1,
+        enable_correlation_mask=True,
+        correlation_selection_mode: str = "threshold",
+        correlation_topk_ratio: float = 0.2,
+        corr_threshold: float = 0.1,
+        collect_corr_stats: bool = False,
+        enable_column_mask: bool = True,
+        column_topk_ratio: float = 0.1,
+        column_start_exclude_ratio: float = 0.1,
+        column_end_exclude_ratio: float = 0.2,
+        enable_last_block_mask=True,
+        last_block_threshold=0.01,
+        diag_sample_ratio: float = 0.15,
+        min_diag_samples: int = 5,
+        max_diag_samples: int = 64,
+        stripe_threshold: float = 0.3,
+        qk_topk_ratio: float = 0.2,
+        attention_vis_heads=(0,),
+        attention_vis_dir=None,
+):
+    """Block-sparse prefill attention with FFT-correlation block selection.
+
+    query_states [B, H, L, D]; key_states / value_states [B, H, L, D]
+    (repeat_kv-expanded, as the reference's callers pass them) or
+    [B, Hkv, L, D] with H % Hkv == 0.  Returns [B, L, H*D] in bf16.
+
+    As in the reference, sequences shorter than 10 blocks use dense causal
+    attention (my_attn_v7.py:506-519), ``last_block_threshold``, ``is_visual``,
+    ``collect_corr_stats`` and the visualisation arguments are accepted and
+    ignored, a non-CUDA input raises AssertionError (:502) and an unknown
+    selection mode raises ValueError (:210).
+    """
+    assert query_states.is_cuda, "input tensors must be on CUDA"
+    q, k, v = query_states, key_states, value_states
+    L_q = q.shape[2]
+    L_k = k.shape[2]
+    if L_q != L_k:
+        raise ValueError("prefill expects equal query and key lengths")
+    B, H, L, D = q.shape
+    min_blocks_needed = 10
+    if L_k < block_size * min_blocks_needed:
+        N = (L + block_size - 1) // block_size
+        bits = _dense_causal_bits(B, H, N, q.device)
+        out = sparse_attention(q, k, v, bits, block_size, causal=True)
+        return out.view(B, L, H * D)
+
+    mask = fft_block_mask(
+        q, k, block_size=block_size, sink_ratio=sink_ratio, recent_ratio=recent_ratio,
+        local_span_ratio=local_span_ratio, enable_correlation_mask=enable_correlation_mask,
+        correlation_selection_mode=correlation_selection_mode,
+        correlation_topk_ratio=correlation_topk_ratio, corr_threshold=corr_threshold,
+        enable_column_mask=enable_column_mask, column_topk_ratio=column_topk_ratio,
+        column_start_exclude_ratio=column_start_exclude_ratio,
+        column_end_exclude_ratio=column_end_exclude_ratio,
+        enable_last_block_mask=enable_last_block_mask, diag_sample_ratio=diag_sample_ratio,
+        min_diag_samples=min_diag_samples, max_diag_samples=max_diag_samples,
+        stripe_threshold=stripe_threshold, qk_topk_ratio=qk_topk_ratio)
+
+    collector = getattr(sys.modules[__name__], "_sparsity_collector", None)
+    if collector is not None:
+        N = mask.n_blocks
+        collector.setdefault("final", []).append(float(mask.row_count.sum()) / (B * H * N * N))
+
+    out = sparse_attention(q, k, v, mask.bits, block_size, causal=is_causal)
+    return out.view(B, L, H * D)

@@ -5,8 +5,8 @@
  * (lines 454-792): block mean pooling, FFT lag correlation, stripe/diffuse head
  * classification, four auxiliary block masks, and a call into the third-party
  * `block_sparse_attn_func` CUDA kernel (my_attn_v7.py:775-786).  Every entry
- * point below replaces one step of that function; `ffts_prefill` replaces the
- * whole of it.
+ * point below replaces one step of that function; ffts_pool + ffts_block_mask
+ * + ffts_sparse_attn_fwd, in that order, replace the whole of it.
  *
  * Conventions
  *   - All tensor arguments are DEVICE pointers with explicit element strides.
@@ -31,6 +31,12 @@
 #define FFTSPARSE_B200_H
 
 #include <stdint.h>
+
+#if defined(__GNUC__)
+#define FFTS_API __attribute__((visibility("default")))
+#else
+#define FFTS_API
+#endif
 
 #ifdef __cplusplus
 extern "C" {
@@ -83,13 +89,13 @@ typedef struct ffts_mask_params {
 } ffts_mask_params;
 
 /* Library version (major*10000 + minor*100 + patch). */
-int32_t ffts_version(void);
+FFTS_API int32_t ffts_version(void);
 
 /* Message for the last error returned on this thread ("" if none). */
-const char *ffts_last_error_string(void);
+FFTS_API const char *ffts_last_error_string(void);
 
 /* Upload the constant tables to `device` (idempotent, synchronous). */
-int32_t ffts_init(int32_t device);
+FFTS_API int32_t ffts_init(int32_t device);
 
 /*
  * Block mean pooling.  Replaces block_mean_pool (my_attn_v7.py:105-114) as
@@ -97,12 +103,12 @@ int32_t ffts_init(int32_t device);
  * block n (the partial last block is zero-padded and still divided by
  * block_size), rounded to the input dtype.  out is contiguous [B, H, N, D].
  */
-int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L,
+FFTS_API int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L,
                   int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_l,
                   int32_t block_size, void *out, void *stream);
 
 /* Bytes of device workspace ffts_block_mask / ffts_prefill need. */
-int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
+FFTS_API int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 
 /*
  * Block-mask selection from pooled blocks.  Replaces my_attn_v7.py:546-641:
@@ -121,7 +127,7 @@ int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
  *   stripe_var  out: fp32 [B, H] mean normalised diff variance, or NULL
  *   workspace   >= ffts_mask_workspace_bytes(...) bytes, 256-byte aligned
  */
-int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B,
+FFTS_API int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B,
                         int64_t H, int64_t Hkv, int64_t D,
                         const ffts_mask_params *params, uint32_t *mask_bits,
                         int32_t *row_count, float *corr, float *corr_sum,
@@ -132,7 +138,7 @@ int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B
  * Expand packed bits to the reference's bool block mask [B, H, N, N] (uint8),
  * i.e. the `base_blockmask` argument at my_attn_v7.py:780.
  */
-int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_t N,
+FFTS_API int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_t N,
                          uint8_t *out, void *stream);
 
 /*
@@ -147,7 +153,7 @@ int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_
  * D must be 128; block_size 32, 64 or 128; q/k/v strides multiples of 8
  * elements with unit stride in D.
  */
-int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B,
+FFTS_API int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B,
                              int64_t H, int64_t Hkv, int64_t L, int64_t D,
                              const int64_t *q_strides /* b,h,l */,
                              const int64_t *k_strides /* b,h,l */,

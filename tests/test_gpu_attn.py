@@ -1,0 +1,125 @@
+"""GPU parity of the tcgen05 block-sparse attention kernel against the fp32 CPU
+oracle.  Tolerance (bf16 inputs and output): max |err| <= 2e-2 and
+mean |err| <= 1e-3."""
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_ABS = 1e-3
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import fftsparse_b200
+    fftsparse_b200.load_library()
+    return fftsparse_b200
+
+
+def random_mask(B, H, N, density, gen, diag=True):
+    m = torch.rand(B, H, N, N, generator=gen) < density
+    m &= torch.ones(N, N, dtype=torch.bool).tril()
+    if diag:
+        m |= torch.eye(N, dtype=torch.bool)
+    return m
+
+
+def run_case(lib, B, H, Hkv, L, bs, density, seed=0, causal=True, empty_rows=False, heads=None, rows=None):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, L, 128, generator=g).bfloat16()
+    k = torch.randn(B, Hkv, L, 128, generator=g).bfloat16()
+    v = torch.randn(B, Hkv, L, 128, generator=g).bfloat16()
+    N = (L + bs - 1) // bs
+    mask = random_mask(B, H, N, density, g, diag=not empty_rows)
+    if empty_rows:
+        mask[:, :, ::3] = False
+    bits = O.pack_bool(mask)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = lib.sparse_attention(q.cuda(), k.cuda(), v.cuda(), bits.cuda(), bs, causal=causal, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, "kernel reported a wait time-out"
+    got = out.float().cpu().permute(0, 2, 1, 3)  # [B, H, L, D]
+    ref = O.sparse_attention(q, k, v, mask, bs, causal=causal, heads=heads, rows=rows)
+    if heads is not None or rows is not None:
+        sel = torch.zeros(B, H, L, dtype=torch.bool)
+        for h in (range(H) if heads is None else heads):
+            for i in (range(N) if rows is None else rows):
+                sel[:, h, i * bs:(i + 1) * bs] = True
+        got, ref = got[sel], ref[sel]
+    err = (got - ref).abs()
+    assert float(err.max()) <= MAX_ABS, float(err.max())
+    assert float(err.mean()) <= MEAN_ABS, float(err.mean())
+    return got, ref
+
+
+def test_tiny_single_tile(lib):
+    run_case(lib, 1, 1, 1, 128, 128, 1.0)
+
+
+def test_two_tiles_dense(lib):
+    run_case(lib, 1, 2, 2, 256, 128, 1.0)
+
+
+@pytest.mark.parametrize("bs", [128, 64, 32])
+def test_random_masks(lib, bs):
+    run_case(lib, 1, 4, 4, 2048, bs, 0.3, seed=bs)
+
+
+def test_ragged_length(lib):
+    run_case(lib, 1, 2, 2, 1000 + 37, 128, 0.5, seed=7)
+
+
+def test_gqa_and_batch(lib):
+    run_case(lib, 2, 8, 2, 1536, 128, 0.25, seed=11)
+
+
+def test_empty_rows_are_zero(lib):
+    got, ref = run_case(lib, 1, 2, 2, 1024, 128, 0.4, seed=5, empty_rows=True)
+    assert float(ref[..., :128, :].abs().max()) == 0.0
+
+
+def test_non_causal_flag(lib):
+    run_case(lib, 1, 2, 2, 768, 128, 0.5, seed=9, causal=False)
+
+
+def test_long_rows_subset(lib):
+    # 8K tokens, 64 key tiles per row at most; check 2 heads x 6 query blocks.
+    run_case(lib, 1, 4, 1, 8192, 128, 0.2, seed=13, heads=[0, 3], rows=[0, 1, 17, 40, 62, 63])
+
+
+def test_dense_matches_sdpa(lib):
+    g = torch.Generator().manual_seed(1)
+    L = 2048 + 64
+    q = torch.randn(1, 4, L, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(1, 4, L, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(1, 4, L, 128, generator=g).bfloat16().cuda()
+    N = (L + 127) // 128
+    bits = torch.full((1, 4, N, (N + 31) // 32), -1, dtype=torch.int32, device="cuda")
+    out = lib.sparse_attention(q, k, v, bits, 128).float().permute(0, 2, 1, 3)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=True)
+    err = (out - ref).abs()
+    assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
+
+
+def test_output_layout_and_strides(lib):
+    g = torch.Generator().manual_seed(2)
+    B, H, L = 1, 4, 512
+    base = torch.randn(B, L, H, 128, generator=g).bfloat16().cuda()
+    q = base.transpose(1, 2)  # non-contiguous [B, H, L, D] view
+    k = torch.randn(B, H, L, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(B, H, L, 128, generator=g).bfloat16().cuda()
+    N = L // 128
+    bits = torch.full((B, H, N, 1), -1, dtype=torch.int32, device="cuda")
+    out = lib.sparse_attention(q, k, v, bits, 128)
+    ref = lib.sparse_attention(q.contiguous(), k, v, bits, 128)
+    assert torch.equal(out, ref)
+
+
+def test_rejects_fp32(lib):
+    x = torch.zeros(1, 1, 128, 128, device="cuda")
+    bits = torch.full((1, 1, 1, 1), -1, dtype=torch.int32, device="cuda")
+    with pytest.raises(TypeError):
+        lib.sparse_attention(x, x, x, bits, 128)
