@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark: ms/layer of the FFTSparse prefill hot path at 128K tokens.
+
+One step = one attention layer of BASELINE config 3: block mean pooling of q
+and k, FFT-correlation block-mask selection and block-sparse causal attention
+(the whole of myattn_prefill, attn_src/fft_attn/my_attn_v7.py:454-792) for
+L = 131072 tokens, 32 query heads over 8 KV heads, head_dim 128, bf16, block
+128, keep ratio 0.05, on seeded synthetic inputs (fftsparse_b200/synthetic.py).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N = 1 calls the drop-in ``myattn_prefill`` with repeat_kv-expanded k/v, the
+exact call of the reference's benchmark
+(eval/efficiency/benchmark_attention_multilayer.py:146-157, :308).  N > 1
+(launched by torchrun, one rank per GPU, NCCL) shards the 8 KV groups over the
+ranks and all-gathers the head-major outputs (fftsparse_b200/dist.py); total
+work is fixed, so the scaling is strong.  ``--impl reference`` times the CPU
+restatement of the reference path (oracle/) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "ms/layer (FFT mask select + block-sparse attn) at 128k"
+UNIT = "ms/layer"
+SEQ_LEN = 131072
+HQ, HKV, HEAD_DIM, BLOCK = 32, 8, 128, 128
+
+
+def mask_kwargs(keep_ratio: float) -> dict:
+    """Keep ratio r -> the reference's arguments (topk mode; efficiency-script ratios,
+    eval/efficiency/1_run_eval_multilayer.sh:46-63, :72)."""
+    return dict(block_size=BLOCK, sink_ratio=0.01, recent_ratio=0.0, local_span_ratio=0.02,
+                enable_correlation_mask=True, correlation_selection_mode="topk",
+                correlation_topk_ratio=keep_ratio, corr_threshold=1.0, enable_column_mask=True,
+                column_topk_ratio=0.2, enable_last_block_mask=True, diag_sample_ratio=0.15,
+                min_diag_samples=5, max_diag_samples=64, qk_topk_ratio=keep_ratio,
+                stripe_threshold=0.3)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--keep-ratio", type=float, default=0.05)
+    ap.add_argument("--seq-len", type=int, default=SEQ_LEN)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- helpers
+def load_peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(HERE, "gpurun_out", f"clocks_gpu{index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
+                             parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(loaded)}
+
+
+def causal_pairs(bits: torch.Tensor, L: int, bs: int) -> int:
+    """Exact number of kept (query, key) pairs with key <= query."""
+    B, H, N, W = bits.shape
+    shifts = torch.arange(32, device=bits.device, dtype=torch.int64)
+    dense = ((bits.to(torch.int64)[..., None] >> shifts) & 1).reshape(B, H, N, W * 32)[..., :N].to(torch.int64)
+    sizes = torch.full((N,), bs, dtype=torch.int64, device=bits.device)
+    sizes[-1] = L - (N - 1) * bs
+    full = (dense * sizes[None, None, :, None] * sizes[None, None, None, :]).sum()
+    diag = torch.diagonal(dense, dim1=2, dim2=3)  # [B, H, N]
+    tri = sizes * (sizes + 1) // 2
+    # replace the diagonal's rows*cols by the causal triangle
+    corr = (diag * (tri - sizes * sizes)[None, None, :]).sum()
+    return int(full + corr)
+
+
+# ----------------------------------------------------------- CPU baseline
+def cpu_baseline_sample(q, k, v, keep_ratio, heads_sample=1):
+    """Oracle port on the host cores: full-size mask selection for all heads
+    (C, OpenMP) plus fp32 attention for ``heads_sample`` heads, scaled to H."""
+    from oracle import oracle as O  # the checker, timed here as the CPU baseline
+    from fftsparse_b200.params import derive_mask_params
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    kw = mask_kwargs(keep_ratio)
+    L = q.shape[2]
+    params = derive_mask_params(L, **kw)
+    t0 = time.perf_counter()
+    ref = O.prefill_mask(q, k, params)
+    t_mask = time.perf_counter() - t0
+    mask = O.unpack_bits(ref["bits"], params.n_blocks)
+    H = q.shape[1]
+    heads = list(range(heads_sample))
+    t0 = time.perf_counter()
+    O.sparse_attention(q, k, v, mask, BLOCK, heads=heads)
+    t_attn = time.perf_counter() - t0
+    ms = 1e3 * (t_mask + t_attn * H / heads_sample)
+    return ms, {"mask_s": t_mask, "attn_s_per_head": t_attn / heads_sample,
+                "threads": torch.get_num_threads(), "cpu_count": os.cpu_count()}
+
+
+def run_reference(args):
+    """--impl reference: the CPU path on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from fftsparse_b200.synthetic import make_inputs
+    q, k, v = make_inputs(args.seq_len, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16)
+    times, info = [], {}
+    for i in range(args.warmup + args.steps):
+        ms, info = cpu_baseline_sample(q, k, v, args.keep_ratio)
+        if i >= args.warmup:
+            times.append(ms)
+    value = sum(times) / len(times)
+    sample = (f"per step: full {args.seq_len}-token mask selection for all {HQ} heads + fp32 attention "
+              f"for 1 head, attention scaled x{HQ}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"cfg3: L={args.seq_len}, Hq={HQ}, Hkv={HKV} (expanded), D={HEAD_DIM}, "
+                               f"block {BLOCK}, keep ratio {args.keep_ratio}", "seq_len": args.seq_len,
+                   "global_batch": 1, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": info.get("threads"),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "detail": info,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch.distributed as dist
+
+    import fftsparse_b200 as F
+    from fftsparse_b200.dist import kv_group_shard, local_views, sharded_prefill
+    from fftsparse_b200.synthetic import make_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    F.load_library()
+    kw = mask_kwargs(args.keep_ratio)
+    L = args.seq_len
+
+    # inputs: CPU draws (same values on every rank), RoPE and cast on the device
+    q, k, v = make_inputs(L, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16, device=str(dev))
+    torch.cuda.synchronize(dev)
+
+    def step():
+        if world == 1:
+            return F.myattn_prefill(q, k, v, 0, **kw)
+        return sharded_prefill(q, k, v, 0, num_kv_heads=HKV, **kw)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        torch.cuda.synchronize(dev)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+
+    # ---- per-stage timing and the attention kernel's roofline (rank-local shard)
+    shard = kv_group_shard(HQ, HKV, world, rank)
+    ql, kl, vl = local_views(q, k, v, shard)
+    mask = F.fft_block_mask(ql, kl, **kw)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    reps = max(3, args.steps)
+    ev[0].record(stream)
+    for _ in range(reps):
+        F.pool_blocks(ql, BLOCK)
+        F.pool_blocks(kl, BLOCK)
+    ev[1].record(stream)
+    for _ in range(reps):
+        F.fft_block_mask(ql, kl, **kw)
+    ev[2].record(stream)
+    out_l = torch.empty(1, L, shard.heads, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    for _ in range(reps):
+        F.sparse_attention(ql, kl, vl, mask.bits, BLOCK, out=out_l)
+    ev[3].record(stream)
+    torch.cuda.synchronize(dev)
+    t_pool = ev[0].elapsed_time(ev[1]) / reps
+    t_mask = ev[1].elapsed_time(ev[2]) / reps  # includes pooling
+    t_attn = ev[2].elapsed_time(ev[3]) / reps
+    pairs = causal_pairs(mask.bits, L, BLOCK)
+    flops = 4.0 * HEAD_DIM * pairs
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    achieved = flops / (t_attn * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(HERE, "profiles", "attn_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    roofline = {"kernel": "sparse_attn_kernel", "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
+                "peak_kind": f"{peak_kind} bf16 burst", "traffic": traffic,
+                "algorithmic_flops_per_launch": flops, "launch_ms": round(t_attn, 4),
+                "causal_pair_density": pairs / (shard.heads * L * (L + 1) / 2)}
+    pool_bytes = (ql.numel() + kl.numel()) * 2 + mask.q_pooled.numel() * 2 + mask.k_pooled.numel() * 2
+    stages = {"pool_ms": round(t_pool, 4), "pool_gbs": round(pool_bytes / (t_pool * 1e-3) / 1e9, 1),
+              "pool_frac_hbm": round(pool_bytes / (t_pool * 1e-3) / 1e9 / hbm_peak, 4),
+              "select_ms": round(t_mask - t_pool, 4), "attention_ms": round(t_attn, 4),
+              "block_density": round(mask.density(), 5),
+              "stripe_heads": int(mask.is_stripe.sum().item())}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        qh, kh, vh = (x.cpu().pin_memory() for x in local_views(q, k, v, shard))
+        res_h = torch.empty(1, shard.heads, L, HEAD_DIM, dtype=torch.bfloat16).pin_memory() if world > 1 else \
+            torch.empty(1, L, HQ * HEAD_DIM, dtype=torch.bfloat16).pin_memory()
+        del q, k, v
+        torch.cuda.empty_cache()
+
+        def e2e_step():
+            qd = qh.to(dev, non_blocking=True)
+            kd = kh.to(dev, non_blocking=True)
+            vd = vh.to(dev, non_blocking=True)
+            if world == 1:
+                o = F.myattn_prefill(qd, kd, vd, 0, **kw)
+                res_h.copy_(o, non_blocking=True)
+            else:
+                from fftsparse_b200.dist import gather_heads  # noqa: F401
+                full = sharded_prefill(qd, kd, vd, 0, num_kv_heads=HKV // world, **kw)
+                res_h.copy_(full[:, shard.h_lo:shard.h_hi], non_blocking=True)
+
+        # note: for N > 1 each rank receives only its own q/k/v heads
+        if world > 1:
+            def e2e_step():  # noqa: F811
+                qd = qh.to(dev, non_blocking=True)
+                kd = kh.to(dev, non_blocking=True)
+                vd = vh.to(dev, non_blocking=True)
+                m = F.fft_block_mask(qd, kd, **kw)
+                lo = torch.empty(1, shard.heads, L, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+                F.sparse_attention(qd, kd, vd, m.bits, BLOCK, out=lo.permute(0, 2, 1, 3))
+                full = torch.empty(1, HQ, L, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+                from fftsparse_b200.dist import gather_heads
+                gather_heads(lo, full)
+                res_h.copy_(lo, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e2.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        te = torch.tensor([s2.elapsed_time(e2) / args.e2e_steps], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(float(te.item()), 3), "unit": UNIT,
+               "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 2),
+               "d2h_bytes_per_step": int(res_h.numel() * 2), "steps": args.e2e_steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from fftsparse_b200.synthetic import make_inputs as mk
+        qc, kc, vc = mk(L, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16)
+        cms, info = cpu_baseline_sample(qc, kc, vc, args.keep_ratio)
+        cpu = {"value": round(cms, 1), "unit": UNIT, "cores": info["threads"], "kind": "port",
+               "sample": f"full {L}-token mask selection (C oracle, {info['cpu_count']} OpenMP threads) + fp32 "
+                         f"attention for 1 of {HQ} heads scaled x{HQ}; mask {info['mask_s']:.2f} s, "
+                         f"attention {info['attn_s_per_head']:.2f} s/head"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(ms_max, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms_max, 4), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"cfg3: L={L}, Hq={HQ}, Hkv={HKV}, D={HEAD_DIM}, block {BLOCK}, keep ratio "
+                                   f"{args.keep_ratio} (topk mode, efficiency-script ratios); "
+                                   + ("drop-in myattn_prefill with repeat_kv-expanded k/v" if world == 1 else
+                                      f"KV groups sharded {HKV // world} per rank + NCCL all-gather of outputs"),
+                       "model": "Llama-3.1-8B attention-layer shape", "seq_len": L, "global_batch": 1,
+                       "parallelism": "single GPU" if world == 1 else f"kv-group x{world}",
+                       "l2": "inputs (3.2 GB) larger than L2; no flush"},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": 7 * args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "stages": stages,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
