@@ -39,7 +39,8 @@ constexpr int kThreads = 192;  // 6 warps
 constexpr int kTileBytes = kBM * kD * 2;     // 32 KB (two 16 KB swizzle boxes)
 constexpr int kHalfBytes = kTileBytes / 2;   // one [128 rows][64 cols] box
 constexpr int kMaxTiles = 4096;              // key tiles per row of tiles
-constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s bound on any single wait
+constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 1.965 GHz: bound on one wait
+constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own copies / MMAs
 
 // status codes written to the caller's status word
 constexpr int kErrTimeoutProducer = 1;
@@ -78,12 +79,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
@@ -110,14 +105,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false on time-out or when another role has aborted the CTA.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+// Bounded wait: false on time-out (SM clock cycles) or when another role has
+// aborted the CTA.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          long long limit = kWaitCycles) {
   if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 
@@ -217,7 +214,7 @@ constexpr uint32_t idesc_bf16(bool b_mn_major) {
 }
 
 struct Params {
-  int B, H, Hkv, L, bs, causal;
+  int B, H, Hkv, L, bs, bs_shift, causal;
   int nq;         // query tiles per head
   int nblk;       // mask blocks per row (N)
   int W;          // mask words per row
@@ -372,11 +369,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         atomicCAS(prm.status, 0, kErrTimeoutProducer);
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
-        mbar_wait(bar(BQ), 0, &never);
+        mbar_wait(bar(BQ), 0, &never, kDrainCycles);
         for (int n = max(0, issued_k - kStages); n < issued_k; ++n)
-          mbar_wait(bar(BKF + n % kStages), (n / kStages) & 1, &never);
+          mbar_wait(bar(BKF + n % kStages), (n / kStages) & 1, &never, kDrainCycles);
         for (int n = max(0, issued_v - kStages); n < issued_v; ++n)
-          mbar_wait(bar(BVF + n % kStages), (n / kStages) & 1, &never);
+          mbar_wait(bar(BVF + n % kStages), (n / kStages) & 1, &never, kDrainCycles);
       }
     }
   } else if (warp == 5) {
@@ -428,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // drain: wait (bounded) until every MMA this thread issued has completed
       umma_commit(bar(BDRAIN));
       volatile int never = 0;
-      mbar_wait(bar(BDRAIN), 0, &never);
+      mbar_wait(bar(BDRAIN), 0, &never, kDrainCycles);
     }
   } else {
     // ================================================================ softmax (warps 0-3)
@@ -446,38 +443,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j = list[n];
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
       fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tm_s0 + sb * 128 + lane_off + c * 32, s + c * 32);
-      tmem_wait_ld();
-      fence_before();
-      mbar_arrive(bar(BSE + sb));
-      // masks: causal diagonal, ragged end, sub-block selection
+      const uint32_t s_addr = tm_s0 + sb * 128 + lane_off;
+      // masks: causal diagonal, ragged end, sub-block selection (tile-uniform test)
       const int col0 = j * kBN;
-      int lim = prm.L - col0;                     // columns < lim are in range
-      if (prm.causal && j == qt) lim = min(lim, r + 1);
+      const bool edge = (prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1;
+      int lim = 128;
       uint32_t subm = 0xffffffffu;
-      if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const bool keep = c < lim && ((subm >> (c / prm.bs)) & 1u);
-        s[c] = keep ? s[c] : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+      if (edge) {
+        lim = min(128, prm.L - col0);
+        if (prm.causal && j == qt) lim = min(lim, r + 1);
+        if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
       }
+      // pass 1: row max, 32 columns at a time
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32];
+        tmem_ld32(s_addr + c * 32, x);
+        tmem_wait_ld();
+        if (edge) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = c * 32 + e;
+            if (!(col < lim && ((subm >> (col >> prm.bs_shift)) & 1u))) x[e] = -INFINITY;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], x[e]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_new = fmaxf(m_run, mx);
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = fast_exp2((m_run - m_use) * prm.scale_log2);
       const float moff = m_use * prm.scale_log2;
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], prm.scale_log2, -moff));
-        rs += s[c];
-      }
-      l_run = l_run * alpha + rs;
       m_run = m_new;
       if (n >= 1) {
+        // PV(n-1) must be complete: it read P and accumulated into O
         if (!__all_sync(0xffffffffu, mbar_wait(bar(BOF), (n - 1) & 1, abort_flag))) { ok = false; break; }
         fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -493,19 +494,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
-      // P row r -> shared memory, K-major with the 128-byte swizzle
+      // pass 2: P = exp2(s*scale - m), row sum, bf16 P row -> shared memory
+      // (K-major with the 128-byte swizzle: 16-byte chunk c16 of row r at c16 ^ (r & 7))
+      float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x[32];
+        tmem_ld32(s_addr + c * 32, x);
+        tmem_wait_ld();
+        if (edge) {
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(s[ch * 8 + 2 * e], s[ch * 8 + 2 * e + 1]);
-          w[e] = *reinterpret_cast<const uint32_t *>(&pr);
+          for (int e = 0; e < 32; ++e) {
+            const int col = c * 32 + e;
+            if (!(col < lim && ((subm >> (col >> prm.bs_shift)) & 1u))) x[e] = -INFINITY;
+          }
         }
-        const int half = ch >> 3, c16 = ch & 7;
-        uint8_t *dst = pbase + half * kHalfBytes + r * 128 + ((c16 ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          x[e] = fast_exp2(fmaf(x[e], prm.scale_log2, -moff));
+          rs4[e & 3] += x[e];
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(x[q4 * 8 + 2 * e], x[q4 * 8 + 2 * e + 1]);
+            w[e] = *reinterpret_cast<const uint32_t *>(&pr);
+          }
+          const int ch = c * 4 + q4;  // 16-byte chunk index in the 256-byte row
+          const int half = ch >> 3, c16 = ch & 7;
+          uint8_t *dst = pbase + half * kHalfBytes + r * 128 + ((c16 ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
+      // S buffer sb is free once both passes have read it
+      fence_before();
+      mbar_arrive(bar(BSE + sb));
+      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       fence_proxy_async();
       fence_before();
       mbar_arrive(bar(BPF));
@@ -616,6 +642,7 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   if (rc) return rc;
   Params p{};
   p.B = int(B); p.H = int(H); p.Hkv = int(Hkv); p.L = int(L); p.bs = bs; p.causal = causal ? 1 : 0;
+  p.bs_shift = bs == 32 ? 5 : (bs == 64 ? 6 : 7);
   p.nq = int(nq); p.nblk = int(nblk); p.W = int(ceil_div(nblk, 32));
   p.bits = bits;
   p.out = static_cast<__nv_bfloat16 *>(out);
