@@ -33,6 +33,8 @@ EXPORTS = {
     "ffts_mask_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64]),
     "ffts_block_mask": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
                                _I64, _P]),
+    "ffts_block_mask_noalloc": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P,
+                                       _P]),
     "ffts_unpack_mask": (_I32, [_P, _I64, _I64, _I64, _P, _P]),
     "ffts_sparse_attn_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I32,
                                     _I32, _P, _P, _P, _P]),

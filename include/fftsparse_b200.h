@@ -135,6 +135,27 @@ FFTS_API int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, 
                         int64_t workspace_bytes, void *stream);
 
 /*
+ * ffts_block_mask without a workspace argument.  No counterpart in the
+ * reference.  It is for callers that may not allocate device memory when they
+ * run the selection, such as an engine that reserves all GPU memory for its
+ * own pool at start-up, or a plugin hook that must not call cudaMalloc because
+ * it can synchronise the device.  It runs the same kernels on a scratch array
+ * of 8 MiB compiled into the library (resident on every GPU that loads it) and
+ * allocates nothing.  Shapes whose ffts_mask_workspace_bytes(...) exceeds 8 MiB
+ * are rejected with FFTS_E_WORKSPACE (128K tokens x 32 heads needs about
+ * 4.2 MB).  The first call on a device looks up the scratch address and may
+ * upload the constant tables: make it before any stream capture.  All calls on
+ * a device share the scratch, so calls whose kernels overlap on the GPU race;
+ * serialise them.
+ */
+FFTS_API int32_t ffts_block_mask_noalloc(const void *qb, const void *kb, int32_t dtype,
+                                         int64_t B, int64_t H, int64_t Hkv, int64_t D,
+                                         const ffts_mask_params *params,
+                                         uint32_t *mask_bits, int32_t *row_count,
+                                         float *corr, float *corr_sum, uint8_t *is_stripe,
+                                         float *stripe_var, void *stream);
+
+/*
  * Expand packed bits to the reference's bool block mask [B, H, N, N] (uint8),
  * i.e. the `base_blockmask` argument at my_attn_v7.py:780.
  */
