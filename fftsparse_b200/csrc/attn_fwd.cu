@@ -34,7 +34,6 @@ namespace attn {
 constexpr int kBM = 128;       // query rows per tile
 constexpr int kBN = 128;       // key columns per tile
 constexpr int kD = 128;        // head dim
-constexpr int kStages = 2;     // K/V ring depth
 constexpr int kThreads = 192;  // 6 warps
 constexpr int kTileBytes = kBM * kD * 2;     // 32 KB (two 16 KB swizzle boxes)
 constexpr int kHalfBytes = kTileBytes / 2;   // one [128 rows][64 cols] box
@@ -46,33 +45,6 @@ constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own
 constexpr int kErrTimeoutProducer = 1;
 constexpr int kErrTimeoutMma = 2;
 constexpr int kErrTimeoutSoftmax = 3;
-
-struct SmemLayout {
-  // offsets from the 1024-byte aligned base
-  static constexpr int q = 0;
-  static constexpr int k = q + kTileBytes;
-  static constexpr int v = k + kStages * kTileBytes;
-  static constexpr int p = v + kStages * kTileBytes;
-  static constexpr int bars = p + kTileBytes;  // 64 bytes of mbarriers each 8 B
-  static constexpr int nbars = 1 + 4 * kStages + 2 + 2 + 2;
-  static constexpr int tmem_slot = bars + nbars * 8;
-  static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
-  static constexpr int list = misc + 16;        // uint16 tile list
-  static constexpr int end = list + kMaxTiles * 2;
-  static constexpr int bytes = end + 1024;      // + alignment slack
-};
-
-// barrier indices
-constexpr int BQ = 0;
-constexpr int BKF = 1;                 // + stage
-constexpr int BVF = BKF + kStages;     // + stage
-constexpr int BKE = BVF + kStages;     // + stage
-constexpr int BVE = BKE + kStages;     // + stage
-constexpr int BSF = BVE + kStages;     // + s buffer
-constexpr int BSE = BSF + 2;           // + s buffer
-constexpr int BOF = BSE + 2;
-constexpr int BPF = BOF + 1;
-constexpr int BDRAIN = BPF + 1;
 
 // ------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -150,6 +122,36 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// A operand from TMEM (P), B from shared memory (V).
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+      "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+      "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
   uint32_t r[32];
   asm volatile(
@@ -191,6 +193,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for x <= 0 on the FMA pipe: 2^x = 2^floor(x) * 2^f, f in [0, 1), with 2^f
+// from a degree-3 polynomial fitted here to minimise the relative error on
+// [0, 1) (max relative error 7.5e-5, far below bf16's 3.9e-3 for P); the power
+// of two is added to the exponent bits.  Inputs below -126 (including -inf)
+// give exactly 0.
+__device__ __forceinline__ float poly_exp2(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float xi = floorf(xc);
+  const float f = xc - xi;
+  float p = fmaf(0.07802451401948929f, f, 0.2260671705007553f);
+  p = fmaf(p, f, 0.6958335638046265f);
+  p = fmaf(p, f, 0.9999251961708069f);
+  const float r = __int_as_float(__float_as_int(p) + (static_cast<int>(xi) << 23));
+  return x < -126.0f ? 0.0f : r;
+}
+
 // Shared-memory matrix descriptor (tcgen05 "version 1" format).
 // SWIZZLE_128B; lbo/sbo in bytes.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -213,6 +231,43 @@ constexpr uint32_t idesc_bf16(bool b_mn_major) {
          | (uint32_t(kBM >> 4) << 24);    // M
 }
 
+// ------------------------------------------------------------------ layout
+constexpr int kKStages = 3;    // K tile ring
+constexpr int kVStages = 2;    // V tile ring
+constexpr int kSBufs = 3;      // S/P accumulators in TMEM (P overwrites its S buffer)
+constexpr int kPolyEvery = 4;  // one exp2 in kPolyEvery on the FMA pipe, the rest on MUFU
+constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
+
+struct SmemLayout {
+  // offsets from the 1024-byte aligned base
+  static constexpr int q = 0;
+  static constexpr int k = q + kTileBytes;
+  static constexpr int v = k + kKStages * kTileBytes;
+  static constexpr int bars = v + kVStages * kTileBytes;
+  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 3;
+  static constexpr int tmem_slot = bars + nbars * 8;
+  static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
+  static constexpr int list = misc + 16;        // uint16 tile list
+  static constexpr int end = list + kMaxTiles * 2;
+  static constexpr int bytes = end + 1024;      // + alignment slack
+};
+static_assert(SmemLayout::bytes <= 227 * 1024, "shared memory budget");
+
+// barrier indices
+constexpr int BQ = 0;
+constexpr int BKF = 1;                  // K full      [kKStages]
+constexpr int BKE = BKF + kKStages;     // K empty     [kKStages]
+constexpr int BVF = BKE + kKStages;     // V full      [kVStages]
+constexpr int BVE = BVF + kVStages;     // V empty     [kVStages]
+constexpr int BSF = BVE + kVStages;     // S full      [kSBufs]
+constexpr int BPV = BSF + kSBufs;       // PV done with this S/P buffer [kSBufs]
+constexpr int BOF = BPV + kSBufs;       // PV(m) complete (one phase per tile)
+constexpr int BPF = BOF + 1;            // P(m) written to TMEM, O rescaled (128 arrivals)
+constexpr int BDRAIN = BPF + 1;
+
+// TMEM columns: S/P buffers at 0, 128, 256; O at 384
+constexpr uint32_t kTmemO = 384;
+
 struct Params {
   int B, H, Hkv, L, bs, bs_shift, causal;
   int nq;         // query tiles per head
@@ -225,7 +280,7 @@ struct Params {
   int *status;
 };
 
-// Tile bits of 32 consecutive key tiles [32*tw, 32*tw+32) for mask row `mrow`
+// Tile bits of 32 consecutive key tiles [32*tw, 32*tw+32) for mask row `row`
 // when each 128-wide tile covers `sub` mask blocks.
 __device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw, int sub) {
   if (sub == 1) return tw < W ? row[tw] : 0u;
@@ -271,15 +326,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     mbar_init(bar(BQ), 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar(BKF + s), 1);
-      mbar_init(bar(BVF + s), 1);
       mbar_init(bar(BKE + s), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(bar(BVF + s), 1);
       mbar_init(bar(BVE + s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kSBufs; ++s) {
       mbar_init(bar(BSF + s), 1);
-      mbar_init(bar(BSE + s), 128);
+      mbar_init(bar(BPV + s), 1);
     }
     mbar_init(bar(BOF), 1);
     mbar_init(bar(BPF), 128);
@@ -337,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
   const int ntiles = *ntiles_sh;
-  const uint32_t tm_s0 = tmem, tm_o = tmem + 256;
+  const uint32_t tm_o = tmem + kTmemO;
 
   if (warp == 4) {
     // ================================================================ TMA producer
@@ -347,33 +404,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive_tx(bar(BQ), kTileBytes);
       tma_load_4d(sbase + SmemLayout::q, &tm_q, bar(BQ), 0, qt * kBM, h, b);
       tma_load_4d(sbase + SmemLayout::q + kHalfBytes, &tm_q, bar(BQ), 64, qt * kBM, h, b);
-      for (int n = 0; n < ntiles && ok; ++n) {
-        const int s = n % kStages;
-        const uint32_t par = ((n / kStages) & 1) ^ 1;
-        const int j = list[n];
-        if (!mbar_wait(bar(BKE + s), par, abort_flag)) { ok = false; break; }
+      auto load_k = [&](int n) -> bool {
+        const int s = n % kKStages;
+        if (!mbar_wait(bar(BKE + s), ((n / kKStages) & 1) ^ 1, abort_flag)) return false;
         mbar_arrive_tx(bar(BKF + s), kTileBytes);
-        const uint32_t kd = sbase + SmemLayout::k + s * kTileBytes;
-        tma_load_4d(kd, &tm_k, bar(BKF + s), 0, j * kBN, kvh, b);
-        tma_load_4d(kd + kHalfBytes, &tm_k, bar(BKF + s), 64, j * kBN, kvh, b);
+        const uint32_t dst = sbase + SmemLayout::k + s * kTileBytes;
+        const int j = list[n];
+        tma_load_4d(dst, &tm_k, bar(BKF + s), 0, j * kBN, kvh, b);
+        tma_load_4d(dst + kHalfBytes, &tm_k, bar(BKF + s), 64, j * kBN, kvh, b);
         ++issued_k;
-        if (!mbar_wait(bar(BVE + s), par, abort_flag)) { ok = false; break; }
+        return true;
+      };
+      auto load_v = [&](int n) -> bool {
+        const int s = n % kVStages;
+        if (!mbar_wait(bar(BVE + s), ((n / kVStages) & 1) ^ 1, abort_flag)) return false;
         mbar_arrive_tx(bar(BVF + s), kTileBytes);
-        const uint32_t vd = sbase + SmemLayout::v + s * kTileBytes;
-        tma_load_4d(vd, &tm_v, bar(BVF + s), 0, j * kBN, kvh, b);
-        tma_load_4d(vd + kHalfBytes, &tm_v, bar(BVF + s), 64, j * kBN, kvh, b);
+        const uint32_t dst = sbase + SmemLayout::v + s * kTileBytes;
+        const int j = list[n];
+        tma_load_4d(dst, &tm_v, bar(BVF + s), 0, j * kBN, kvh, b);
+        tma_load_4d(dst + kHalfBytes, &tm_v, bar(BVF + s), 64, j * kBN, kvh, b);
         ++issued_v;
+        return true;
+      };
+      // K runs one tile ahead of V: K(n) is released by S(n-3), V(n-1) by PV(n-3)
+      for (int n = 0; n < ntiles && ok; ++n) {
+        ok = load_k(n);
+        if (ok && n >= 1) ok = load_v(n - 1);
       }
+      if (ok) ok = load_v(ntiles - 1);
       if (!ok) {
         *abort_flag = 1;
         atomicCAS(prm.status, 0, kErrTimeoutProducer);
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
         mbar_wait(bar(BQ), 0, &never, kDrainCycles);
-        for (int n = max(0, issued_k - kStages); n < issued_k; ++n)
-          mbar_wait(bar(BKF + n % kStages), (n / kStages) & 1, &never, kDrainCycles);
-        for (int n = max(0, issued_v - kStages); n < issued_v; ++n)
-          mbar_wait(bar(BVF + n % kStages), (n / kStages) & 1, &never, kDrainCycles);
+        for (int n = max(0, issued_k - kKStages); n < issued_k; ++n)
+          mbar_wait(bar(BKF + n % kKStages), (n / kKStages) & 1, &never, kDrainCycles);
+        for (int n = max(0, issued_v - kVStages); n < issued_v; ++n)
+          mbar_wait(bar(BVF + n % kVStages), (n / kVStages) & 1, &never, kDrainCycles);
       }
     }
   } else if (warp == 5) {
@@ -383,38 +451,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(bar(BQ), 0, abort_flag);
       fence_after();
       auto issue_pv = [&](int m) -> bool {
-        const int s = m % kStages;
-        if (!mbar_wait(bar(BVF + s), (m / kStages) & 1, abort_flag)) return false;
+        const int vs = m % kVStages, pb = m % kSBufs;
+        if (!mbar_wait(bar(BVF + vs), (m / kVStages) & 1, abort_flag)) return false;
         if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t vb = sbase + SmemLayout::v + s * kTileBytes;
-        const uint32_t pb = sbase + SmemLayout::p;
+        const uint32_t vsm = sbase + SmemLayout::v + vs * kTileBytes;
+        const uint32_t pt = tmem + pb * 128;  // P (bf16 pairs) in the first 64 columns
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = smem_desc(pb + (kk >> 2) * kHalfBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc(vb + kk * 2048, kHalfBytes, 1024);
-          umma_f16(tm_o, ad, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t bd = smem_desc(vsm + kk * 2048, kHalfBytes, 1024);
+          umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar(BOF));
-        umma_commit(bar(BVE + s));
+        umma_commit(bar(BVE + vs));
+        umma_commit(bar(BPV + pb));
         return true;
       };
       for (int n = 0; n < ntiles && ok; ++n) {
-        const int s = n % kStages, sb = n & 1;
-        ok = mbar_wait(bar(BKF + s), (n / kStages) & 1, abort_flag);
-        if (ok && n >= 2) ok = mbar_wait(bar(BSE + sb), ((n >> 1) - 1) & 1, abort_flag);
+        const int ks = n % kKStages, sb = n % kSBufs;
+        ok = mbar_wait(bar(BKF + ks), (n / kKStages) & 1, abort_flag);
+        // buffer sb last held P(n-3): PV(n-3) must have finished reading it
+        if (ok && n >= kSBufs) ok = mbar_wait(bar(BPV + sb), ((n / kSBufs) - 1) & 1, abort_flag);
         if (!ok) break;
         fence_after();
-        const uint32_t kb = sbase + SmemLayout::k + s * kTileBytes;
-        const uint32_t qb = sbase + SmemLayout::q;
+        const uint32_t ksm = sbase + SmemLayout::k + ks * kTileBytes;
+        const uint32_t qsm = sbase + SmemLayout::q;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16(tm_s0 + sb * 128, smem_desc(qb + off, 16, 1024), smem_desc(kb + off, 16, 1024), idS,
+          umma_f16(tmem + sb * 128, smem_desc(qsm + off, 16, 1024), smem_desc(ksm + off, 16, 1024), idS,
                    kk > 0 ? 1u : 0u);
         }
         umma_commit(bar(BSF + sb));
-        umma_commit(bar(BKE + s));
+        umma_commit(bar(BKE + ks));
         if (n >= 1) ok = issue_pv(n - 1);
       }
       if (ok) ok = issue_pv(ntiles - 1);
@@ -432,53 +501,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = threadIdx.x;  // query row within the tile == TMEM lane
     const int row_g = qt * kBM + r;
     const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.0f;
+    // m_ref: the max the current P and O are scaled to (lags the true max by < 2^8)
+    float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     const int mrow = qt * sub + r / prm.bs;
     const uint32_t *rowbits =
         prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + min(mrow, prm.nblk - 1)) * prm.W;
-    uint8_t *pbase = smem + SmemLayout::p;
     for (int n = 0; n < ntiles; ++n) {
-      const int sb = n & 1;
+      const int sb = n % kSBufs;
       const int j = list[n];
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n / kSBufs) & 1, abort_flag))) { ok = false; break; }
       fence_after();
-      const uint32_t s_addr = tm_s0 + sb * 128 + lane_off;
+      const uint32_t s_addr = tmem + sb * 128 + lane_off;
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s + c * 32);
+      tmem_wait_ld();
       // masks: causal diagonal, ragged end, sub-block selection (tile-uniform test)
       const int col0 = j * kBN;
-      const bool edge = (prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1;
-      int lim = 128;
-      uint32_t subm = 0xffffffffu;
-      if (edge) {
-        lim = min(128, prm.L - col0);
+      if ((prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1) {
+        // keep-bits of this row's 128 columns, one word per 32 columns (a 32-column
+        // word never straddles a mask block since block_size >= 32)
+        int lim = min(128, prm.L - col0);
         if (prm.causal && j == qt) lim = min(lim, r + 1);
+        uint32_t subm = 0xffffffffu;
         if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
-      }
-      // pass 1: row max, 32 columns at a time
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float x[32];
-        tmem_ld32(s_addr + c * 32, x);
-        tmem_wait_ld();
-        if (edge) {
+        uint32_t kw[4];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = c * 32 + e;
-            if (!(col < lim && ((subm >> (col >> prm.bs_shift)) & 1u))) x[e] = -INFINITY;
-          }
+        for (int w = 0; w < 4; ++w) {
+          const int rem = lim - 32 * w;
+          uint32_t m = rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : ((1u << rem) - 1u));
+          if (!((subm >> ((32 * w) >> prm.bs_shift)) & 1u)) m = 0u;
+          kw[w] = m;
         }
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], x[e]);
+        for (int c = 0; c < 128; ++c)
+          if (!((kw[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
       }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-      const float alpha = fast_exp2((m_run - m_use) * prm.scale_log2);
-      const float moff = m_use * prm.scale_log2;
-      m_run = m_new;
+      // lazy rescale: keep m_ref unless the row max exceeds it by more than 2^8
+      float alpha = 1.0f;
+      const bool grow = mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * prm.scale_log2 > kRescaleLog2);
+      if (grow) {
+        alpha = m_ref == -INFINITY ? 0.0f : fast_exp2((m_ref - mx) * prm.scale_log2);
+        m_ref = mx;
+      }
+      const float moff = (m_ref == -INFINITY ? 0.0f : m_ref) * prm.scale_log2;
+      float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // P overwrites the first 64 columns of its S buffer, 16 columns (32 values) at a time
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int c = cc * 32 + e;
+          const float a0 = fmaf(s[c], prm.scale_log2, -moff);
+          const float a1 = fmaf(s[c + 1], prm.scale_log2, -moff);
+          const float e0 = fast_exp2(a0);
+          const float e1 = ((c + 1) % kPolyEvery == kPolyEvery - 1) ? poly_exp2(a1) : fast_exp2(a1);
+          rs4[c & 3] += e0;
+          rs4[(c + 1) & 3] += e1;
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(e0, e1);
+          pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
+        }
+        tmem_st16u(s_addr + cc * 16, pk);
+      }
+      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
+      tmem_wait_st();
       if (n >= 1) {
-        // PV(n-1) must be complete: it read P and accumulated into O
+        // PV(n-1) has accumulated into O: rescale rows whose reference max moved
         if (!__all_sync(0xffffffffu, mbar_wait(bar(BOF), (n - 1) & 1, abort_flag))) { ok = false; break; }
         fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -494,45 +588,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_st();
         }
       }
-      // pass 2: P = exp2(s*scale - m), row sum, bf16 P row -> shared memory
-      // (K-major with the 128-byte swizzle: 16-byte chunk c16 of row r at c16 ^ (r & 7))
-      float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float x[32];
-        tmem_ld32(s_addr + c * 32, x);
-        tmem_wait_ld();
-        if (edge) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = c * 32 + e;
-            if (!(col < lim && ((subm >> (col >> prm.bs_shift)) & 1u))) x[e] = -INFINITY;
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          x[e] = fast_exp2(fmaf(x[e], prm.scale_log2, -moff));
-          rs4[e & 3] += x[e];
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(x[q4 * 8 + 2 * e], x[q4 * 8 + 2 * e + 1]);
-            w[e] = *reinterpret_cast<const uint32_t *>(&pr);
-          }
-          const int ch = c * 4 + q4;  // 16-byte chunk index in the 256-byte row
-          const int half = ch >> 3, c16 = ch & 7;
-          uint8_t *dst = pbase + half * kHalfBytes + r * 128 + ((c16 ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      // S buffer sb is free once both passes have read it
-      fence_before();
-      mbar_arrive(bar(BSE + sb));
-      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
-      fence_proxy_async();
       fence_before();
       mbar_arrive(bar(BPF));
     }
