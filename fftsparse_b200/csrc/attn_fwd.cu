@@ -9,8 +9,9 @@
 // layout the reference returns (:789-790).
 //
 // One CTA computes one 128-row query tile of one head:
-//   warp 4      TMA producer: Q once, then K and V tiles of every selected
-//               128-column key tile into a two-stage ring (no multicast).
+//   warps 4, 6  TMA producers: Q once and the K tiles (warp 4), the V tiles
+//               (warp 6) of every selected 128-column key tile, each into its
+//               own ring (no multicast).
 //   warp 5      MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
 //               accumulator, O += P V into a TMEM accumulator; completion is
 //               signalled with tcgen05.commit on mbarriers.
@@ -34,7 +35,7 @@ namespace attn {
 constexpr int kBM = 128;       // query rows per tile
 constexpr int kBN = 128;       // key columns per tile
 constexpr int kD = 128;        // head dim
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kThreads = 192;  // 6 warps; two CTAs share an SM
 constexpr int kTileBytes = kBM * kD * 2;     // 32 KB (two 16 KB swizzle boxes)
 constexpr int kHalfBytes = kTileBytes / 2;   // one [128 rows][64 cols] box
 constexpr int kMaxTiles = 4096;              // key tiles per row of tiles
@@ -187,6 +188,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -232,10 +239,11 @@ constexpr uint32_t idesc_bf16(bool b_mn_major) {
 }
 
 // ------------------------------------------------------------------ layout
-constexpr int kKStages = 3;    // K tile ring
-constexpr int kVStages = 2;    // V tile ring
-constexpr int kSBufs = 3;      // S/P accumulators in TMEM (P overwrites its S buffer)
-constexpr int kPolyEvery = 4;  // one exp2 in kPolyEvery on the FMA pipe, the rest on MUFU
+constexpr int kKStages = 1;    // K tile (released by the S MMA)
+constexpr int kVStages = 1;    // V tile (released by the PV MMA)
+constexpr int kSBufs = 1;      // S/P accumulator in TMEM (P overwrites S)
+constexpr int kTmemCols = 256; // S/P 128 + O 128 per CTA: two CTAs fill an SM's 512 columns
+constexpr int kPolyEvery = 0;  // if > 0: one exp2 in kPolyEvery on the FMA pipe, the rest on MUFU
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 
 struct SmemLayout {
@@ -244,7 +252,7 @@ struct SmemLayout {
   static constexpr int k = q + kTileBytes;
   static constexpr int v = k + kKStages * kTileBytes;
   static constexpr int bars = v + kVStages * kTileBytes;
-  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 3;
+  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 2;
   static constexpr int tmem_slot = bars + nbars * 8;
   static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
   static constexpr int list = misc + 16;        // uint16 tile list
@@ -261,12 +269,11 @@ constexpr int BVF = BKE + kKStages;     // V full      [kVStages]
 constexpr int BVE = BVF + kVStages;     // V empty     [kVStages]
 constexpr int BSF = BVE + kVStages;     // S full      [kSBufs]
 constexpr int BPV = BSF + kSBufs;       // PV done with this S/P buffer [kSBufs]
-constexpr int BOF = BPV + kSBufs;       // PV(m) complete (one phase per tile)
-constexpr int BPF = BOF + 1;            // P(m) written to TMEM, O rescaled (128 arrivals)
+constexpr int BPF = BPV + kSBufs;       // P(m) written to TMEM, O rescaled (128 arrivals)
 constexpr int BDRAIN = BPF + 1;
 
-// TMEM columns: S/P buffers at 0, 128, 256; O at 384
-constexpr uint32_t kTmemO = 384;
+// TMEM columns: S/P at 0, O at 128
+constexpr uint32_t kTmemO = 128;
 
 struct Params {
   int B, H, Hkv, L, bs, bs_shift, causal;
@@ -295,7 +302,7 @@ __device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw
   return out;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     sparse_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, Params prm) {
   extern __shared__ uint8_t smem_dyn[];
@@ -338,14 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(BSF + s), 1);
       mbar_init(bar(BPV + s), 1);
     }
-    mbar_init(bar(BOF), 1);
     mbar_init(bar(BPF), 128);
     mbar_init(bar(BDRAIN), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 5) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(512));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (warp == 4 && lane == 0) {
@@ -398,50 +404,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     // ================================================================ TMA producer
+    // Q once, then K(n) (its stage is released by S(n-1)) and V(n) (released by
+    // PV(n-1)); the single-stage rings keep this CTA's shared memory small enough
+    // for two CTAs per SM, whose pipelines interleave on the tensor core.
     if (lane == 0 && ntiles > 0) {
       int issued_k = 0, issued_v = 0;
       bool ok = true;
       mbar_arrive_tx(bar(BQ), kTileBytes);
       tma_load_4d(sbase + SmemLayout::q, &tm_q, bar(BQ), 0, qt * kBM, h, b);
       tma_load_4d(sbase + SmemLayout::q + kHalfBytes, &tm_q, bar(BQ), 64, qt * kBM, h, b);
-      auto load_k = [&](int n) -> bool {
-        const int s = n % kKStages;
-        if (!mbar_wait(bar(BKE + s), ((n / kKStages) & 1) ^ 1, abort_flag)) return false;
-        mbar_arrive_tx(bar(BKF + s), kTileBytes);
-        const uint32_t dst = sbase + SmemLayout::k + s * kTileBytes;
-        const int j = list[n];
-        tma_load_4d(dst, &tm_k, bar(BKF + s), 0, j * kBN, kvh, b);
-        tma_load_4d(dst + kHalfBytes, &tm_k, bar(BKF + s), 64, j * kBN, kvh, b);
-        ++issued_k;
-        return true;
-      };
-      auto load_v = [&](int n) -> bool {
-        const int s = n % kVStages;
-        if (!mbar_wait(bar(BVE + s), ((n / kVStages) & 1) ^ 1, abort_flag)) return false;
-        mbar_arrive_tx(bar(BVF + s), kTileBytes);
-        const uint32_t dst = sbase + SmemLayout::v + s * kTileBytes;
-        const int j = list[n];
-        tma_load_4d(dst, &tm_v, bar(BVF + s), 0, j * kBN, kvh, b);
-        tma_load_4d(dst + kHalfBytes, &tm_v, bar(BVF + s), 64, j * kBN, kvh, b);
-        ++issued_v;
-        return true;
-      };
-      // K runs one tile ahead of V: K(n) is released by S(n-3), V(n-1) by PV(n-3)
       for (int n = 0; n < ntiles && ok; ++n) {
-        ok = load_k(n);
-        if (ok && n >= 1) ok = load_v(n - 1);
+        const int j = list[n];
+        if (!mbar_wait(bar(BKE), (n & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_tx(bar(BKF), kTileBytes);
+        tma_load_4d(sbase + SmemLayout::k, &tm_k, bar(BKF), 0, j * kBN, kvh, b);
+        tma_load_4d(sbase + SmemLayout::k + kHalfBytes, &tm_k, bar(BKF), 64, j * kBN, kvh, b);
+        ++issued_k;
+        if (!mbar_wait(bar(BVE), (n & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_tx(bar(BVF), kTileBytes);
+        tma_load_4d(sbase + SmemLayout::v, &tm_v, bar(BVF), 0, j * kBN, kvh, b);
+        tma_load_4d(sbase + SmemLayout::v + kHalfBytes, &tm_v, bar(BVF), 64, j * kBN, kvh, b);
+        ++issued_v;
       }
-      if (ok) ok = load_v(ntiles - 1);
       if (!ok) {
         *abort_flag = 1;
         atomicCAS(prm.status, 0, kErrTimeoutProducer);
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
         mbar_wait(bar(BQ), 0, &never, kDrainCycles);
-        for (int n = max(0, issued_k - kKStages); n < issued_k; ++n)
-          mbar_wait(bar(BKF + n % kKStages), (n / kKStages) & 1, &never, kDrainCycles);
-        for (int n = max(0, issued_v - kVStages); n < issued_v; ++n)
-          mbar_wait(bar(BVF + n % kVStages), (n / kVStages) & 1, &never, kDrainCycles);
+        if (issued_k > 0) mbar_wait(bar(BKF), (issued_k - 1) & 1, &never, kDrainCycles);
+        if (issued_v > 0) mbar_wait(bar(BVF), (issued_v - 1) & 1, &never, kDrainCycles);
       }
     }
   } else if (warp == 5) {
@@ -451,40 +443,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(bar(BQ), 0, abort_flag);
       fence_after();
       auto issue_pv = [&](int m) -> bool {
-        const int vs = m % kVStages, pb = m % kSBufs;
-        if (!mbar_wait(bar(BVF + vs), (m / kVStages) & 1, abort_flag)) return false;
+        const int vs = 0, pb = 0;
+        if (!mbar_wait(bar(BVF), m & 1, abort_flag)) return false;
         if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t vsm = sbase + SmemLayout::v + vs * kTileBytes;
-        const uint32_t pt = tmem + pb * 128;  // P (bf16 pairs) in the first 64 columns
+        const uint32_t vsm = sbase + SmemLayout::v;
+        const uint32_t pt = tmem + 64;  // P (bf16 pairs) in columns [64, 128) of the S buffer
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t bd = smem_desc(vsm + kk * 2048, kHalfBytes, 1024);
           umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(bar(BOF));
         umma_commit(bar(BVE + vs));
         umma_commit(bar(BPV + pb));
         return true;
       };
-      for (int n = 0; n < ntiles && ok; ++n) {
-        const int ks = n % kKStages, sb = n % kSBufs;
-        ok = mbar_wait(bar(BKF + ks), (n / kKStages) & 1, abort_flag);
-        // buffer sb last held P(n-3): PV(n-3) must have finished reading it
-        if (ok && n >= kSBufs) ok = mbar_wait(bar(BPV + sb), ((n / kSBufs) - 1) & 1, abort_flag);
-        if (!ok) break;
+      auto issue_s = [&](int n) -> bool {
+        if (!mbar_wait(bar(BKF), n & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t ksm = sbase + SmemLayout::k + ks * kTileBytes;
+        const uint32_t ksm = sbase + SmemLayout::k;
         const uint32_t qsm = sbase + SmemLayout::q;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16(tmem + sb * 128, smem_desc(qsm + off, 16, 1024), smem_desc(ksm + off, 16, 1024), idS,
-                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem, smem_desc(qsm + off, 16, 1024), smem_desc(ksm + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar(BSF + sb));
-        umma_commit(bar(BKE + ks));
-        if (n >= 1) ok = issue_pv(n - 1);
+        umma_commit(bar(BSF));
+        umma_commit(bar(BKE));
+        return true;
+      };
+      // S(n) overwrites P(n-1) in TMEM, so PV(n-1) is issued first; tcgen05.mma
+      // operations of one thread execute in issue order.
+      if (ok) ok = issue_s(0);
+      for (int n = 1; n < ntiles && ok; ++n) {
+        ok = issue_pv(n - 1);
+        if (ok) ok = issue_s(n);
       }
       if (ok) ok = issue_pv(ntiles - 1);
       if (!ok) {
@@ -513,20 +506,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n / kSBufs) & 1, abort_flag))) { ok = false; break; }
       fence_after();
       const uint32_t s_addr = tmem + sb * 128 + lane_off;
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s + c * 32);
-      tmem_wait_ld();
-      // masks: causal diagonal, ragged end, sub-block selection (tile-uniform test)
+      // keep-bits of this row's 128 columns, one word per 32 columns (a 32-column
+      // word never straddles a mask block since block_size >= 32); all ones on
+      // interior tiles
       const int col0 = j * kBN;
-      if ((prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1) {
-        // keep-bits of this row's 128 columns, one word per 32 columns (a 32-column
-        // word never straddles a mask block since block_size >= 32)
+      uint32_t kw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      const bool edge = (prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1;
+      if (edge) {
         int lim = min(128, prm.L - col0);
         if (prm.causal && j == qt) lim = min(lim, r + 1);
         uint32_t subm = 0xffffffffu;
         if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
-        uint32_t kw[4];
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const int rem = lim - 32 * w;
@@ -534,13 +524,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!((subm >> ((32 * w) >> prm.bs_shift)) & 1u)) m = 0u;
           kw[w] = m;
         }
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (!((kw[c >> 5] >> (c & 31)) & 1u)) s[c] = -INFINITY;
       }
+      // pass 1: row max over two 64-column halves (64 values live at a time)
+      float x[64];
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      for (int hf = 0; hf < 2; ++hf) {
+        tmem_ld32(s_addr + hf * 64, x);
+        tmem_ld32(s_addr + hf * 64 + 32, x + 32);
+        tmem_wait_ld();
+        if (edge) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (!((kw[2 * hf + (c >> 5)] >> (c & 31)) & 1u)) x[c] = -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) mx4[(c >> 1) & 3] = max3f(mx4[(c >> 1) & 3], x[c], x[c + 1]);
+      }
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       // lazy rescale: keep m_ref unless the row max exceeds it by more than 2^8
       float alpha = 1.0f;
@@ -550,48 +550,75 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = mx;
       }
       const float moff = (m_ref == -INFINITY ? 0.0f : m_ref) * prm.scale_log2;
-      float rs4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      // P overwrites the first 64 columns of its S buffer, 16 columns (32 values) at a time
+      // pass 2: P = exp2(s*scale - m) as bf16 pairs into columns [64, 128) of the
+      // S buffer.  S columns 64..127 are still in registers from pass 1 and are
+      // consumed first, so P only ever overwrites S values already read; S
+      // columns 0..63 are reloaded afterwards.
+      float2 rs2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      const float2 sc2 = make_float2(prm.scale_log2, prm.scale_log2);
+      const float2 off2 = make_float2(-moff, -moff);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t pk[16];
+      for (int hf = 1; hf >= 0; --hf) {
+        if (hf == 0) {
+          tmem_ld32(s_addr, x);
+          tmem_ld32(s_addr + 32, x + 32);
+          tmem_wait_ld();
+          if (edge) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int c = cc * 32 + e;
-          const float a0 = fmaf(s[c], prm.scale_log2, -moff);
-          const float a1 = fmaf(s[c + 1], prm.scale_log2, -moff);
-          const float e0 = fast_exp2(a0);
-          const float e1 = ((c + 1) % kPolyEvery == kPolyEvery - 1) ? poly_exp2(a1) : fast_exp2(a1);
-          rs4[c & 3] += e0;
-          rs4[(c + 1) & 3] += e1;
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(e0, e1);
-          pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
-        }
-        tmem_st16u(s_addr + cc * 16, pk);
-      }
-      l_run = l_run * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
-      tmem_wait_st();
-      if (n >= 1) {
-        // PV(n-1) has accumulated into O: rescale rows whose reference max moved
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(BOF), (n - 1) & 1, abort_flag))) { ok = false; break; }
-        fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            tmem_ld32(tm_o + lane_off + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(tm_o + lane_off + c * 32, o);
+            for (int c = 0; c < 64; ++c)
+              if (!((kw[c >> 5] >> (c & 31)) & 1u)) x[c] = -INFINITY;
           }
-          tmem_wait_st();
         }
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int c = cc * 32 + e;
+            const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
+            float2 ex;
+            ex.x = fast_exp2(a.x);
+            ex.y = (kPolyEvery > 0 && (c + 1) % kPolyEvery == kPolyEvery - 1) ? poly_exp2(a.y) : fast_exp2(a.y);
+            rs2[(e >> 1) & 1] = __fadd2_rn(rs2[(e >> 1) & 1], ex);
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(ex.x, ex.y);
+            pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
+          }
+          tmem_st16u(s_addr + 64 + hf * 32 + cc * 16, pk);
+        }
+      }
+      const float2 rsum = __fadd2_rn(rs2[0], rs2[1]);
+      l_run = l_run * alpha + (rsum.x + rsum.y);
+      tmem_wait_st();
+      if (n >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // O must hold PV(n-1) before it is rescaled.  PV(n-1) committed onto the
+        // barrier of its P buffer; that barrier cannot have moved past this
+        // phase because PV(n+2) needs this thread's P(n+2).
+        const int pb = (n - 1) % kSBufs;
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(BPV + pb), ((n - 1) / kSBufs) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(tm_o + lane_off + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 v = __fmul2_rn(make_float2(o[e], o[e + 1]), make_float2(alpha, alpha));
+            o[e] = v.x;
+            o[e + 1] = v.y;
+          }
+          tmem_st32(tm_o + lane_off + c * 32, o);
+        }
+        tmem_wait_st();
       }
       fence_before();
       mbar_arrive(bar(BPF));
     }
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(BOF), (ntiles - 1) & 1, abort_flag));
+    if (ok && ntiles > 0)
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV + (ntiles - 1) % kSBufs), ((ntiles - 1) / kSBufs) & 1, abort_flag));
     if (!ok) {
       *abort_flag = 1;
       atomicCAS(prm.status, 0, kErrTimeoutSoftmax);
@@ -631,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 5) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  if (warp == 5) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
 }
 
 // ----------------------------------------------------------------- host side
