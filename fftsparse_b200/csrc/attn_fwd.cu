@@ -78,6 +78,21 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or ~0.1 ms pass, instead of spinning and taking issue slots from
+// the softmax warps that share its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(100000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: false on time-out (SM clock cycles) or when another role has
 // aborted the CTA.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
@@ -85,7 +100,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > limit) return false;
   }
@@ -200,20 +215,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for x <= 0 on the FMA pipe: 2^x = 2^floor(x) * 2^f, f in [0, 1), with 2^f
-// from a degree-3 polynomial fitted here to minimise the relative error on
-// [0, 1) (max relative error 7.5e-5, far below bf16's 3.9e-3 for P); the power
-// of two is added to the exponent bits.  Inputs below -126 (including -inf)
-// give exactly 0.
-__device__ __forceinline__ float poly_exp2(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float xi = floorf(xc);
-  const float f = xc - xi;
-  float p = fmaf(0.07802451401948929f, f, 0.2260671705007553f);
-  p = fmaf(p, f, 0.6958335638046265f);
-  p = fmaf(p, f, 0.9999251961708069f);
-  const float r = __int_as_float(__float_as_int(p) + (static_cast<int>(xi) << 23));
-  return x < -126.0f ? 0.0f : r;
+// 2^a for a pair of values on the FMA and ALU pipes only (the MUFU pipe that
+// ex2.approx uses is the softmax's bottleneck at head_dim 128).  Range
+// reduction: a = n + f with n = round-to-nearest(a) read from the low mantissa
+// bits of a + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
+// fitted here to minimise the relative error on [-0.5, 0.5] (max 7.5e-5, far
+// below bf16's 3.9e-3 for P); 2^n is added to the exponent bits.  Inputs below
+// -126 (including -inf) give exactly 0.
+__device__ __forceinline__ float2 poly_exp2x2(float2 a) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float2 ac = make_float2(fmaxf(a.x, -126.0f), fmaxf(a.y, -126.0f));
+  const float2 t = __fadd2_rn(ac, make_float2(kMagic, kMagic));
+  const float2 r = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(r, make_float2(-1.0f, -1.0f), ac);
+  float2 p = __ffma2_rn(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
+                        make_float2(0.2426111251115799f, 0.2426111251115799f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  // (bits(t) << 23) == n << 23 modulo 2^32, since bits(1.5 * 2^23) has 22 trailing zeros
+  const float ex = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  const float ey = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return make_float2(a.x < -126.0f ? 0.0f : ex, a.y < -126.0f ? 0.0f : ey);
 }
 
 // Shared-memory matrix descriptor (tcgen05 "version 1" format).
@@ -243,7 +265,7 @@ constexpr int kKStages = 1;    // K tile (released by the S MMA)
 constexpr int kVStages = 1;    // V tile (released by the PV MMA)
 constexpr int kSBufs = 1;      // S/P accumulator in TMEM (P overwrites S)
 constexpr int kTmemCols = 256; // S/P 128 + O 128 per CTA: two CTAs fill an SM's 512 columns
-constexpr int kPolyEvery = 0;  // if > 0: one exp2 in kPolyEvery on the FMA pipe, the rest on MUFU
+constexpr int kPolyPairEvery = 0;  // if > 0: one column pair in kPolyPairEvery takes the FMA-pipe exp2
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 
 struct SmemLayout {
@@ -577,8 +599,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int c = cc * 32 + e;
             const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
             float2 ex;
-            ex.x = fast_exp2(a.x);
-            ex.y = (kPolyEvery > 0 && (c + 1) % kPolyEvery == kPolyEvery - 1) ? poly_exp2(a.y) : fast_exp2(a.y);
+            if (kPolyPairEvery > 0 && (c >> 1) % kPolyPairEvery == kPolyPairEvery - 1) {
+              ex = poly_exp2x2(a);
+            } else {
+              ex.x = fast_exp2(a.x);
+              ex.y = fast_exp2(a.y);
+            }
             rs2[(e >> 1) & 1] = __fadd2_rn(rs2[(e >> 1) & 1], ex);
             const __nv_bfloat162 pr = __floats2bfloat162_rn(ex.x, ex.y);
             pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
