@@ -266,6 +266,7 @@ constexpr int kVStages = 1;    // V tile (released by the PV MMA)
 constexpr int kSBufs = 1;      // S/P accumulator in TMEM (P overwrites S)
 constexpr int kTmemCols = 256; // S/P 128 + O 128 per CTA: two CTAs fill an SM's 512 columns
 constexpr int kPolyPairEvery = 0;  // if > 0: one column pair in kPolyPairEvery takes the FMA-pipe exp2
+constexpr int kPolyMod = kPolyPairEvery > 0 ? kPolyPairEvery : 1;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 
 struct SmemLayout {
@@ -599,7 +600,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int c = cc * 32 + e;
             const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
             float2 ex;
-            if (kPolyPairEvery > 0 && (c >> 1) % kPolyPairEvery == kPolyPairEvery - 1) {
+            bool use_poly = false;
+            if constexpr (kPolyPairEvery > 0) use_poly = (c >> 1) % kPolyMod == kPolyMod - 1;
+            if (use_poly) {
               ex = poly_exp2x2(a);
             } else {
               ex.x = fast_exp2(a.x);

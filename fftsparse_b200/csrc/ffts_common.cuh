@@ -73,6 +73,26 @@ __device__ inline void load_vec_f32<__nv_bfloat16>(const __nv_bfloat16 *p, float
   }
 }
 
+// Widen a 16-byte word of T to fp32.
+template <typename T>
+__device__ inline void widen_vec(const uint4 &v, float *out);
+
+template <>
+__device__ inline void widen_vec<float>(const uint4 &v, float *out) {
+  out[0] = __uint_as_float(v.x); out[1] = __uint_as_float(v.y);
+  out[2] = __uint_as_float(v.z); out[3] = __uint_as_float(v.w);
+}
+
+template <>
+__device__ inline void widen_vec<__nv_bfloat16>(const uint4 &v, float *out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
 // Monotone 32-bit key of a float: larger value -> larger key; -0 maps to +0.
 __device__ __forceinline__ uint32_t f32_key(float f) {
   if (f == 0.0f) f = 0.0f;

@@ -411,11 +411,57 @@ __device__ double lane_tree(double v, double *part) {
   return r;
 }
 
+// ------------------------------------------------------- stripe statistic
+// One CTA per (sampled lag, b, h): the normalised variance of the adjacent
+// differences along one block-score diagonal (my_attn_v7.py:342-351), written to
+// nv[bh * S + s].  head_stats_kernel averages the S values in sample order.
+template <typename T>
+__global__ void __launch_bounds__(256) diag_stats_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
+                                                         int H, int Hkv, int D, ffts_mask_params p,
+                                                         double *__restrict__ nv) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int N = p.n_blocks;
+  double *part = reinterpret_cast<double *>(smem_raw);  // [256]
+  float *vals = reinterpret_cast<float *>(part + kLanes);  // [N]
+  const int s = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / H, h = bh % H;
+  const T *q = qb + int64_t(bh) * N * D;
+  const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
+  const double sqrtD = sqrt((double)D);
+  const int tau = p.diag_taus[s];
+  const int m = N - tau - 1, n = m - 1;
+  for (int t = threadIdx.x; t < m; t += blockDim.x)
+    vals[t] = __double2float_rn(__ddiv_rn(dot64_rows(q + int64_t(t + tau) * D, k + int64_t(t) * D, D), sqrtD));
+  __syncthreads();
+  double var;
+  if (n >= 2) {
+    double a = 0.0;
+    for (int e = threadIdx.x; e < n; e += blockDim.x) a = __dadd_rn(a, (double)__fsub_rn(vals[e + 1], vals[e]));
+    const double mean = __ddiv_rn(lane_tree(a, part), (double)n);
+    a = 0.0;
+    for (int e = threadIdx.x; e < n; e += blockDim.x) {
+      const double dv = __dsub_rn((double)__fsub_rn(vals[e + 1], vals[e]), mean);
+      a = __dadd_rn(a, __dmul_rn(dv, dv));
+    }
+    var = __ddiv_rn(lane_tree(a, part), (double)(n - 1));
+  } else {
+    var = __longlong_as_double(0x7ff8000000000000ll);
+  }
+  double a = 0.0;
+  for (int e = threadIdx.x; e < m; e += blockDim.x) a = __dadd_rn(a, fabs((double)vals[e]));
+  const double sabs = lane_tree(a, part);
+  double mabs = m > 0 ? __ddiv_rn(sabs, (double)m) : __longlong_as_double(0x7ff8000000000000ll);
+  const double floor6 = (double)1e-6f;
+  if (mabs < floor6) mabs = floor6;
+  if (threadIdx.x == 0) nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s] = __ddiv_rn(var, mabs);
+}
+
 // ------------------------------------------------------------ head stats
 template <typename T>
 __global__ void __launch_bounds__(256) head_stats_kernel(const T *__restrict__ qb,
                                                          const T *__restrict__ kb, int H, int Hkv,
                                                          int D, ffts_mask_params p,
+                                                         const double *__restrict__ nv,
                                                          int32_t *__restrict__ stripe_ws,
                                                          uint8_t *__restrict__ is_stripe_out,
                                                          float *__restrict__ stripe_var_out,
@@ -438,40 +484,12 @@ __global__ void __launch_bounds__(256) head_stats_kernel(const T *__restrict__ q
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
   const double sqrtD = sqrt((double)D);
 
-  // ---- stripe statistic
-  double total = 0.0;
+  // ---- stripe statistic: average of the per-lag values in sample order
   float svar = INFINITY;
   int stripe = 0;
   if (p.corr_on && !p.stripe_all_diffuse) {
-    for (int s = 0; s < p.n_diag_samples; ++s) {
-      const int tau = p.diag_taus[s];
-      const int m = N - tau - 1, n = m - 1;
-      for (int t = threadIdx.x; t < m; t += blockDim.x)
-        vals[t] = __double2float_rn(__ddiv_rn(dot64_rows(q + int64_t(t + tau) * D, k + int64_t(t) * D, D), sqrtD));
-      __syncthreads();
-      double var;
-      if (n >= 2) {
-        double a = 0.0;
-        for (int e = threadIdx.x; e < n; e += blockDim.x)
-          a = __dadd_rn(a, (double)__fsub_rn(vals[e + 1], vals[e]));
-        const double mean = __ddiv_rn(lane_tree(a, part), (double)n);
-        a = 0.0;
-        for (int e = threadIdx.x; e < n; e += blockDim.x) {
-          const double dv = __dsub_rn((double)__fsub_rn(vals[e + 1], vals[e]), mean);
-          a = __dadd_rn(a, __dmul_rn(dv, dv));
-        }
-        var = __ddiv_rn(lane_tree(a, part), (double)(n - 1));
-      } else {
-        var = __longlong_as_double(0x7ff8000000000000ll);
-      }
-      double a = 0.0;
-      for (int e = threadIdx.x; e < m; e += blockDim.x) a = __dadd_rn(a, fabs((double)vals[e]));
-      const double sabs = lane_tree(a, part);
-      double mabs = m > 0 ? __ddiv_rn(sabs, (double)m) : __longlong_as_double(0x7ff8000000000000ll);
-      const double floor6 = (double)1e-6f;
-      if (mabs < floor6) mabs = floor6;
-      total = __dadd_rn(total, __ddiv_rn(var, mabs));
-    }
+    double total = 0.0;
+    for (int s = 0; s < p.n_diag_samples; ++s) total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s]);
     svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
     stripe = svar <= p.stripe_threshold;
   }
@@ -718,6 +736,7 @@ __global__ void unpack_kernel(const uint32_t *__restrict__ bits, int64_t rows, i
 // ------------------------------------------------------------- host side
 struct MaskWorkspace {
   float2 *partial;
+  double *nv;  // [B*H][FFTS_MAX_DIAG_SAMPLES] per-lag stripe statistics
   uint32_t *tausel, *colsel, *lastsel;
   int32_t *stripe;
   int64_t bytes;
@@ -735,6 +754,8 @@ static MaskWorkspace carve(void *ws, int64_t B, int64_t H, int64_t N, int64_t D)
   int64_t off = 0;
   m.partial = reinterpret_cast<float2 *>(p + off);
   off += align256(B * H * nchunk * F * int64_t(sizeof(float2)));
+  m.nv = reinterpret_cast<double *>(p + off);
+  off += align256(B * H * FFTS_MAX_DIAG_SAMPLES * 8);
   m.tausel = reinterpret_cast<uint32_t *>(p + off);
   off += align256(B * H * W * 4);
   m.colsel = reinterpret_cast<uint32_t *>(p + off);
@@ -780,10 +801,17 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
     if (corr) FFTS_CUDA(cudaMemsetAsync(corr, 0, size_t(BH) * N * 4, stream));
     if (csum) FFTS_CUDA(cudaMemsetAsync(csum, 0, size_t(BH) * N * 4, stream));
   }
+  if (p.corr_on && !p.stripe_all_diffuse) {
+    const size_t smemd = size_t(kLanes) * 8 + size_t(N) * 4;
+    FFTS_CUDA(cudaFuncSetAttribute(diag_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smemd)));
+    diag_stats_kernel<T><<<dim3(unsigned(p.n_diag_samples), BH), 256, smemd, stream>>>(qb, kb, int(H), int(Hkv),
+                                                                                       int(D), p, ws.nv);
+    FFTS_CUDA(cudaGetLastError());
+  }
   const size_t smem3 = size_t(kLanes) * 8 + size_t(32) * D * 8 + size_t(N) * 8 + size_t(W) * 4;
   FFTS_CUDA(cudaFuncSetAttribute(head_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3)));
-  head_stats_kernel<T><<<BH, 256, smem3, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, ws.stripe, is_stripe, svar,
-                                                   ws.colsel, ws.lastsel);
+  head_stats_kernel<T><<<BH, 256, smem3, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, ws.nv, ws.stripe, is_stripe,
+                                                   svar, ws.colsel, ws.lastsel);
   FFTS_CUDA(cudaGetLastError());
   const int R = N <= 1024 ? 16 : max(1, 16384 / N);
   const size_t smem4 = size_t(R) * D * 8 + size_t(R) * N * 4 + size_t(R) * W * 4 + 8 * 256 * 4 + size_t(R) * 4;

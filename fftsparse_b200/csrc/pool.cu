@@ -5,14 +5,13 @@
 // (:528-530) and pools those; this kernel reads [B, H, L, D] in place with any
 // (b, h, l) strides, so the copies disappear.
 //
-// One CTA of 256 threads pools one (b, h, block).  With G = D / VEC 16-byte
-// lanes (VEC = 8 bf16 or 4 fp32 channels) and P = 256 / G row phases, thread
-// (p, g) sums rows p, p+P, ... of channels [g*VEC, g*VEC+VEC) in fp32 in row
-// order (padded rows contribute +0), the P partials are combined by the tree
-// part[p] += part[p+s] for s = P/2 .. 1, and the total is divided by
-// block_size and rounded to the input dtype.  This order is the canonical one
-// the CPU oracle restates.  A warp reads two or four whole rows per 16-byte
-// load instruction, so every access is a fully used 512-byte transaction.
+// A CTA of 256 threads pools 256/G blocks of one (b, h), where G = D / VEC
+// 16-byte lanes span a row (VEC = 8 bf16 or 4 fp32 channels).  Thread (s, g)
+// sums rows 0 .. block_size-1 of block s in its VEC channels in fp32, in row
+// order (rows past L contribute +0), then divides by block_size and rounds to
+// the input dtype: the canonical order the CPU oracle restates.  No shared
+// memory and no barriers; sixteen 16-byte loads per thread are in flight at a
+// time, and a warp's load instruction reads whole 256-byte rows.
 
 #include "ffts_common.cuh"
 
@@ -23,64 +22,40 @@ __global__ void __launch_bounds__(256) pool_kernel(const T *__restrict__ x, int6
                                                    int D, int64_t sb, int64_t sh, int64_t sl,
                                                    int bs, int64_t N, T *__restrict__ out) {
   constexpr int VEC = Elem<T>::kVec;
-  extern __shared__ float part[];  // [P][D]
+  constexpr int U = 16;  // loads in flight per thread
   const int G = D / VEC;
-  const int P = 256 / G;
-  const int tid = threadIdx.x;
-  const int g = tid % G;
-  const int p = tid / G;
-  const int64_t n = blockIdx.x;
+  const int per_cta = 256 / G;
+  const int g = threadIdx.x % G;
+  const int64_t n = int64_t(blockIdx.x) * per_cta + threadIdx.x / G;
   const int64_t bh = blockIdx.y;
+  if (n >= N) return;
   const int64_t b = bh / H, h = bh % H;
   const T *base = x + b * sb + h * sh + int64_t(g) * VEC;
-
   float acc[VEC];
 #pragma unroll
   for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-
-  // Rows in groups of 8 so that eight independent 16-byte loads are in flight.
-  for (int r0 = p; r0 < bs; r0 += 8 * P) {
-    float v[8][VEC];
+  for (int r0 = 0; r0 < bs; r0 += U) {
+    uint4 raw[U];  // the 16-byte words of U rows, widened during the in-order adds
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int r = r0 + u * P;
-      const int64_t t = n * bs + r;
-      if (r < bs && t < L) {
-        load_vec_f32<T>(base + t * sl, v[u]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) v[u][e] = 0.0f;
-      }
+    for (int u = 0; u < U; ++u) {
+      const int64_t t = n * bs + r0 + u;
+      raw[u] = (r0 + u < bs && t < L) ? *reinterpret_cast<const uint4 *>(base + t * sl) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      if (r0 + u * P < bs) {
+    for (int u = 0; u < U; ++u) {
+      if (r0 + u < bs) {
+        float v[VEC];
+        widen_vec<T>(raw[u], v);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) acc[e] = __fadd_rn(acc[e], v[u][e]);
+        for (int e = 0; e < VEC; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
       }
     }
   }
+  T res[VEC];
 #pragma unroll
-  for (int e = 0; e < VEC; ++e) part[p * D + g * VEC + e] = acc[e];
-  __syncthreads();
-  for (int s = P / 2; s >= 1; s >>= 1) {
-    if (p < s) {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int i = g * VEC + e;
-        part[p * D + i] = __fadd_rn(part[p * D + i], part[(p + s) * D + i]);
-      }
-    }
-    __syncthreads();
-  }
-  if (p == 0) {
-    T res[VEC];
-#pragma unroll
-    for (int e = 0; e < VEC; ++e)
-      res[e] = Elem<T>::from_f32(__fdiv_rn(part[g * VEC + e], (float)bs));
-    T *o = out + (bh * N + n) * D + g * VEC;
-    *reinterpret_cast<uint4 *>(o) = *reinterpret_cast<const uint4 *>(res);
-  }
+  for (int e = 0; e < VEC; ++e) res[e] = Elem<T>::from_f32(__fdiv_rn(acc[e], (float)bs));
+  T *o = out + (bh * N + n) * D + g * VEC;
+  *reinterpret_cast<uint4 *>(o) = *reinterpret_cast<const uint4 *>(res);
 }
 
 int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D,
@@ -97,15 +72,14 @@ int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64
                "pool: pointers must be 16-byte aligned");
   FFTS_REQUIRE(B * H <= 65535, "pool: B*H too large");
   const int64_t N = ceil_div(L, bs);
-  const int G = int(D / vec), P = 256 / G;
-  const size_t smem = size_t(P) * D * sizeof(float);
-  dim3 grid(unsigned(N), unsigned(B * H));
+  const int G = int(D / vec), per_cta = 256 / G;
+  dim3 grid(unsigned(ceil_div(N, per_cta)), unsigned(B * H));
   if (dtype == FFTS_DTYPE_BF16)
-    pool_kernel<__nv_bfloat16><<<grid, 256, smem, stream>>>(
+    pool_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         static_cast<const __nv_bfloat16 *>(x), H, L, int(D), sb, sh, sl, bs, N,
         static_cast<__nv_bfloat16 *>(out));
   else
-    pool_kernel<float><<<grid, 256, smem, stream>>>(static_cast<const float *>(x), H, L, int(D), sb,
+    pool_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float *>(x), H, L, int(D), sb,
                                                     sh, sl, bs, N, static_cast<float *>(out));
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;

@@ -10,8 +10,8 @@
  * "canonical" arithmetic), so that the GPU kernels and this file produce
  * bit-identical block masks:
  *
- *   pooling      fp32 sums in a fixed 256-lane tree, / block_size, rounded
- *                to the input dtype                        (ref :105-114)
+ *   pooling      fp32 sums in row order, / block_size, rounded to the
+ *                input dtype                               (ref :105-114)
  *   lag corr.    zero-padded radix-2 DIT FFT in fp32 of z = q + i k per
  *                channel, cross spectrum summed over channels, one inverse
  *                FFT, then the reference's fp32 post-processing  (ref :117-157)
@@ -72,41 +72,28 @@ static inline uint32_t f32_key(float f) {
 
 /* ---------------------------------------------------------------- pooling */
 
-/* Canonical block mean: G = D/VEC lanes own VEC channels each, P = 256/G
- * row phases; phase p sums rows p, p+P, ... in order (fp32, from +0), the P
- * partials are combined by the tree part[p] += part[p+s], s = P/2 .. 1, and
- * the total is divided by block_size in fp32 and rounded to the dtype. */
+/* Canonical block mean: each channel's block_size values are summed in fp32 in
+ * row order starting from +0 (rows past L contribute +0), the sum is divided
+ * by block_size in fp32 and rounded to the dtype. */
 int ffo_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D,
              int64_t sb, int64_t sh, int64_t sl, int bs, void *out) {
-  const int vec = dtype == FFTS_DTYPE_BF16 ? 8 : 4;
-  if (D % vec) return -1;
-  const int64_t G = D / vec;
-  if (G <= 0 || 256 % G) return -1;
-  const int P = (int)(256 / G);
   const int64_t N = (L + bs - 1) / bs;
 #pragma omp parallel for collapse(2) schedule(static)
   for (int64_t bh = 0; bh < B * H; ++bh) {
     for (int64_t n = 0; n < N; ++n) {
       const int64_t b = bh / H, h = bh % H;
-      float part[256];
       for (int64_t d = 0; d < D; ++d) {
-        for (int p = 0; p < P; ++p) {
-          float acc = 0.0f;
-          for (int r = p; r < bs; r += P) {
-            const int64_t t = n * bs + r;
-            float v = 0.0f;
-            if (t < L) {
-              const int64_t off = b * sb + h * sh + t * sl + d;
-              v = dtype == FFTS_DTYPE_BF16 ? bf16_to_f32(((const uint16_t *)x)[off])
-                                           : ((const float *)x)[off];
-            }
-            acc = acc + v;
+        float acc = 0.0f;
+        for (int r = 0; r < bs; ++r) {
+          const int64_t t = n * bs + r;
+          float v = 0.0f;
+          if (t < L) {
+            const int64_t off = b * sb + h * sh + t * sl + d;
+            v = dtype == FFTS_DTYPE_BF16 ? bf16_to_f32(((const uint16_t *)x)[off]) : ((const float *)x)[off];
           }
-          part[p] = acc;
+          acc = acc + v;
         }
-        for (int s = P / 2; s >= 1; s /= 2)
-          for (int p = 0; p < s; ++p) part[p] = part[p] + part[p + s];
-        const float mean = part[0] / (float)bs;
+        const float mean = acc / (float)bs;
         const int64_t o = ((b * H + h) * N + n) * D + d;
         if (dtype == FFTS_DTYPE_BF16)
           ((uint16_t *)out)[o] = f32_to_bf16_rne(mean);
