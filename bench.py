@@ -92,7 +92,7 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -239,14 +239,13 @@ def run_ours(args):
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize(dev)
-    barrier()
-
     stream = torch.cuda.current_stream(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # clocks are sampled from the first warm-up step to the end of the timed loop
     with ClockSampler(local_rank) as clocks:
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize(dev)
         barrier()
         torch.cuda.synchronize(dev)
         start.record(stream)
@@ -260,6 +259,26 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
+
+    # ---- the same layer with un-expanded GQA k/v (8 KV heads): identical outputs,
+    # the 4 q-heads of a group then share K/V tiles in L2
+    k8 = k[:, ::HQ // HKV].contiguous()
+    v8 = v[:, ::HQ // HKV].contiguous()
+    for _ in range(2):
+        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, **kw)
+    torch.cuda.synchronize(dev)
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(args.steps):
+        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, **kw)
+    g1.record(stream)
+    torch.cuda.synchronize(dev)
+    tg = torch.tensor([g0.elapsed_time(g1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+    gqa_native_ms = float(tg.item())
+    del k8, v8
 
     # ---- per-stage timing and the attention kernel's roofline (rank-local shard)
     shard = kv_group_shard(HQ, HKV, world, rank)
@@ -387,6 +406,7 @@ def run_ours(args):
             "roofline": roofline,
             "cpu_baseline": cpu,
             "stages": stages,
+            "gqa_native_ms_per_layer": round(gqa_native_ms, 4),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
