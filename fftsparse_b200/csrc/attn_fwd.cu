@@ -8,18 +8,20 @@
 // [L, H, D] first, :528-530) and writes the output directly in the [B, L, H, D]
 // layout the reference returns (:789-790).
 //
-// One CTA computes one 128-row query tile of one head:
-//   warps 4, 6  TMA producers: Q once and the K tiles (warp 4), the V tiles
-//               (warp 6) of every selected 128-column key tile, each into its
-//               own ring (no multicast).
+// One CTA computes one 128-row query tile of one head, walking the selected
+// key columns in 64-key tiles; two CTAs share an SM (256 TMEM columns and
+// ~106 KB of shared memory each), so their pipelines interleave on the SM's
+// tensor core:
+//   warp 4      TMA producer: Q once, then the K and V tiles of every selected
+//               tile into two-stage rings (no multicast).
 //   warp 5      MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
-//               accumulator, O += P V into a TMEM accumulator; completion is
-//               signalled with tcgen05.commit on mbarriers.
-//   warps 0-3   softmax: thread r owns query row r (TMEM lane r); reads S with
-//               tcgen05.ld, applies the causal / ragged / sub-block masks, keeps
-//               the running max and sum, rescales O in TMEM when the max moves,
-//               writes P (bf16, 128B-swizzled K-major) to shared memory for the
-//               PV MMA, and finally normalises O and stores it.
+//               accumulator (2 x 64 columns), O += P V with P read from TMEM;
+//               completion is signalled with tcgen05.commit on mbarriers.
+//   warps 0-3   softmax: thread r owns query row r (TMEM lane r); reads S(n)
+//               while the tensor core computes S(n+1), applies the causal /
+//               ragged / block masks, keeps the running max (rescaling O in
+//               TMEM only when it grows by more than 2^8) and sum, and writes P
+//               as bf16 pairs over its S buffer; finally normalises O and stores.
 // Unselected key tiles are never loaded.  Every mbarrier wait is bounded: on a
 // time-out the CTA records an error status, stops issuing work, waits (bounded)
 // for its own TMA copies and MMAs in flight, frees TMEM and exits.
@@ -32,13 +34,15 @@
 namespace ffts {
 namespace attn {
 
-constexpr int kBM = 128;       // query rows per tile
-constexpr int kBN = 128;       // key columns per tile
+constexpr int kBM = 128;       // query rows per CTA
+constexpr int kBN = 64;        // key columns per tile
 constexpr int kD = 128;        // head dim
 constexpr int kThreads = 192;  // 6 warps; two CTAs share an SM
-constexpr int kTileBytes = kBM * kD * 2;     // 32 KB (two 16 KB swizzle boxes)
-constexpr int kHalfBytes = kTileBytes / 2;   // one [128 rows][64 cols] box
-constexpr int kMaxTiles = 4096;              // key tiles per row of tiles
+constexpr int kQBytes = kBM * kD * 2;        // 32 KB: two [128 rows][64 cols] swizzle boxes
+constexpr int kQHalf = kQBytes / 2;
+constexpr int kKVBytes = kBN * kD * 2;       // 16 KB: two [64 rows][64 cols] swizzle boxes
+constexpr int kKVHalf = kKVBytes / 2;
+constexpr int kMaxTiles = 4096;              // 64-key tiles per query tile (L <= 262144)
 constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 1.965 GHz: bound on one wait
 constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own copies / MMAs
 
@@ -250,21 +254,22 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return d;
 }
 
-// Instruction descriptor: kind::f16, bf16 x bf16 -> fp32, M = 128, N = 128.
-constexpr uint32_t idesc_bf16(bool b_mn_major) {
+// Instruction descriptor: kind::f16, bf16 x bf16 -> fp32, M = 128, N = n.
+constexpr uint32_t idesc_bf16(bool b_mn_major, int n) {
   return (1u << 4)                        // D format: f32
          | (1u << 7)                      // A format: bf16
          | (1u << 10)                     // B format: bf16
          | (b_mn_major ? (1u << 16) : 0u) // B major-ness
-         | (uint32_t(kBN >> 3) << 17)     // N
+         | (uint32_t(n >> 3) << 17)       // N
          | (uint32_t(kBM >> 4) << 24);    // M
 }
 
 // ------------------------------------------------------------------ layout
-constexpr int kKStages = 1;    // K tile (released by the S MMA)
-constexpr int kVStages = 1;    // V tile (released by the PV MMA)
-constexpr int kSBufs = 1;      // S/P accumulator in TMEM (P overwrites S)
-constexpr int kTmemCols = 256; // S/P 128 + O 128 per CTA: two CTAs fill an SM's 512 columns
+// ------------------------------------------------------------------ layout
+constexpr int kKStages = 2;     // K tile ring (a stage is released by the S MMA that read it)
+constexpr int kVStages = 2;     // V tile ring (released by the PV MMA)
+constexpr int kTmemCols = 256;  // S0, S1 (64 columns each) + O (128): two CTAs fill an SM's 512
+constexpr uint32_t kTmemO = 128;
 constexpr int kPolyPairEvery = 0;  // if > 0: one column pair in kPolyPairEvery takes the FMA-pipe exp2
 constexpr int kPolyMod = kPolyPairEvery > 0 ? kPolyPairEvery : 1;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
@@ -272,17 +277,17 @@ constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows b
 struct SmemLayout {
   // offsets from the 1024-byte aligned base
   static constexpr int q = 0;
-  static constexpr int k = q + kTileBytes;
-  static constexpr int v = k + kKStages * kTileBytes;
-  static constexpr int bars = v + kVStages * kTileBytes;
-  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 * kSBufs + 2;
+  static constexpr int k = q + kQBytes;
+  static constexpr int v = k + kKStages * kKVBytes;
+  static constexpr int bars = v + kVStages * kKVBytes;
+  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 + 3;
   static constexpr int tmem_slot = bars + nbars * 8;
   static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
   static constexpr int list = misc + 16;        // uint16 tile list
   static constexpr int end = list + kMaxTiles * 2;
   static constexpr int bytes = end + 1024;      // + alignment slack
 };
-static_assert(SmemLayout::bytes <= 227 * 1024, "shared memory budget");
+static_assert(2 * (SmemLayout::bytes + 1024) <= 228 * 1024, "two CTAs must fit in an SM's shared memory");
 
 // barrier indices
 constexpr int BQ = 0;
@@ -290,17 +295,14 @@ constexpr int BKF = 1;                  // K full      [kKStages]
 constexpr int BKE = BKF + kKStages;     // K empty     [kKStages]
 constexpr int BVF = BKE + kKStages;     // V full      [kVStages]
 constexpr int BVE = BVF + kVStages;     // V empty     [kVStages]
-constexpr int BSF = BVE + kVStages;     // S full      [kSBufs]
-constexpr int BPV = BSF + kSBufs;       // PV done with this S/P buffer [kSBufs]
-constexpr int BPF = BPV + kSBufs;       // P(m) written to TMEM, O rescaled (128 arrivals)
+constexpr int BSF = BVE + kVStages;     // S(n) in TMEM buffer n % 2 [2]
+constexpr int BPV = BSF + 2;            // PV(n) complete (one phase per tile)
+constexpr int BPF = BPV + 1;            // P(n) in TMEM, O rescaled (128 arrivals)
 constexpr int BDRAIN = BPF + 1;
-
-// TMEM columns: S/P at 0, O at 128
-constexpr uint32_t kTmemO = 128;
 
 struct Params {
   int B, H, Hkv, L, bs, bs_shift, causal;
-  int nq;         // query tiles per head
+  int nq;         // query tiles (128 rows) per head
   int nblk;       // mask blocks per row (N)
   int W;          // mask words per row
   const uint32_t *bits;
@@ -310,17 +312,19 @@ struct Params {
   int *status;
 };
 
-// Tile bits of 32 consecutive key tiles [32*tw, 32*tw+32) for mask row `row`
-// when each 128-wide tile covers `sub` mask blocks.
-__device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw, int sub) {
-  if (sub == 1) return tw < W ? row[tw] : 0u;
+// Bits of 32 consecutive 64-key tiles [32*tw, 32*tw+32) of one mask row: a
+// tile is kept if any mask block it overlaps is kept.
+__device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw, int bs) {
   uint32_t out = 0;
   for (int t = 0; t < 32; ++t) {
-    const int blk0 = (tw * 32 + t) * sub;
-    const int w = blk0 >> 5;
-    if (w >= W) break;
-    const uint32_t grp = (row[w] >> (blk0 & 31)) & ((1u << sub) - 1u);
-    out |= uint32_t(grp != 0) << t;
+    const int c0 = (tw * 32 + t) * kBN;            // first key of the tile
+    const int b0 = c0 / bs, b1 = (c0 + kBN - 1) / bs;
+    bool on = false;
+    for (int blk = b0; blk <= b1; ++blk) {
+      if ((blk >> 5) >= W) break;
+      on |= (row[blk >> 5] >> (blk & 31)) & 1u;
+    }
+    out |= uint32_t(on) << t;
   }
   return out;
 }
@@ -350,7 +354,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kvh = x % prm.Hkv;
   const int b = x / prm.Hkv;
   const int h = kvh * G + hg;
-  const int sub = kBM / prm.bs;  // mask blocks per tile edge
+  const int rows_per_blk = prm.bs;                 // query rows per mask row
+  const int mrows = (kBM + prm.bs - 1) / prm.bs;   // mask rows covered by this query tile
 
   // ---- setup: barriers, TMEM, tile list
   if (threadIdx.x == 0) {
@@ -364,10 +369,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar(BVF + s), 1);
       mbar_init(bar(BVE + s), 1);
     }
-    for (int s = 0; s < kSBufs; ++s) {
-      mbar_init(bar(BSF + s), 1);
-      mbar_init(bar(BPV + s), 1);
-    }
+    mbar_init(bar(BSF), 1);
+    mbar_init(bar(BSF + 1), 1);
+    mbar_init(bar(BPV), 1);
     mbar_init(bar(BPF), 128);
     mbar_init(bar(BDRAIN), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -382,9 +386,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     prefetch_map(&tm_k);
     prefetch_map(&tm_v);
   }
-  // Key tiles to visit: OR of the sub x sub mask blocks of each tile, causal cut.
+  // 64-key tiles to visit: OR over the mask rows of this query tile, causal cut.
   const int nkv_all = (prm.L + kBN - 1) / kBN;
-  const int nkv = prm.causal ? min(qt + 1, nkv_all) : nkv_all;
+  const int nkv = prm.causal ? min((qt + 1) * (kBM / kBN), nkv_all) : nkv_all;
   const int TW = (nkv + 31) / 32;
   if (warp == 0) {
     int base = 0;
@@ -392,11 +396,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int tw = c + lane;
       uint32_t word = 0;
       if (tw < TW) {
-        for (int s = 0; s < sub; ++s) {
-          const int mrow = qt * sub + s;
+        for (int s = 0; s < mrows; ++s) {
+          const int mrow = qt * mrows + s;
           if (mrow < prm.nblk) {
             const uint32_t *row = prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + mrow) * prm.W;
-            word |= tile_word(row, prm.W, tw, sub);
+            word |= tile_word(row, prm.W, tw, prm.bs);
           }
         }
         const int lim = nkv - tw * 32;  // tiles valid in this word
@@ -427,27 +431,31 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 4) {
     // ================================================================ TMA producer
-    // Q once, then K(n) (its stage is released by S(n-1)) and V(n) (released by
-    // PV(n-1)); the single-stage rings keep this CTA's shared memory small enough
-    // for two CTAs per SM, whose pipelines interleave on the tensor core.
+    // Q once; K(n+1) runs one tile ahead of V(n).  K(n) reuses the stage of
+    // K(n-2), released by S(n-2); V(n) the stage of V(n-2), released by PV(n-2).
     if (lane == 0 && ntiles > 0) {
       int issued_k = 0, issued_v = 0;
       bool ok = true;
-      mbar_arrive_tx(bar(BQ), kTileBytes);
+      mbar_arrive_tx(bar(BQ), kQBytes);
       tma_load_4d(sbase + SmemLayout::q, &tm_q, bar(BQ), 0, qt * kBM, h, b);
-      tma_load_4d(sbase + SmemLayout::q + kHalfBytes, &tm_q, bar(BQ), 64, qt * kBM, h, b);
-      for (int n = 0; n < ntiles && ok; ++n) {
+      tma_load_4d(sbase + SmemLayout::q + kQHalf, &tm_q, bar(BQ), 64, qt * kBM, h, b);
+      auto load = [&](int n, bool is_k) -> bool {
+        const int s = n % 2;
+        const int full = (is_k ? BKF : BVF) + s, empty = (is_k ? BKE : BVE) + s;
+        if (!mbar_wait(bar(empty), ((n >> 1) & 1) ^ 1, abort_flag)) return false;
+        mbar_arrive_tx(bar(full), kKVBytes);
+        const uint32_t dst = sbase + (is_k ? SmemLayout::k : SmemLayout::v) + s * kKVBytes;
+        const CUtensorMap *map = is_k ? &tm_k : &tm_v;
         const int j = list[n];
-        if (!mbar_wait(bar(BKE), (n & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_tx(bar(BKF), kTileBytes);
-        tma_load_4d(sbase + SmemLayout::k, &tm_k, bar(BKF), 0, j * kBN, kvh, b);
-        tma_load_4d(sbase + SmemLayout::k + kHalfBytes, &tm_k, bar(BKF), 64, j * kBN, kvh, b);
-        ++issued_k;
-        if (!mbar_wait(bar(BVE), (n & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_tx(bar(BVF), kTileBytes);
-        tma_load_4d(sbase + SmemLayout::v, &tm_v, bar(BVF), 0, j * kBN, kvh, b);
-        tma_load_4d(sbase + SmemLayout::v + kHalfBytes, &tm_v, bar(BVF), 64, j * kBN, kvh, b);
-        ++issued_v;
+        tma_load_4d(dst, map, bar(full), 0, j * kBN, kvh, b);
+        tma_load_4d(dst + kKVHalf, map, bar(full), 64, j * kBN, kvh, b);
+        if (is_k) ++issued_k; else ++issued_v;
+        return true;
+      };
+      ok = load(0, true);
+      for (int n = 0; n < ntiles && ok; ++n) {
+        if (n + 1 < ntiles) ok = load(n + 1, true);
+        if (ok) ok = load(n, false);
       }
       if (!ok) {
         *abort_flag = 1;
@@ -455,54 +463,60 @@ __global__ void __launch_bounds__(kThreads, 2)
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
         mbar_wait(bar(BQ), 0, &never, kDrainCycles);
-        if (issued_k > 0) mbar_wait(bar(BKF), (issued_k - 1) & 1, &never, kDrainCycles);
-        if (issued_v > 0) mbar_wait(bar(BVF), (issued_v - 1) & 1, &never, kDrainCycles);
+        for (int n = max(0, issued_k - 2); n < issued_k; ++n)
+          mbar_wait(bar(BKF + n % 2), (n >> 1) & 1, &never, kDrainCycles);
+        for (int n = max(0, issued_v - 2); n < issued_v; ++n)
+          mbar_wait(bar(BVF + n % 2), (n >> 1) & 1, &never, kDrainCycles);
       }
     }
   } else if (warp == 5) {
     // ================================================================ MMA issuer
+    // S(0), S(1), then per tile n: PV(n) (after P(n)), S(n+2).  S(n+2) overwrites
+    // the TMEM buffer that held P(n); tcgen05.mma operations of one thread
+    // execute in issue order, so PV(n) has read P(n) by then.
     if (lane == 0 && ntiles > 0) {
-      const uint32_t idS = idesc_bf16(false), idPV = idesc_bf16(true);
+      const uint32_t idS = idesc_bf16(false, kBN), idPV = idesc_bf16(true, kD);
       bool ok = mbar_wait(bar(BQ), 0, abort_flag);
       fence_after();
-      auto issue_pv = [&](int m) -> bool {
-        const int vs = 0, pb = 0;
-        if (!mbar_wait(bar(BVF), m & 1, abort_flag)) return false;
-        if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
-        fence_after();
-        const uint32_t vsm = sbase + SmemLayout::v;
-        const uint32_t pt = tmem + 64;  // P (bf16 pairs) in columns [64, 128) of the S buffer
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bd = smem_desc(vsm + kk * 2048, kHalfBytes, 1024);
-          umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(BVE + vs));
-        umma_commit(bar(BPV + pb));
-        return true;
-      };
       auto issue_s = [&](int n) -> bool {
-        if (!mbar_wait(bar(BKF), n & 1, abort_flag)) return false;
+        const int s = n % 2;
+        if (!mbar_wait(bar(BKF + s), (n >> 1) & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t ksm = sbase + SmemLayout::k;
+        const uint32_t ksm = sbase + SmemLayout::k + s * kKVBytes;
         const uint32_t qsm = sbase + SmemLayout::q;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          umma_f16(tmem, smem_desc(qsm + off, 16, 1024), smem_desc(ksm + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+          const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+          umma_f16(tmem + s * kBN, smem_desc(qsm + qoff, 16, 1024), smem_desc(ksm + koff, 16, 1024), idS,
+                   kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar(BSF));
-        umma_commit(bar(BKE));
+        umma_commit(bar(BSF + s));
+        umma_commit(bar(BKE + s));
         return true;
       };
-      // S(n) overwrites P(n-1) in TMEM, so PV(n-1) is issued first; tcgen05.mma
-      // operations of one thread execute in issue order.
+      auto issue_pv = [&](int m) -> bool {
+        const int s = m % 2;
+        if (!mbar_wait(bar(BVF + s), (m >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
+        fence_after();
+        const uint32_t vsm = sbase + SmemLayout::v + s * kKVBytes;
+        const uint32_t pt = tmem + s * kBN;  // P(m): bf16 pairs in the first 32 columns of S buffer m % 2
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = smem_desc(vsm + kk * 2048, kKVHalf, 1024);
+          umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(BVE + s));
+        umma_commit(bar(BPV));
+        return true;
+      };
       if (ok) ok = issue_s(0);
-      for (int n = 1; n < ntiles && ok; ++n) {
-        ok = issue_pv(n - 1);
-        if (ok) ok = issue_s(n);
+      if (ok && ntiles > 1) ok = issue_s(1);
+      for (int n = 0; n < ntiles && ok; ++n) {
+        ok = issue_pv(n);
+        if (ok && n + 2 < ntiles) ok = issue_s(n + 2);
       }
-      if (ok) ok = issue_pv(ntiles - 1);
       if (!ok) {
         *abort_flag = 1;
         atomicCAS(prm.status, 0, kErrTimeoutMma);
@@ -520,50 +534,43 @@ __global__ void __launch_bounds__(kThreads, 2)
     // m_ref: the max the current P and O are scaled to (lags the true max by < 2^8)
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    const int mrow = qt * sub + r / prm.bs;
-    const uint32_t *rowbits =
-        prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + min(mrow, prm.nblk - 1)) * prm.W;
+    const int mrow = min(qt * mrows + r / rows_per_blk, prm.nblk - 1);
+    const uint32_t *rowbits = prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + mrow) * prm.W;
+    const float2 sc2 = make_float2(prm.scale_log2, prm.scale_log2);
     for (int n = 0; n < ntiles; ++n) {
-      const int sb = n % kSBufs;
+      const int sb = n % 2;
       const int j = list[n];
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n / kSBufs) & 1, abort_flag))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
       fence_after();
-      const uint32_t s_addr = tmem + sb * 128 + lane_off;
-      // keep-bits of this row's 128 columns, one word per 32 columns (a 32-column
-      // word never straddles a mask block since block_size >= 32); all ones on
-      // interior tiles
+      const uint32_t s_addr = tmem + sb * kBN + lane_off;
+      float x[kBN];
+      tmem_ld32(s_addr, x);
+      tmem_ld32(s_addr + 32, x + 32);
+      tmem_wait_ld();
+      // masks: causal diagonal, ragged end, and (block_size < 128) this row's own
+      // mask row; whole 32-column words since block_size >= 32
       const int col0 = j * kBN;
-      uint32_t kw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-      const bool edge = (prm.causal && j == qt) || (col0 + kBN > prm.L) || sub > 1;
-      if (edge) {
-        int lim = min(128, prm.L - col0);
-        if (prm.causal && j == qt) lim = min(lim, r + 1);
-        uint32_t subm = 0xffffffffu;
-        if (sub > 1) subm = (rowbits[(j * sub) >> 5] >> ((j * sub) & 31)) & ((1u << sub) - 1u);
+      if ((prm.causal && col0 + kBN - 1 > qt * kBM) || col0 + kBN > prm.L || prm.bs < kBM) {
+        int lim = min(kBN, prm.L - col0);
+        if (prm.causal) lim = min(lim, row_g - col0 + 1);
+        uint32_t kw[2];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
+        for (int w = 0; w < 2; ++w) {
           const int rem = lim - 32 * w;
           uint32_t m = rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : ((1u << rem) - 1u));
-          if (!((subm >> ((32 * w) >> prm.bs_shift)) & 1u)) m = 0u;
+          if (prm.bs < kBM) {
+            const int blk = (col0 + 32 * w) >> prm.bs_shift;
+            if (!((rowbits[blk >> 5] >> (blk & 31)) & 1u)) m = 0u;
+          }
           kw[w] = m;
         }
+#pragma unroll
+        for (int c = 0; c < kBN; ++c)
+          if (!((kw[c >> 5] >> (c & 31)) & 1u)) x[c] = -INFINITY;
       }
-      // pass 1: row max over two 64-column halves (64 values live at a time)
-      float x[64];
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        tmem_ld32(s_addr + hf * 64, x);
-        tmem_ld32(s_addr + hf * 64 + 32, x + 32);
-        tmem_wait_ld();
-        if (edge) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (!((kw[2 * hf + (c >> 5)] >> (c & 31)) & 1u)) x[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) mx4[(c >> 1) & 3] = max3f(mx4[(c >> 1) & 3], x[c], x[c + 1]);
-      }
+      for (int c = 0; c < kBN; c += 2) mx4[(c >> 1) & 3] = max3f(mx4[(c >> 1) & 3], x[c], x[c + 1]);
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       // lazy rescale: keep m_ref unless the row max exceeds it by more than 2^8
       float alpha = 1.0f;
@@ -573,57 +580,39 @@ __global__ void __launch_bounds__(kThreads, 2)
         m_ref = mx;
       }
       const float moff = (m_ref == -INFINITY ? 0.0f : m_ref) * prm.scale_log2;
-      // pass 2: P = exp2(s*scale - m) as bf16 pairs into columns [64, 128) of the
-      // S buffer.  S columns 64..127 are still in registers from pass 1 and are
-      // consumed first, so P only ever overwrites S values already read; S
-      // columns 0..63 are reloaded afterwards.
-      float2 rs2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-      const float2 sc2 = make_float2(prm.scale_log2, prm.scale_log2);
       const float2 off2 = make_float2(-moff, -moff);
+      // P = exp2(s*scale - m) as bf16 pairs into the first 32 columns of this S
+      // buffer (S has been read in full)
+      float2 rs2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
 #pragma unroll
-      for (int hf = 1; hf >= 0; --hf) {
-        if (hf == 0) {
-          tmem_ld32(s_addr, x);
-          tmem_ld32(s_addr + 32, x + 32);
-          tmem_wait_ld();
-          if (edge) {
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t pk[16];
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (!((kw[c >> 5] >> (c & 31)) & 1u)) x[c] = -INFINITY;
+        for (int e = 0; e < 32; e += 2) {
+          const int c = cc * 32 + e;
+          const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
+          float2 ex;
+          bool use_poly = false;
+          if constexpr (kPolyPairEvery > 0) use_poly = (c >> 1) % kPolyMod == kPolyMod - 1;
+          if (use_poly) {
+            ex = poly_exp2x2(a);
+          } else {
+            ex.x = fast_exp2(a.x);
+            ex.y = fast_exp2(a.y);
           }
+          rs2[(e >> 1) & 1] = __fadd2_rn(rs2[(e >> 1) & 1], ex);
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(ex.x, ex.y);
+          pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
         }
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const int c = cc * 32 + e;
-            const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
-            float2 ex;
-            bool use_poly = false;
-            if constexpr (kPolyPairEvery > 0) use_poly = (c >> 1) % kPolyMod == kPolyMod - 1;
-            if (use_poly) {
-              ex = poly_exp2x2(a);
-            } else {
-              ex.x = fast_exp2(a.x);
-              ex.y = fast_exp2(a.y);
-            }
-            rs2[(e >> 1) & 1] = __fadd2_rn(rs2[(e >> 1) & 1], ex);
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(ex.x, ex.y);
-            pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
-          }
-          tmem_st16u(s_addr + 64 + hf * 32 + cc * 16, pk);
-        }
+        tmem_st16u(s_addr + cc * 16, pk);
       }
       const float2 rsum = __fadd2_rn(rs2[0], rs2[1]);
       l_run = l_run * alpha + (rsum.x + rsum.y);
       tmem_wait_st();
       if (n >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        // O must hold PV(n-1) before it is rescaled.  PV(n-1) committed onto the
-        // barrier of its P buffer; that barrier cannot have moved past this
-        // phase because PV(n+2) needs this thread's P(n+2).
-        const int pb = (n - 1) % kSBufs;
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(BPV + pb), ((n - 1) / kSBufs) & 1, abort_flag))) {
+        // O must hold PV(n-1) before it is rescaled; that barrier cannot have
+        // completed PV(n) (which needs this thread's P(n)), so its parity is exact.
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(BPV), (n - 1) & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -646,8 +635,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       fence_before();
       mbar_arrive(bar(BPF));
     }
-    if (ok && ntiles > 0)
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV + (ntiles - 1) % kSBufs), ((ntiles - 1) / kSBufs) & 1, abort_flag));
+    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV), (ntiles - 1) & 1, abort_flag));
     if (!ok) {
       *abort_flag = 1;
       atomicCAS(prm.status, 0, kErrTimeoutSoftmax);
@@ -703,7 +691,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-static int make_map(CUtensorMap *map, const void *base, int64_t L, int64_t Hx, int64_t B, const int64_t *st) {
+static int make_map(CUtensorMap *map, const void *base, int64_t L, int64_t Hx, int64_t B, const int64_t *st,
+                    int box_rows) {
   auto enc = get_encode();
   if (!enc) {
     set_error(FFTS_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -711,7 +700,7 @@ static int make_map(CUtensorMap *map, const void *base, int64_t L, int64_t Hx, i
   }
   cuuint64_t dims[4] = {cuuint64_t(kD), cuuint64_t(L), cuuint64_t(Hx), cuuint64_t(B)};
   cuuint64_t strides[3] = {cuuint64_t(st[2]) * 2, cuuint64_t(st[1]) * 2, cuuint64_t(st[0]) * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, cuuint32_t(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -737,7 +726,7 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   FFTS_REQUIRE(B >= 1 && H >= 1 && Hkv >= 1 && H % Hkv == 0 && L >= 1, "sparse_attn: bad shape");
   const int64_t nblk = ceil_div(L, bs);
   const int64_t nq = ceil_div(L, kBM);
-  FFTS_REQUIRE(nblk <= kMaxBlocks && nq <= kMaxTiles, "sparse_attn: sequence too long for the tile list");
+  FFTS_REQUIRE(nblk <= kMaxBlocks && ceil_div(L, kBN) <= kMaxTiles, "sparse_attn: sequence too long for the tile list");
   FFTS_REQUIRE(L < (int64_t(1) << 31) && B * H * nq < (int64_t(1) << 31), "sparse_attn: grid too large");
   for (const int64_t *st : {qs, ks, vs})
     FFTS_REQUIRE(st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0 && st[2] >= D,
@@ -747,9 +736,9 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
                "sparse_attn: tensors must be 16-byte aligned");
   FFTS_REQUIRE(os[0] % 8 == 0 && os[1] % 8 == 0 && os[2] % 8 == 0, "sparse_attn: output strides must be 16-byte multiples");
   CUtensorMap mq, mk, mv;
-  int rc = make_map(&mq, q, L, H, B, qs);
-  if (!rc) rc = make_map(&mk, k, L, Hkv, B, ks);
-  if (!rc) rc = make_map(&mv, v, L, Hkv, B, vs);
+  int rc = make_map(&mq, q, L, H, B, qs, kBM);
+  if (!rc) rc = make_map(&mk, k, L, Hkv, B, ks, kBN);
+  if (!rc) rc = make_map(&mv, v, L, Hkv, B, vs, kBN);
   if (rc) return rc;
   Params p{};
   p.B = int(B); p.H = int(H); p.Hkv = int(Hkv); p.L = int(L); p.bs = bs; p.causal = causal ? 1 : 0;
