@@ -296,13 +296,16 @@ def run_ours(args):
         F.fft_block_mask(ql, kl, **kw)
     ev[2].record(stream)
     out_l = torch.empty(1, L, shard.heads, HEAD_DIM, dtype=torch.bfloat16, device=dev)
+    attn_status = torch.zeros(1, dtype=torch.int32, device=dev)
     for _ in range(reps):
-        F.sparse_attention(ql, kl, vl, mask.bits, BLOCK, out=out_l)
+        F.sparse_attention(ql, kl, vl, mask.bits, BLOCK, out=out_l, status=attn_status)
     ev[3].record(stream)
     torch.cuda.synchronize(dev)
     t_pool = ev[0].elapsed_time(ev[1]) / reps
     t_mask = ev[1].elapsed_time(ev[2]) / reps  # includes pooling
     t_attn = ev[2].elapsed_time(ev[3]) / reps
+    if int(attn_status.item()) != 0:
+        raise RuntimeError(f"attention kernel reported status {int(attn_status.item())} (a bounded wait timed out)")
     pairs = causal_pairs(mask.bits, L, BLOCK)
     flops = 4.0 * HEAD_DIM * pairs
     hbm_peak, bf16_peak, peak_kind = load_peaks()

@@ -280,7 +280,7 @@ struct SmemLayout {
   static constexpr int k = q + kQBytes;
   static constexpr int v = k + kKStages * kKVBytes;
   static constexpr int bars = v + kVStages * kKVBytes;
-  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 + 3;
+  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2 + 1;
   static constexpr int tmem_slot = bars + nbars * 8;
   static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
   static constexpr int list = misc + 16;        // uint16 tile list
@@ -296,9 +296,13 @@ constexpr int BKE = BKF + kKStages;     // K empty     [kKStages]
 constexpr int BVF = BKE + kKStages;     // V full      [kVStages]
 constexpr int BVE = BVF + kVStages;     // V empty     [kVStages]
 constexpr int BSF = BVE + kVStages;     // S(n) in TMEM buffer n % 2 [2]
-constexpr int BPV = BSF + 2;            // PV(n) complete (one phase per tile)
-constexpr int BPF = BPV + 1;            // P(n) in TMEM, O rescaled (128 arrivals)
-constexpr int BDRAIN = BPF + 1;
+constexpr int BPV = BSF + 2;            // PV(n) complete, per S buffer n % 2 [2]
+constexpr int BPF = BPV + 2;            // P(n) in TMEM, O rescaled, per S buffer n % 2 (128 arrivals) [2]
+constexpr int BDRAIN = BPF + 2;
+// Every ring of barriers above has one barrier per buffer because the softmax
+// may run a full tile ahead of the MMA issuer (S(n+1) is computed before PV(n)
+// is issued): with a single P barrier it could complete two phases before the
+// issuer observes the first, and the parity wait would alias.
 
 struct Params {
   int B, H, Hkv, L, bs, bs_shift, causal;
@@ -372,7 +376,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(bar(BSF), 1);
     mbar_init(bar(BSF + 1), 1);
     mbar_init(bar(BPV), 1);
+    mbar_init(bar(BPV + 1), 1);
     mbar_init(bar(BPF), 128);
+    mbar_init(bar(BPF + 1), 128);
     mbar_init(bar(BDRAIN), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       auto issue_pv = [&](int m) -> bool {
         const int s = m % 2;
         if (!mbar_wait(bar(BVF + s), (m >> 1) & 1, abort_flag)) return false;
-        if (!mbar_wait(bar(BPF), m & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(BPF + s), (m >> 1) & 1, abort_flag)) return false;
         fence_after();
         const uint32_t vsm = sbase + SmemLayout::v + s * kKVBytes;
         const uint32_t pt = tmem + s * kBN;  // P(m): bf16 pairs in the first 32 columns of S buffer m % 2
@@ -508,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar(BVE + s));
-        umma_commit(bar(BPV));
+        umma_commit(bar(BPV + s));
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -610,9 +616,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       l_run = l_run * alpha + (rsum.x + rsum.y);
       tmem_wait_st();
       if (n >= 1 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-        // O must hold PV(n-1) before it is rescaled; that barrier cannot have
-        // completed PV(n) (which needs this thread's P(n)), so its parity is exact.
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(BPV), (n - 1) & 1, abort_flag))) {
+        // O must hold PV(n-1) before it is rescaled.  PV(n-1) completes the
+        // barrier of S buffer (n-1) % 2; that barrier's previous phase (PV(n-3))
+        // is complete and its next (PV(n+1)) needs P(n+1), so the parity is exact.
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(bar(BPV + (n - 1) % 2), ((n - 1) >> 1) & 1, abort_flag))) {
           ok = false;
           break;
         }
@@ -633,9 +641,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_st();
       }
       fence_before();
-      mbar_arrive(bar(BPF));
+      mbar_arrive(bar(BPF + sb));
     }
-    if (ok && ntiles > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV), (ntiles - 1) & 1, abort_flag));
+    // O is final once PV(ntiles-1) has completed (its commit also covers every
+    // earlier MMA).  Its buffer's barrier has completed PV(ntiles-3) and has no
+    // later phase, so the parity is exact.
+    if (ok && ntiles > 0) {
+      const int m = ntiles - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV + m % 2), (m >> 1) & 1, abort_flag));
+    }
     if (!ok) {
       *abort_flag = 1;
       atomicCAS(prm.status, 0, kErrTimeoutSoftmax);

@@ -1,27 +1,29 @@
 // mask.cu -- FFTSparse block-mask selection on sm_100a.
 //
 // Replaces the selection half of myattn_prefill (attn_src/fft_attn/my_attn_v7.py
-// :532-641) with four kernels that keep every decision on the device (the
+// :532-641) with three launches that keep every decision on the device (the
 // reference syncs the host at :273 and :597 and loops over sampled diagonals on
 // the host at :342-357):
 //
-//   fft_partial_kernel   per (b, h, 8-channel chunk): zero-padded FFT of
-//                        z = q + i k per channel (warp-shuffle butterflies for
-//                        spans < 32, shared-memory butterflies above), cross
-//                        spectrum Q conj(K) summed over the chunk's channels.
-//                        (batch_fft_cross_correlation, :117-131)
-//   corr_select_kernel   per (b, h): sum of chunk spectra, one inverse FFT,
-//                        the reference's post-processing (:132-155), and the
-//                        lag selection by normalised threshold or quantile
-//                        (create_correlation_block_mask, :195-208).
-//   head_stats_kernel    per (b, h): stripe statistic over sampled diagonals
-//                        (compute_stripe_variance, :301-383), hot key columns
-//                        (create_column_block_mask, :390-447) and the last
-//                        query row's top-k (create_last_block_query_mask, :54-72).
-//   mask_build_kernel    per (b, h, row tile): per-row QK top-k for diffuse
-//                        heads (create_qk_topk_block_mask, :256-294) and the
-//                        union with the prior, Toeplitz lag, column and last-row
-//                        masks (:74-98, :212-225, :606-641) into packed bits.
+//   select_stage1_kernel  one launch for all independent per-head jobs:
+//      fft_partial_body   per (b, h, 8-channel chunk): zero-padded FFT of
+//                         z = q + i k per channel (warp-shuffle butterflies for
+//                         spans < 32, shared-memory butterflies above), cross
+//                         spectrum Q conj(K) summed over the chunk's channels
+//                         (batch_fft_cross_correlation, :117-131);
+//      diag_stats_body    per (b, h, sampled lag): the normalised variance of
+//                         one block-score diagonal (compute_stripe_variance,
+//                         :301-383);
+//      colrow_body        per (b, h): hot key columns (create_column_block_mask,
+//                         :390-447) and the last query row's top-k
+//                         (create_last_block_query_mask, :54-72).
+//   corr_select_kernel    per (b, h): the stripe decision, one inverse FFT of the
+//                         summed spectrum, the post-processing (:132-155) and the
+//                         lag selection (create_correlation_block_mask, :195-208).
+//   mask_build_kernel     per (b, h, row tile): per-row QK top-k for diffuse
+//                         heads (create_qk_topk_block_mask, :256-294) and the
+//                         union with the prior, Toeplitz lag, column and last-row
+//                         masks (:74-98, :212-225, :606-641) into packed bits.
 //
 // Arithmetic is the canonical one restated by oracle/ffts_oracle.c: fp32 FFT
 // butterflies with no contraction (__fmul_rn/__fadd_rn), exact-product fp64
@@ -31,6 +33,7 @@
 #include <math.h>
 #include <stdarg.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -136,18 +139,14 @@ __device__ void fft_block(float2 *x, int M, int nfft, const float2 *tw, bool inv
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) fft_partial_kernel(const T *__restrict__ qb,
-                                                          const T *__restrict__ kb, int H, int Hkv,
-                                                          int N, int D, int M, int nf,
-                                                          float2 *__restrict__ partial) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__device__ void fft_partial_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int N,
+                                 int D, int M, int nf, float2 *__restrict__ partial, int chunk, int nchunk,
+                                 int bh, unsigned char *smem_raw) {
   float2 *tw = reinterpret_cast<float2 *>(smem_raw);  // [M/2]
   float2 *acc = tw + M / 2;                            // [M/2 + 1]
   float2 *buf = acc + (M / 2 + 1) + 1;                 // [nf][M] (16-byte aligned)
   const int F = M / 2 + 1;
   const int bits = ilog2_ceil(M);
-  const int chunk = blockIdx.x, nchunk = gridDim.x;
-  const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
@@ -188,6 +187,8 @@ __global__ void __launch_bounds__(256) fft_partial_kernel(const T *__restrict__ 
   float2 *out = partial + (int64_t(bh) * nchunk + chunk) * F;
   for (int f = threadIdx.x; f < F; f += blockDim.x) out[f] = acc[f];
 }
+
+static size_t fft_partial_smem(int M, int nf) { return size_t(M / 2 + M / 2 + 2 + size_t(nf) * M) * sizeof(float2); }
 
 // ------------------------------------------------------- block selection
 // Ascending-rank selection of 32-bit keys (keys[0..n)) by 8-bit radix passes.
@@ -264,9 +265,17 @@ __device__ void block_topk_bits(const uint32_t *keys, int lo, int hi, int k, uin
 }
 
 // -------------------------------------------------- correlation + lag select
+// Stage 2, one CTA per (b, h): the stripe decision (average of the per-lag
+// statistics in sample order, my_attn_v7.py:359-363), then the summed cross
+// spectrum's inverse FFT, post-processing and lag selection.  With the lag mask
+// off it writes is_stripe = 0 and zero lag scores / selections.
 __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restrict__ partial,
                                                           int nchunk, int N, int M,
                                                           ffts_mask_params p,
+                                                          const double *__restrict__ nv,
+                                                          int32_t *__restrict__ stripe_ws,
+                                                          uint8_t *__restrict__ is_stripe_out,
+                                                          float *__restrict__ stripe_var_out,
                                                           float *__restrict__ corr_out,
                                                           float *__restrict__ csum_out,
                                                           uint32_t *__restrict__ tausel) {
@@ -283,6 +292,27 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
   const int bits = ilog2_ceil(M);
   const int W = (N + 31) / 32;
   const int stride = kMaxFFT / M;
+  if (threadIdx.x == 0) {
+    float svar = INFINITY;
+    int stripe = 0;
+    if (p.corr_on && !p.stripe_all_diffuse) {
+      double total = 0.0;
+      for (int s = 0; s < p.n_diag_samples; ++s) total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s]);
+      svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
+      stripe = svar <= p.stripe_threshold;
+    }
+    stripe_ws[bh] = stripe;
+    if (is_stripe_out) is_stripe_out[bh] = (uint8_t)stripe;
+    if (stripe_var_out) stripe_var_out[bh] = svar;
+  }
+  if (!p.corr_on) {
+    for (int w = threadIdx.x; w < W; w += blockDim.x) tausel[int64_t(bh) * W + w] = 0u;
+    for (int t = threadIdx.x; t < N; t += blockDim.x) {
+      if (corr_out) corr_out[int64_t(bh) * N + t] = 0.0f;
+      if (csum_out) csum_out[int64_t(bh) * N + t] = 0.0f;
+    }
+    return;
+  }
   for (int j = threadIdx.x; j < M / 2; j += blockDim.x) tw[j] = g_twiddle[j * stride];
   const float2 *part = partial + int64_t(bh) * nchunk * F;
   for (int f = threadIdx.x; f < F; f += blockDim.x) {
@@ -414,16 +444,14 @@ __device__ double lane_tree(double v, double *part) {
 // ------------------------------------------------------- stripe statistic
 // One CTA per (sampled lag, b, h): the normalised variance of the adjacent
 // differences along one block-score diagonal (my_attn_v7.py:342-351), written to
-// nv[bh * S + s].  head_stats_kernel averages the S values in sample order.
+// nv[bh * S + s].  corr_select_kernel averages the S values in sample order.
 template <typename T>
-__global__ void __launch_bounds__(256) diag_stats_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
-                                                         int H, int Hkv, int D, ffts_mask_params p,
-                                                         double *__restrict__ nv) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__device__ void diag_stats_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
+                                const ffts_mask_params &p, double *__restrict__ nv, int s, int bh,
+                                unsigned char *smem_raw) {
   const int N = p.n_blocks;
   double *part = reinterpret_cast<double *>(smem_raw);  // [256]
   float *vals = reinterpret_cast<float *>(part + kLanes);  // [N]
-  const int s = blockIdx.x, bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
@@ -456,69 +484,58 @@ __global__ void __launch_bounds__(256) diag_stats_kernel(const T *__restrict__ q
   if (threadIdx.x == 0) nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s] = __ddiv_rn(var, mabs);
 }
 
+static size_t diag_stats_smem(int N) { return size_t(kLanes) * 8 + size_t(N) * 4; }
+
 // ------------------------------------------------------------ head stats
+// Hot key columns (create_column_block_mask, my_attn_v7.py:403-437) and the last
+// query row's top-k (create_last_block_query_mask, :54-72) of one (b, h).
+// Column scores are produced for every head; the mask composition applies them
+// only where the reference does (stripe heads, or all heads without the lag mask).
+// The suffix sums over q run from row N-2 downwards in 32-row chunks staged
+// through shared memory (row strides padded by one element against bank
+// conflicts); each column's dot product is one fp64 FMA chain in d order.
 template <typename T>
-__global__ void __launch_bounds__(256) head_stats_kernel(const T *__restrict__ qb,
-                                                         const T *__restrict__ kb, int H, int Hkv,
-                                                         int D, ffts_mask_params p,
-                                                         const double *__restrict__ nv,
-                                                         int32_t *__restrict__ stripe_ws,
-                                                         uint8_t *__restrict__ is_stripe_out,
-                                                         float *__restrict__ stripe_var_out,
-                                                         uint32_t *__restrict__ colsel,
-                                                         uint32_t *__restrict__ lastsel) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__device__ void colrow_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
+                            const ffts_mask_params &p, uint32_t *__restrict__ colsel,
+                            uint32_t *__restrict__ lastsel, int bh, unsigned char *smem_raw, int *hist, int *bc) {
   const int N = p.n_blocks;
   const int W = (N + 31) / 32;
-  double *part = reinterpret_cast<double *>(smem_raw);      // [256]
-  double *pch = part + kLanes;                              // [32][D]
-  float *vals = reinterpret_cast<float *>(pch + 32 * D);    // [N]
+  const int QS = D + 1;  // padded row stride (elements)
+  float *qs = reinterpret_cast<float *>(smem_raw);      // [32][QS]
+  float *ks = qs + 32 * QS;                             // [32][QS]
+  double *pch = reinterpret_cast<double *>(ks + 32 * QS + (32 * QS & 1));  // [32][QS], 8-byte aligned
+  float *vals = reinterpret_cast<float *>(pch + 32 * QS);  // [N]
   uint32_t *keys = reinterpret_cast<uint32_t *>(vals + N);  // [N]
   uint32_t *words = keys + N;                               // [W]
-  __shared__ int hist[256];
-  __shared__ int bc[4];
-  __shared__ int stripe_sh;
-  const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
   const double sqrtD = sqrt((double)D);
 
-  // ---- stripe statistic: average of the per-lag values in sample order
-  float svar = INFINITY;
-  int stripe = 0;
-  if (p.corr_on && !p.stripe_all_diffuse) {
-    double total = 0.0;
-    for (int s = 0; s < p.n_diag_samples; ++s) total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s]);
-    svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
-    stripe = svar <= p.stripe_threshold;
-  }
-  if (threadIdx.x == 0) {
-    stripe_ws[bh] = stripe;
-    if (is_stripe_out) is_stripe_out[bh] = (uint8_t)stripe;
-    if (stripe_var_out) stripe_var_out[bh] = svar;
-  }
-
-  // ---- hot key columns
-  const int col_apply = p.col_on && (!p.corr_on || stripe);
   for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
   __syncthreads();
-  if (col_apply && p.col_end > p.col_start) {
+  if (p.col_on && p.col_end > p.col_start) {
     double P = 0.0;
     for (int jhi = N - 1; jhi >= 0; jhi -= 32) {
-      const int jlo = max(0, jhi - 31);
+      const int rows = min(32, jhi + 1);
+      for (int e = threadIdx.x; e < rows * D; e += blockDim.x) {
+        const int t = e / D, dd = e - t * D;
+        const int64_t off = int64_t(jhi - t) * D + dd;
+        qs[t * QS + dd] = Elem<T>::to_f32(q[off]);
+        ks[t * QS + dd] = Elem<T>::to_f32(k[off]);
+      }
+      __syncthreads();
       if (threadIdx.x < D) {
-        for (int j = jhi; j >= jlo; --j) {
-          if (j <= N - 2) P = __dadd_rn(P, (double)Elem<T>::to_f32(q[int64_t(j) * D + threadIdx.x]));
-          pch[(jhi - j) * D + threadIdx.x] = P;
+        for (int t = 0; t < rows; ++t) {
+          if (jhi - t <= N - 2) P = __dadd_rn(P, (double)qs[t * QS + threadIdx.x]);
+          pch[t * QS + threadIdx.x] = P;
         }
       }
       __syncthreads();
-      if (threadIdx.x <= jhi - jlo) {
-        const int j = jhi - threadIdx.x;
+      if (threadIdx.x < rows) {
+        const int t = threadIdx.x, j = jhi - t;
         double acc = 0.0;
-        for (int d = 0; d < D; ++d)
-          acc = __fma_rn(pch[threadIdx.x * D + d], (double)Elem<T>::to_f32(k[int64_t(j) * D + d]), acc);
+        for (int d = 0; d < D; ++d) acc = __fma_rn(pch[t * QS + d], (double)ks[t * QS + d], acc);
         const int cnt = max(1, N - j - 1);
         vals[j] = __double2float_rn(__ddiv_rn(__ddiv_rn(acc, sqrtD), (double)cnt));
       }
@@ -532,20 +549,50 @@ __global__ void __launch_bounds__(256) head_stats_kernel(const T *__restrict__ q
   for (int w = threadIdx.x; w < W; w += blockDim.x) colsel[int64_t(bh) * W + w] = words[w];
   __syncthreads();
 
-  // ---- last query row
   for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
   __syncthreads();
   if (p.last_on) {
     for (int j = threadIdx.x; j < N; j += blockDim.x) {
-      const double s = dot64_rows(q + int64_t(N - 1) * D, k + int64_t(j) * D, D);
-      keys[j] = f32_key(Elem<T>::round_f32(__double2float_rn(s)));
+      const double sc = dot64_rows(q + int64_t(N - 1) * D, k + int64_t(j) * D, D);
+      keys[j] = f32_key(Elem<T>::round_f32(__double2float_rn(sc)));
     }
     __syncthreads();
     block_topk_bits(keys, 0, N, p.last_topk, words, hist, bc);
   }
   __syncthreads();
   for (int w = threadIdx.x; w < W; w += blockDim.x) lastsel[int64_t(bh) * W + w] = words[w];
-  (void)stripe_sh;
+}
+
+static size_t colrow_smem(int N, int D) {
+  const size_t QS = size_t(D) + 1;
+  return (64 * QS + 1) * 4 + 32 * QS * 8 + size_t(N) * 8 + size_t((N + 31) / 32) * 4 + 16;
+}
+
+// Stage 1 of the selection: every independent per-head job of the path in one
+// launch, so that these small latency-bound jobs run side by side across the
+// SMs: blocks [0, nF) compute FFT partial spectra (one per (b, h, 8-channel
+// chunk)), blocks [nF, nF+nD) the per-lag stripe statistics (one per (b, h,
+// sampled lag)), and the last B*H blocks the column and last-row selections.
+template <typename T>
+__global__ void __launch_bounds__(256) select_stage1_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
+                                                            int H, int Hkv, int D, ffts_mask_params p, int M,
+                                                            int nf, int nchunk, int nF, int nD,
+                                                            float2 *__restrict__ partial, double *__restrict__ nv,
+                                                            uint32_t *__restrict__ colsel,
+                                                            uint32_t *__restrict__ lastsel) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int hist[256];
+  __shared__ int bc[4];
+  const int bid = blockIdx.x;
+  if (bid < nF) {
+    fft_partial_body<T>(qb, kb, H, Hkv, p.n_blocks, D, M, nf, partial, bid % nchunk, nchunk, bid / nchunk,
+                        smem_raw);
+  } else if (bid < nF + nD) {
+    const int e = bid - nF;
+    diag_stats_body<T>(qb, kb, H, Hkv, D, p, nv, e % p.n_diag_samples, e / p.n_diag_samples, smem_raw);
+  } else {
+    colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid - nF - nD, smem_raw, hist, bc);
+  }
 }
 
 // ------------------------------------------------------- warp selection
@@ -779,39 +826,26 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
                           cudaStream_t stream) {
   const int N = p.n_blocks;
   const int M = 1 << ilog2_ceil(2 * int64_t(N));
-  const int F = M / 2 + 1;
   const int nchunk = int(ceil_div(D, kDChunk));
   const int W = int(ceil_div(N, 32));
   const unsigned BH = unsigned(B * H);
-  if (p.corr_on) {
-    // FFT partial spectra
-    const size_t fixed = size_t(M / 2 + F + 1) * sizeof(float2);
-    int nf = kDChunk;
-    while (nf > 1 && fixed + size_t(nf) * M * sizeof(float2) > 200 * 1024) nf >>= 1;
-    const size_t smem1 = fixed + size_t(nf) * M * sizeof(float2);
-    FFTS_CUDA(cudaFuncSetAttribute(fft_partial_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
-    fft_partial_kernel<T><<<dim3(nchunk, BH), 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), N, int(D), M, nf, ws.partial);
-    FFTS_CUDA(cudaGetLastError());
-    const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
-    FFTS_CUDA(cudaFuncSetAttribute(corr_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2)));
-    corr_select_kernel<<<BH, 512, smem2, stream>>>(ws.partial, nchunk, N, M, p, corr, csum, ws.tausel);
-    FFTS_CUDA(cudaGetLastError());
-  } else {
-    FFTS_CUDA(cudaMemsetAsync(ws.tausel, 0, size_t(BH) * W * 4, stream));
-    if (corr) FFTS_CUDA(cudaMemsetAsync(corr, 0, size_t(BH) * N * 4, stream));
-    if (csum) FFTS_CUDA(cudaMemsetAsync(csum, 0, size_t(BH) * N * 4, stream));
-  }
-  if (p.corr_on && !p.stripe_all_diffuse) {
-    const size_t smemd = size_t(kLanes) * 8 + size_t(N) * 4;
-    FFTS_CUDA(cudaFuncSetAttribute(diag_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smemd)));
-    diag_stats_kernel<T><<<dim3(unsigned(p.n_diag_samples), BH), 256, smemd, stream>>>(qb, kb, int(H), int(Hkv),
-                                                                                       int(D), p, ws.nv);
-    FFTS_CUDA(cudaGetLastError());
-  }
-  const size_t smem3 = size_t(kLanes) * 8 + size_t(32) * D * 8 + size_t(N) * 8 + size_t(W) * 4;
-  FFTS_CUDA(cudaFuncSetAttribute(head_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem3)));
-  head_stats_kernel<T><<<BH, 256, smem3, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, ws.nv, ws.stripe, is_stripe,
-                                                   svar, ws.colsel, ws.lastsel);
+  // stage 1: FFT partial spectra, per-lag stripe statistics, column and last-row selections
+  int nf = kDChunk;
+  while (nf > 1 && fft_partial_smem(M, nf) > 64 * 1024) nf >>= 1;
+  const int nF = p.corr_on ? nchunk * int(BH) : 0;
+  const int nD = (p.corr_on && !p.stripe_all_diffuse) ? p.n_diag_samples * int(BH) : 0;
+  size_t smem1 = colrow_smem(N, int(D));
+  if (nF) smem1 = std::max(smem1, fft_partial_smem(M, nf));
+  if (nD) smem1 = std::max(smem1, diag_stats_smem(N));
+  FFTS_CUDA(cudaFuncSetAttribute(select_stage1_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
+  select_stage1_kernel<T><<<unsigned(nF + nD + BH), 256, smem1, stream>>>(
+      qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, nF, nD, ws.partial, ws.nv, ws.colsel, ws.lastsel);
+  FFTS_CUDA(cudaGetLastError());
+  // stage 2: stripe decision, inverse FFT, lag selection
+  const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
+  FFTS_CUDA(cudaFuncSetAttribute(corr_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2)));
+  corr_select_kernel<<<BH, 512, smem2, stream>>>(ws.partial, nchunk, N, M, p, ws.nv, ws.stripe, is_stripe, svar,
+                                                 corr, csum, ws.tausel);
   FFTS_CUDA(cudaGetLastError());
   const int R = N <= 1024 ? 16 : max(1, 16384 / N);
   const size_t smem4 = size_t(R) * D * 8 + size_t(R) * N * 4 + size_t(R) * W * 4 + 8 * 256 * 4 + size_t(R) * 4;
