@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-ttft", action="store_true")
+    ap.add_argument("--ttft-layers", type=int, default=32)
     return ap.parse_args()
 
 
@@ -202,6 +204,129 @@ def run_reference(args):
         "detail": info,
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- TTFT (cfg 4)
+class Llama8BShape:
+    """Random-init decoder with Llama-3.1-8B shapes: hidden
+    4096, 32 q / 8 kv heads of 128, SwiGLU 14336, RMSNorm, RoPE base 500000,
+    vocab 128256, bf16.  Weights ~ N(0, 0.02) drawn with one seed (identical on
+    every rank), norm weights 1.  The dense parts are torch/cuBLAS; every
+    layer's attention is fftsparse_b200's operator on un-expanded GQA k/v.
+    With world > 1 each rank keeps only its KV groups' columns of the QKV
+    projection, runs attention for its heads, and one all-gather per layer
+    assembles the head-major output that o_proj consumes (o_proj and the MLP
+    are replicated)."""
+
+    H, HKV, D, HIDDEN, INTER, VOCAB = 32, 8, 128, 4096, 14336, 128256
+
+    def __init__(self, layers, device, world=1, rank=0, seed=0):
+        from fftsparse_b200.dist import kv_group_shard
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.shard = kv_group_shard(self.H, self.HKV, world, rank)
+        self.world = world
+        D = self.D
+
+        def w(*shape):
+            return (torch.randn(*shape, generator=g, device=device, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+
+        sh = self.shard
+        cols = torch.cat([torch.arange(sh.h_lo * D, sh.h_hi * D),
+                          self.H * D + torch.arange(sh.kv_lo * D, sh.kv_hi * D),
+                          (self.H + self.HKV) * D + torch.arange(sh.kv_lo * D, sh.kv_hi * D)]).to(device)
+        self.embed = w(self.VOCAB, self.HIDDEN)
+        self.layers = []
+        for _ in range(layers):
+            wqkv = w(self.HIDDEN, (self.H + 2 * self.HKV) * D)
+            self.layers.append(dict(
+                wqkv=wqkv if world == 1 else wqkv[:, cols].contiguous(),
+                wo=w(self.H * D, self.HIDDEN),
+                wgu=w(self.HIDDEN, 2 * self.INTER),
+                wd=w(self.INTER, self.HIDDEN)))
+            del wqkv
+        self.lm_head = w(self.HIDDEN, self.VOCAB)
+        self.device = device
+        self._rope = None
+
+    @staticmethod
+    def rmsnorm(x, eps=1e-5):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.bfloat16)
+
+    def forward(self, ids, kw):
+        import fftsparse_b200 as F
+        from fftsparse_b200.dist import sharded_prefill
+        L, D = ids.shape[0], self.D
+        Hl, Hkvl = self.shard.heads, self.shard.kv_hi - self.shard.kv_lo
+        if self._rope is None or self._rope[0].shape[0] != L:
+            inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
+            fr = torch.arange(L, device=self.device, dtype=torch.float64)[:, None] * inv[None]
+            emb = torch.cat([fr, fr], -1)
+            self._rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16))
+        cos, sin = self._rope
+
+        def rope(x):  # x [1, h, L, D]
+            x1, x2 = x[..., :D // 2], x[..., D // 2:]
+            return x * cos + torch.cat([-x2, x1], -1) * sin
+
+        h = self.embed[ids]
+        full = None if self.world == 1 else torch.empty(1, self.H, L, D, dtype=torch.bfloat16, device=self.device)
+        for lw in self.layers:
+            x = self.rmsnorm(h)
+            qkv = x @ lw["wqkv"]
+            q = rope(qkv[:, :Hl * D].view(L, Hl, D).transpose(0, 1)[None])
+            k = rope(qkv[:, Hl * D:(Hl + Hkvl) * D].view(L, Hkvl, D).transpose(0, 1)[None])
+            v = qkv[:, (Hl + Hkvl) * D:].view(L, Hkvl, D).transpose(0, 1)[None].contiguous()
+            del qkv
+            if self.world == 1:
+                attn = F.myattn_prefill(q, k, v, 0, **kw).view(L, self.H * D)
+            else:
+                sharded_prefill(q, k, v, 0, out=full, inputs_are_local=True, **kw)
+                attn = full[0].transpose(0, 1).reshape(L, self.H * D)
+            del q, k, v
+            h = h + attn @ lw["wo"]
+            del attn
+            x = self.rmsnorm(h)
+            gu = x @ lw["wgu"]
+            h = h + (torch.nn.functional.silu(gu[:, :self.INTER]) * gu[:, self.INTER:]) @ lw["wd"]
+            del gu
+        return self.rmsnorm(h[-1:]) @ self.lm_head  # logits of the last position only
+
+
+def run_ttft(args, dev, world, rank, stream, barrier):
+    """Prefill TTFT of the 8B-shape decoder: token ids already on the device to
+    the last position's logits, device-timed with CUDA events, max over ranks."""
+    import torch.distributed as dist
+    L = args.seq_len
+    model = Llama8BShape(args.ttft_layers, dev, world, rank)
+    g = torch.Generator(device=dev).manual_seed(0)
+    ids = torch.randint(0, model.VOCAB, (L,), generator=g, device=dev)
+    kw = mask_kwargs(args.keep_ratio)
+    reps = 2
+    with torch.no_grad():
+        model.forward(ids, kw)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            logits = model.forward(ids, kw)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    finite = bool(torch.isfinite(logits.float()).all())
+    del model
+    torch.cuda.empty_cache()
+    return {"value": round(float(t.item()) / 1e3, 4), "unit": "s",
+            "workload": f"cfg4: Llama-3.1-8B-shape decoder, {args.ttft_layers} layers, random N(0,0.02) weights "
+                        f"(seed 0), bf16; prefill of {L} uniform random token ids (seed 0) to the last-token "
+                        f"logits; FFTSparse attention (keep ratio {args.keep_ratio}) in every layer, GQA k/v "
+                        f"un-expanded; dense parts torch/cuBLAS"
+                        + ("" if world == 1 else f"; QKV columns and attention sharded by KV group over {world} "
+                                                 f"ranks, o_proj/MLP replicated"),
+            "logits_finite": finite, "reps": reps}
 
 
 # --------------------------------------------------------------- our arm
@@ -381,6 +506,10 @@ def run_ours(args):
                "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 2),
                "d2h_bytes_per_step": int(res_h.numel() * 2), "steps": args.e2e_steps}
 
+    ttft = None
+    if not args.no_ttft:
+        ttft = run_ttft(args, dev, world, rank, stream, barrier)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from fftsparse_b200.synthetic import make_inputs as mk
@@ -405,11 +534,12 @@ def run_ours(args):
                        "l2": "inputs (3.2 GB) larger than L2; no flush"},
             "clocks": clocks.summary(),
             "e2e": e2e,
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 6 * args.steps,  # 2 pool + select stage 1 + stage 2 + mask build + attention
             "roofline": roofline,
             "cpu_baseline": cpu,
             "stages": stages,
             "gqa_native_ms_per_layer": round(gqa_native_ms, 4),
+            "ttft": ttft,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -76,23 +76,32 @@ def gather_heads(local_out: torch.Tensor, full_out: torch.Tensor, group=None) ->
 
 
 def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx: int = 0, *,
-                    group=None, out: Optional[torch.Tensor] = None, **kwargs) -> torch.Tensor:
+                    group=None, out: Optional[torch.Tensor] = None, inputs_are_local: bool = False,
+                    **kwargs) -> torch.Tensor:
     """FFTSparse prefill of the rank's KV groups followed by the output all-gather.
 
     Returns the head-major output [B, H, L, D] (bf16) on every rank.  The mask
-    arguments are those of myattn_prefill.
+    arguments are those of myattn_prefill.  With ``inputs_are_local`` the q/k/v
+    given already hold only this rank's heads (its KV groups, in rank order), as
+    when each rank computes its own columns of the QKV projection.
     """
     from .prefill import fft_block_mask, sparse_attention
 
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     B, H, L, D = q.shape
-    # KV groups: k's own head count, or (for repeat_kv-expanded k) num_kv_heads
-    n_kv = kwargs.pop("num_kv_heads", None)
-    if k.shape[1] != H or n_kv is None:
-        n_kv = k.shape[1]
-    shard = kv_group_shard(H, n_kv, world, rank)
-    ql, kl, vl = local_views(q, k, v, shard)
+    if inputs_are_local:
+        kwargs.pop("num_kv_heads", None)
+        H = H * world
+        shard = kv_group_shard(H, k.shape[1] * world if k.shape[1] != q.shape[1] else H, world, rank)
+        ql, kl, vl = q, k, v
+    else:
+        # KV groups: k's own head count, or (for repeat_kv-expanded k) num_kv_heads
+        n_kv = kwargs.pop("num_kv_heads", None)
+        if k.shape[1] != H or n_kv is None:
+            n_kv = k.shape[1]
+        shard = kv_group_shard(H, n_kv, world, rank)
+        ql, kl, vl = local_views(q, k, v, shard)
     block_size = kwargs.pop("block_size", 128)
     is_causal = kwargs.pop("is_causal", True)
     mask = fft_block_mask(ql, kl, block_size=block_size, **kwargs)

@@ -1,7 +1,8 @@
 """Multi-process host logic of the KV-group sharded prefill, on CPU ranks (gloo).
 
-The CUDA kernels are replaced by the CPU oracle inside each rank, so these tests
-check what the sharding adds: which heads a rank owns, the head-major
+The two CUDA entry points sharded_prefill calls are replaced by the CPU oracle
+inside each rank, so these tests run the real host code and check what the
+sharding adds: which heads a rank owns, the head-major
 all-gather, equality with the unsharded result, and that a rank that dies
 before the collective turns into an error on its peer instead of a hang.
 """
@@ -46,31 +47,47 @@ def test_local_views_expanded_and_gqa():
     assert torch.equal(ks, k_kv[:, 1:2])
 
 
-def _cpu_sharded_prefill(q, k, v, kw):
-    """sharded_prefill's host logic with the oracle standing in for the kernels."""
-    from oracle import oracle as O
+def _patch_kernels_with_oracle():
+    """Swap the two CUDA entry points sharded_prefill calls for oracle stand-ins,
+    so the real host logic (shard choice, local views, output layout, gather)
+    runs on CPU ranks."""
+    from types import SimpleNamespace
+
+    import fftsparse_b200.prefill as P
     from fftsparse_b200.params import derive_mask_params
-    world, rank = dist.get_world_size(), dist.get_rank()
-    B, H, L, D = q.shape
-    shard = kv_group_shard(H, k.shape[1], world, rank)
-    ql, kl, vl = local_views(q, k, v, shard)
-    params = derive_mask_params(L, **kw)
-    m = O.prefill_mask(ql.contiguous(), kl.contiguous(), params)
-    dense = O.unpack_bits(m["bits"], params.n_blocks)
-    local = O.sparse_attention(ql, kl, vl, dense, params.block_size).to(torch.bfloat16)
-    out = torch.empty(B, H, L, D, dtype=torch.bfloat16)
-    return gather_heads(local, out)
+    from oracle import oracle as O
+
+    def fake_mask(q, k, block_size=128, **kw):
+        params = derive_mask_params(q.shape[2], block_size=block_size, **kw)
+        m = O.prefill_mask(q.contiguous(), k.contiguous(), params)
+        return SimpleNamespace(bits=O.unpack_bits(m["bits"], params.n_blocks))
+
+    def fake_attn(q, k, v, dense, bs, causal=True, out=None, status=None):
+        res = O.sparse_attention(q, k, v, dense, bs, causal=causal).to(torch.bfloat16)  # [B, H, L, D]
+        out.copy_(res.permute(0, 2, 1, 3))
+        return out
+
+    P.fft_block_mask = fake_mask
+    P.sparse_attention = fake_attn
 
 
 def _worker(rank, world, port, result_q, kw):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
+        from fftsparse_b200.dist import sharded_prefill
         from oracle.synth import make_inputs
+        _patch_kernels_with_oracle()
         q, k, v = make_inputs(1536, num_q_heads=8, num_kv_heads=2, dtype=torch.bfloat16, expand=False)
-        out = _cpu_sharded_prefill(q, k, v, kw)
+        out_full = sharded_prefill(q, k, v, 0, **kw)
+        # each rank holding only its own heads (its columns of a QKV projection)
+        s = kv_group_shard(8, 2, world, rank)
+        ql, kl, vl = local_views(q, k, v, s)
+        out_local = sharded_prefill(ql.contiguous(), kl.contiguous(), vl.contiguous(), 0,
+                                    inputs_are_local=True, **kw)
         if rank == 0:
-            result_q.put(out.view(torch.int16).numpy().tobytes())
+            result_q.put((out_full.view(torch.int16).numpy().tobytes(),
+                          out_local.view(torch.int16).numpy().tobytes()))
     finally:
         dist.destroy_process_group()
 
@@ -85,12 +102,14 @@ def test_sharded_equals_unsharded_world2():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out, kw)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q_out.get(timeout=300)
+    got_full, got_local = q_out.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     import numpy as np
-    got = torch.from_numpy(np.frombuffer(got, dtype=np.int16).copy()).view(torch.bfloat16).view(1, 8, 1536, 128)
+
+    def as_bf16(b):
+        return torch.from_numpy(np.frombuffer(b, dtype=np.int16).copy()).view(torch.bfloat16).view(1, 8, 1536, 128)
 
     from oracle import oracle as O
     from oracle.synth import make_inputs
@@ -99,7 +118,8 @@ def test_sharded_equals_unsharded_world2():
     params = derive_mask_params(1536, **kw)
     m = O.prefill_mask(q, k, params)
     ref = O.sparse_attention(q, k, v, O.unpack_bits(m["bits"], params.n_blocks), 128).to(torch.bfloat16)
-    assert torch.equal(got, ref)
+    assert torch.equal(as_bf16(got_full), ref)
+    assert torch.equal(as_bf16(got_local), ref)
 
 
 def _dying_worker(rank, world, port, result_q):
