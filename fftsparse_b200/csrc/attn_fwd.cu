@@ -219,29 +219,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^a for a pair of values on the FMA and ALU pipes only (the MUFU pipe that
-// ex2.approx uses is the softmax's bottleneck at head_dim 128).  Range
-// reduction: a = n + f with n = round-to-nearest(a) read from the low mantissa
-// bits of a + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial
-// fitted here to minimise the relative error on [-0.5, 0.5] (max 7.5e-5, far
-// below bf16's 3.9e-3 for P); 2^n is added to the exponent bits.  Inputs below
-// -126 (including -inf) give exactly 0.
-__device__ __forceinline__ float2 poly_exp2x2(float2 a) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  const float2 ac = make_float2(fmaxf(a.x, -126.0f), fmaxf(a.y, -126.0f));
-  const float2 t = __fadd2_rn(ac, make_float2(kMagic, kMagic));
-  const float2 r = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
-  const float2 f = __ffma2_rn(r, make_float2(-1.0f, -1.0f), ac);
-  float2 p = __ffma2_rn(make_float2(0.0551716685295105f, 0.0551716685295105f), f,
-                        make_float2(0.2426111251115799f, 0.2426111251115799f));
-  p = __ffma2_rn(p, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
-  p = __ffma2_rn(p, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
-  // (bits(t) << 23) == n << 23 modulo 2^32, since bits(1.5 * 2^23) has 22 trailing zeros
-  const float ex = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
-  const float ey = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
-  return make_float2(a.x < -126.0f ? 0.0f : ex, a.y < -126.0f ? 0.0f : ey);
-}
-
 // Shared-memory matrix descriptor (tcgen05 "version 1" format).
 // SWIZZLE_128B; lbo/sbo in bytes.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -270,9 +247,11 @@ constexpr int kKStages = 2;     // K tile ring (a stage is released by the S MMA
 constexpr int kVStages = 2;     // V tile ring (released by the PV MMA)
 constexpr int kTmemCols = 256;  // S0, S1 (64 columns each) + O (128): two CTAs fill an SM's 512
 constexpr uint32_t kTmemO = 128;
-constexpr int kPolyPairEvery = 0;  // if > 0: one column pair in kPolyPairEvery takes the FMA-pipe exp2
-constexpr int kPolyMod = kPolyPairEvery > 0 ? kPolyPairEvery : 1;
-constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
+// P is kept <= 2^64 against the row's reference max: O and l are rescaled only
+// when a row's scores outgrow it by that much (fp32 O stays far from overflow:
+// < 2^64 * 2^18 keys * |v|)
+constexpr float kRescaleLog2 = 64.0f;
+constexpr float kPMax = 18446744073709551616.0f;  // 2^64
 
 struct SmemLayout {
   // offsets from the 1024-byte aligned base
@@ -537,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = threadIdx.x;  // query row within the tile == TMEM lane
     const int row_g = qt * kBM + r;
     const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    // m_ref: the max the current P and O are scaled to (lags the true max by < 2^8)
+    // m_ref: the max the current P and O are scaled to (lags the true max by < 2^64 in P)
     float m_ref = -INFINITY, l_run = 0.0f;
     bool ok = true;
     const int mrow = min(qt * mrows + r / rows_per_blk, prm.nblk - 1);
@@ -549,17 +528,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
       fence_after();
       const uint32_t s_addr = tmem + sb * kBN + lane_off;
-      float x[kBN];
-      tmem_ld32(s_addr, x);
-      tmem_ld32(s_addr + 32, x + 32);
-      tmem_wait_ld();
       // masks: causal diagonal, ragged end, and (block_size < 128) this row's own
       // mask row; whole 32-column words since block_size >= 32
       const int col0 = j * kBN;
-      if ((prm.causal && col0 + kBN - 1 > qt * kBM) || col0 + kBN > prm.L || prm.bs < kBM) {
+      const bool edge = (prm.causal && col0 + kBN - 1 > qt * kBM) || col0 + kBN > prm.L || prm.bs < kBM;
+      uint32_t kw[2] = {0xffffffffu, 0xffffffffu};
+      if (edge) {
         int lim = min(kBN, prm.L - col0);
         if (prm.causal) lim = min(lim, row_g - col0 + 1);
-        uint32_t kw[2];
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
           const int rem = lim - 32 * w;
@@ -570,47 +546,77 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
           kw[w] = m;
         }
-#pragma unroll
-        for (int c = 0; c < kBN; ++c)
-          if (!((kw[c >> 5] >> (c & 31)) & 1u)) x[c] = -INFINITY;
       }
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float x[kBN];
+      tmem_ld32(s_addr, x);
+      tmem_wait_ld();
+      tmem_ld32(s_addr + 32, x + 32);  // lands while the first half is processed
+      if (edge) {
 #pragma unroll
-      for (int c = 0; c < kBN; c += 2) mx4[(c >> 1) & 3] = max3f(mx4[(c >> 1) & 3], x[c], x[c + 1]);
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      // lazy rescale: keep m_ref unless the row max exceeds it by more than 2^8
-      float alpha = 1.0f;
-      const bool grow = mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * prm.scale_log2 > kRescaleLog2);
-      if (grow) {
-        alpha = m_ref == -INFINITY ? 0.0f : fast_exp2((m_ref - mx) * prm.scale_log2);
-        m_ref = mx;
+        for (int c = 0; c < 32; ++c)
+          if (!((kw[0] >> c) & 1u)) x[c] = -INFINITY;
       }
-      const float moff = (m_ref == -INFINITY ? 0.0f : m_ref) * prm.scale_log2;
-      const float2 off2 = make_float2(-moff, -moff);
-      // P = exp2(s*scale - m) as bf16 pairs into the first 32 columns of this S
-      // buffer (S has been read in full)
+      // P = exp2(s*scale - m_ref) as bf16 pairs over the first 32 columns of this
+      // S buffer (the columns already read).  The common path takes m_ref as it
+      // stands, without this tile's max, and keeps the result when every P of
+      // the row is <= 2^kRescaleLog2 (checked on the tile's row sum).  A row's
+      // first valid tile, or a tile whose P would exceed that, takes the max
+      // path: new m_ref, O and l rescaled by alpha, P recomputed.
       float2 rs2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      float alpha = 1.0f;
+      bool fast = !__any_sync(0xffffffffu, m_ref == -INFINITY);
+      auto exp_half = [&](int cc, float2 off2) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int c = cc * 32 + e;
           const float2 a = __ffma2_rn(make_float2(x[c], x[c + 1]), sc2, off2);
           float2 ex;
-          bool use_poly = false;
-          if constexpr (kPolyPairEvery > 0) use_poly = (c >> 1) % kPolyMod == kPolyMod - 1;
-          if (use_poly) {
-            ex = poly_exp2x2(a);
-          } else {
-            ex.x = fast_exp2(a.x);
-            ex.y = fast_exp2(a.y);
-          }
+          ex.x = fast_exp2(a.x);
+          ex.y = fast_exp2(a.y);
           rs2[(e >> 1) & 1] = __fadd2_rn(rs2[(e >> 1) & 1], ex);
           const __nv_bfloat162 pr = __floats2bfloat162_rn(ex.x, ex.y);
           pk[e >> 1] = *reinterpret_cast<const uint32_t *>(&pr);
         }
         tmem_st16u(s_addr + cc * 16, pk);
+      };
+      if (fast) {
+        const float moff = m_ref * prm.scale_log2;
+        exp_half(0, make_float2(-moff, -moff));
+        tmem_wait_ld();
+        if (edge) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (!((kw[1] >> c) & 1u)) x[32 + c] = -INFINITY;
+        }
+        exp_half(1, make_float2(-moff, -moff));
+        const float tsum = (rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y);
+        if (__any_sync(0xffffffffu, !(tsum <= kPMax))) {
+          fast = false;
+          tmem_wait_st();  // the max path below rewrites P
+          rs2[0] = rs2[1] = make_float2(0.0f, 0.0f);
+        }
+      } else {
+        tmem_wait_ld();
+        if (edge) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (!((kw[1] >> c) & 1u)) x[32 + c] = -INFINITY;
+        }
+      }
+      if (!fast) {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) mx4[(c >> 1) & 3] = max3f(mx4[(c >> 1) & 3], x[c], x[c + 1]);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        const bool grow = mx > m_ref && (m_ref == -INFINITY || (mx - m_ref) * prm.scale_log2 > kRescaleLog2);
+        if (grow) {
+          alpha = m_ref == -INFINITY ? 0.0f : fast_exp2((m_ref - mx) * prm.scale_log2);
+          m_ref = mx;
+        }
+        const float moff = (m_ref == -INFINITY ? 0.0f : m_ref) * prm.scale_log2;
+        exp_half(0, make_float2(-moff, -moff));
+        exp_half(1, make_float2(-moff, -moff));
       }
       const float2 rsum = __fadd2_rn(rs2[0], rs2[1]);
       l_run = l_run * alpha + (rsum.x + rsum.y);
