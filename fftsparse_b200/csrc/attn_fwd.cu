@@ -43,6 +43,7 @@ constexpr int kQHalf = kQBytes / 2;
 constexpr int kKVBytes = kBN * kD * 2;       // 16 KB: two [64 rows][64 cols] swizzle boxes
 constexpr int kKVHalf = kKVBytes / 2;
 constexpr int kMaxTiles = 4096;              // 64-key tiles per query tile (L <= 262144)
+constexpr int kTileWords = kMaxTiles / 32;   // tile bitmask words
 constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 1.965 GHz: bound on one wait
 constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own copies / MMAs
 
@@ -50,6 +51,7 @@ constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own
 constexpr int kErrTimeoutProducer = 1;
 constexpr int kErrTimeoutMma = 2;
 constexpr int kErrTimeoutSoftmax = 3;
+constexpr int kErrSmemAlign = 4;  // dynamic shared memory not 1024-byte aligned: nothing was run
 
 // ------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -243,7 +245,7 @@ constexpr uint32_t idesc_bf16(bool b_mn_major, int n) {
 
 // ------------------------------------------------------------------ layout
 // ------------------------------------------------------------------ layout
-constexpr int kKStages = 2;     // K tile ring (a stage is released by the S MMA that read it)
+constexpr int kKStages = 3;     // K tile ring (a stage is released by the S MMA that read it)
 constexpr int kVStages = 2;     // V tile ring (released by the PV MMA)
 constexpr int kTmemCols = 256;  // S0, S1 (64 columns each) + O (128): two CTAs fill an SM's 512
 constexpr uint32_t kTmemO = 128;
@@ -254,18 +256,19 @@ constexpr float kRescaleLog2 = 64.0f;
 constexpr float kPMax = 18446744073709551616.0f;  // 2^64
 
 struct SmemLayout {
-  // offsets from the 1024-byte aligned base
+  // offsets from the dynamic shared memory base (1024-byte aligned, checked)
   static constexpr int q = 0;
   static constexpr int k = q + kQBytes;
   static constexpr int v = k + kKStages * kKVBytes;
   static constexpr int bars = v + kVStages * kKVBytes;
-  static constexpr int nbars = 1 + 2 * kKStages + 2 * kVStages + 2 + 2 + 2 + 1;
+  static constexpr int nbars = 1 + 2 * kKStages + kVStages + 2 + 2 + 2 + 1;
   static constexpr int tmem_slot = bars + nbars * 8;
   static constexpr int misc = tmem_slot + 16;  // abort flag, tile count
-  static constexpr int list = misc + 16;        // uint16 tile list
-  static constexpr int end = list + kMaxTiles * 2;
-  static constexpr int bytes = end + 1024;      // + alignment slack
+  static constexpr int words = misc + 16;       // tile bitmask [kTileWords]
+  static constexpr int end = words + kTileWords * 4;
+  static constexpr int bytes = end;
 };
+// two CTAs per SM: 228 KB per SM, 1 KB of it reserved per CTA
 static_assert(2 * (SmemLayout::bytes + 1024) <= 228 * 1024, "two CTAs must fit in an SM's shared memory");
 
 // barrier indices
@@ -273,9 +276,8 @@ constexpr int BQ = 0;
 constexpr int BKF = 1;                  // K full      [kKStages]
 constexpr int BKE = BKF + kKStages;     // K empty     [kKStages]
 constexpr int BVF = BKE + kKStages;     // V full      [kVStages]
-constexpr int BVE = BVF + kVStages;     // V empty     [kVStages]
-constexpr int BSF = BVE + kVStages;     // S(n) in TMEM buffer n % 2 [2]
-constexpr int BPV = BSF + 2;            // PV(n) complete, per S buffer n % 2 [2]
+constexpr int BSF = BVF + kVStages;     // S(n) in TMEM buffer n % 2 [2]
+constexpr int BPV = BSF + 2;            // PV(n) complete, per S buffer n % 2 (also frees V stage n % 2) [2]
 constexpr int BPF = BPV + 2;            // P(n) in TMEM, O rescaled, per S buffer n % 2 (128 arrivals) [2]
 constexpr int BDRAIN = BPF + 2;
 // Every ring of barriers above has one barrier per buffer because the softmax
@@ -312,17 +314,37 @@ __device__ __forceinline__ uint32_t tile_word(const uint32_t *row, int W, int tw
   return out;
 }
 
+// Walks the set bits of the tile bitmask in increasing order; next() is called
+// exactly once per selected tile, so it never reads past the last set bit.
+struct TileCursor {
+  const uint32_t *words;
+  int w;
+  uint32_t cur;
+  __device__ explicit TileCursor(const uint32_t *wd) : words(wd), w(0), cur(wd[0]) {}
+  __device__ __forceinline__ int next() {
+    while (cur == 0) cur = words[++w];
+    const int t = __ffs(cur) - 1;
+    cur &= cur - 1;
+    return w * 32 + t;
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 2)
     sparse_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, Params prm) {
-  extern __shared__ uint8_t smem_dyn[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(16) uint8_t smem_dyn[];
+  uint8_t *smem = smem_dyn;
+  // SWIZZLE_128B TMA boxes and MMA descriptors need 1024-byte aligned tiles
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicCAS(prm.status, 0, kErrSmemAlign);
+    return;
+  }
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + SmemLayout::bars;
   auto bar = [&](int i) { return bar0 + 8u * uint32_t(i); };
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + SmemLayout::misc);
   int *ntiles_sh = reinterpret_cast<int *>(smem + SmemLayout::misc + 4);
-  uint16_t *list = reinterpret_cast<uint16_t *>(smem + SmemLayout::list);
+  uint32_t *words = reinterpret_cast<uint32_t *>(smem + SmemLayout::words);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SmemLayout::tmem_slot);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -348,10 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(bar(BKF + s), 1);
       mbar_init(bar(BKE + s), 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(bar(BVF + s), 1);
-      mbar_init(bar(BVE + s), 1);
-    }
+    for (int s = 0; s < kVStages; ++s) mbar_init(bar(BVF + s), 1);
     mbar_init(bar(BSF), 1);
     mbar_init(bar(BSF + 1), 1);
     mbar_init(bar(BPV), 1);
@@ -391,19 +410,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int lim = nkv - tw * 32;  // tiles valid in this word
         if (lim < 32) word &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
       }
-      const int cntw = __popc(word);
-      int incl = cntw;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      int pos = base + incl - cntw;
-      while (word) {
-        const int t = __ffs(word) - 1;
-        word &= word - 1;
-        list[pos++] = uint16_t(tw * 32 + t);
-      }
-      base += __shfl_sync(0xffffffffu, incl, 31);
+      if (tw < TW) words[tw] = word;
+      int cnt = __popc(word);
+      for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+      base += cnt;
     }
     if (lane == 0) *ntiles_sh = base;
   }
@@ -417,21 +427,26 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 4) {
     // ================================================================ TMA producer
     // Q once; K(n+1) runs one tile ahead of V(n).  K(n) reuses the stage of
-    // K(n-2), released by S(n-2); V(n) the stage of V(n-2), released by PV(n-2).
+    // K(n-3), released by S(n-3); V(n) the stage of V(n-2), released by PV(n-2).
     if (lane == 0 && ntiles > 0) {
       int issued_k = 0, issued_v = 0;
       bool ok = true;
       mbar_arrive_tx(bar(BQ), kQBytes);
       tma_load_4d(sbase + SmemLayout::q, &tm_q, bar(BQ), 0, qt * kBM, h, b);
       tma_load_4d(sbase + SmemLayout::q + kQHalf, &tm_q, bar(BQ), 64, qt * kBM, h, b);
+      TileCursor kcur(words), vcur(words);
       auto load = [&](int n, bool is_k) -> bool {
-        const int s = n % 2;
-        const int full = (is_k ? BKF : BVF) + s, empty = (is_k ? BKE : BVE) + s;
-        if (!mbar_wait(bar(empty), ((n >> 1) & 1) ^ 1, abort_flag)) return false;
+        const int ns = is_k ? kKStages : kVStages;
+        const int s = n % ns;
+        // a K stage is free once S(n-3) has completed (its empty barrier), a V
+        // stage once PV(n-2) has (the PV barrier of that buffer): the phase the
+        // V wait names is the latest one, since PV(n) needs the copy issued here
+        const int full = (is_k ? BKF : BVF) + s, empty = (is_k ? BKE : BPV) + s;
+        if (!mbar_wait(bar(empty), ((n / ns) & 1) ^ 1, abort_flag)) return false;
         mbar_arrive_tx(bar(full), kKVBytes);
         const uint32_t dst = sbase + (is_k ? SmemLayout::k : SmemLayout::v) + s * kKVBytes;
         const CUtensorMap *map = is_k ? &tm_k : &tm_v;
-        const int j = list[n];
+        const int j = is_k ? kcur.next() : vcur.next();
         tma_load_4d(dst, map, bar(full), 0, j * kBN, kvh, b);
         tma_load_4d(dst + kKVHalf, map, bar(full), 64, j * kBN, kvh, b);
         if (is_k) ++issued_k; else ++issued_v;
@@ -448,8 +463,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
         mbar_wait(bar(BQ), 0, &never, kDrainCycles);
-        for (int n = max(0, issued_k - 2); n < issued_k; ++n)
-          mbar_wait(bar(BKF + n % 2), (n >> 1) & 1, &never, kDrainCycles);
+        for (int n = max(0, issued_k - kKStages); n < issued_k; ++n)
+          mbar_wait(bar(BKF + n % kKStages), (n / kKStages) & 1, &never, kDrainCycles);
         for (int n = max(0, issued_v - 2); n < issued_v; ++n)
           mbar_wait(bar(BVF + n % 2), (n >> 1) & 1, &never, kDrainCycles);
       }
@@ -463,21 +478,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t idS = idesc_bf16(false, kBN), idPV = idesc_bf16(true, kD);
       bool ok = mbar_wait(bar(BQ), 0, abort_flag);
       fence_after();
+      // Shared-memory descriptors of the tile bases; a 16-byte multiple offset
+      // within shared memory adds (offset >> 4) to the address field, which
+      // cannot carry out of its 14 bits below 256 KB.
+      const uint64_t dq = smem_desc(sbase + SmemLayout::q, 16, 1024);
+      const uint64_t dk0 = smem_desc(sbase + SmemLayout::k, 16, 1024);
+      const uint64_t dv0 = smem_desc(sbase + SmemLayout::v, kKVHalf, 1024);
       auto issue_s = [&](int n) -> bool {
-        const int s = n % 2;
-        if (!mbar_wait(bar(BKF + s), (n >> 1) & 1, abort_flag)) return false;
+        const int s = n % 2, ks = n % kKStages;
+        if (!mbar_wait(bar(BKF + ks), (n / kKStages) & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t ksm = sbase + SmemLayout::k + s * kKVBytes;
-        const uint32_t qsm = sbase + SmemLayout::q;
+        const uint64_t dk = dk0 + uint64_t((ks * kKVBytes) >> 4);
+        const uint32_t td = tmem + s * kBN;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
           const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-          umma_f16(tmem + s * kBN, smem_desc(qsm + qoff, 16, 1024), smem_desc(ksm + koff, 16, 1024), idS,
-                   kk > 0 ? 1u : 0u);
+          umma_f16(td, dq + (qoff >> 4), dk + (koff >> 4), idS, kk > 0 ? 1u : 0u);
         }
         umma_commit(bar(BSF + s));
-        umma_commit(bar(BKE + s));
+        umma_commit(bar(BKE + ks));
         return true;
       };
       auto issue_pv = [&](int m) -> bool {
@@ -485,14 +505,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(bar(BVF + s), (m >> 1) & 1, abort_flag)) return false;
         if (!mbar_wait(bar(BPF + s), (m >> 1) & 1, abort_flag)) return false;
         fence_after();
-        const uint32_t vsm = sbase + SmemLayout::v + s * kKVBytes;
+        const uint64_t dv = dv0 + uint64_t((s * kKVBytes) >> 4);
         const uint32_t pt = tmem + s * kBN;  // P(m): bf16 pairs in the first 32 columns of S buffer m % 2
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t bd = smem_desc(vsm + kk * 2048, kKVHalf, 1024);
-          umma_f16_ts(tm_o, pt + kk * 8, bd, idPV, (m > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(BVE + s));
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_f16_ts(tm_o, pt + kk * 8, dv + uint64_t((kk * 2048) >> 4), idPV, (m > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar(BPV + s));
         return true;
       };
@@ -522,9 +539,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int mrow = min(qt * mrows + r / rows_per_blk, prm.nblk - 1);
     const uint32_t *rowbits = prm.bits + ((int64_t(b) * prm.H + h) * prm.nblk + mrow) * prm.W;
     const float2 sc2 = make_float2(prm.scale_log2, prm.scale_log2);
+    TileCursor cur(words);
     for (int n = 0; n < ntiles; ++n) {
       const int sb = n % 2;
-      const int j = list[n];
+      const int j = cur.next();
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
       fence_after();
       const uint32_t s_addr = tmem + sb * kBN + lane_off;
@@ -776,6 +794,9 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
     p.status = static_cast<int *>(sink);
   }
   FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes));
+  // the largest shared-memory carveout, so that two CTAs fit on an SM
+  FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 int(cudaSharedmemCarveoutMaxShared)));
   const unsigned grid = unsigned(B * H * nq);
   sparse_attn_kernel<<<grid, kThreads, SmemLayout::bytes, stream>>>(mq, mk, mv, p);
   FFTS_CUDA(cudaGetLastError());
