@@ -190,6 +190,196 @@ __device__ void fft_partial_body(const T *__restrict__ qb, const T *__restrict__
 
 static size_t fft_partial_smem(int M, int nf) { return size_t(M / 2 + M / 2 + 2 + size_t(nf) * M) * sizeof(float2); }
 
+// ------------------------------------------------- register-resident FFT
+// The same radix-2 decimation-in-time transforms and cross spectra as
+// fft_partial_body (identical butterflies, twiddles and channel order, so the
+// partial spectra are bit-identical), for M = 32 * R <= 2048 points held in
+// registers: one warp per channel, element i of the bit-reversed sequence in
+// lane i / R, register i % R.  Spans h < R pair registers of one lane; the five
+// spans h >= R pair lanes (shuffles).  One CTA of 8 warps takes one (b, h,
+// 8-channel chunk); the channels' cross spectra are summed in channel order
+// through shared memory.  Twiddles are re-laid per span so that the lanes of a
+// warp read them from consecutive shared-memory words.
+__host__ __device__ constexpr int rev_bits(int x, int n) {
+  int y = 0;
+  for (int i = 0; i < n; ++i) y |= ((x >> i) & 1) << (n - 1 - i);
+  return y;
+}
+__host__ __device__ constexpr int log2_exact(int x) { return x <= 1 ? 0 : 1 + log2_exact(x >> 1); }
+
+__device__ __forceinline__ void butterfly(float &ar, float &ai, float &br, float &bi, float2 w) {
+  const float p1 = __fmul_rn(w.x, br), p2 = __fmul_rn(w.y, bi);
+  const float p3 = __fmul_rn(w.x, bi), p4 = __fmul_rn(w.y, br);
+  const float tr = __fsub_rn(p1, p2), ti = __fadd_rn(p3, p4);
+  br = __fsub_rn(ar, tr);
+  bi = __fsub_rn(ai, ti);
+  ar = __fadd_rn(ar, tr);
+  ai = __fadd_rn(ai, ti);
+}
+
+template <int R>
+constexpr size_t fft_warp_smem(int N, size_t elem) {
+  const size_t stage = size_t(2) * kDChunk * size_t(N) * elem;
+  const size_t sums = size_t(kDChunk) * R * 17 * sizeof(float2);
+  return size_t(32 * R) * sizeof(float2) + (stage > sums ? stage : sums);
+}
+
+template <typename T, int R>
+__global__ void __launch_bounds__(256, 1) fft_warp_kernel(const T *__restrict__ qb, const T *__restrict__ kb, int H,
+                                                          int Hkv, int N, int D, int nchunk,
+                                                          float2 *__restrict__ partial) {
+  constexpr int LR = log2_exact(R);
+  constexpr int M = 32 * R;
+  constexpr int F = M / 2 + 1;
+  constexpr int PS = R * 17;  // padded per-channel stride of the cross-spectrum buffer
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float2 *tin = reinterpret_cast<float2 *>(smem_raw);  // [R]: span h < R, index h + k
+  float2 *tx = tin + R;                                 // [31 R]: span R << j at R (2^j - 1), index r 2^j + m
+  unsigned char *uni = reinterpret_cast<unsigned char *>(tx + 31 * R);
+  T *qs = reinterpret_cast<T *>(uni);                   // [8][N] staged channels (then reused)
+  T *ks = qs + kDChunk * N;
+  float2 *cs = reinterpret_cast<float2 *>(uni);         // [8][R][17] cross spectra
+  const int chunk = blockIdx.x % nchunk, bh = blockIdx.x / nchunk;
+  const int b = bh / H, h = bh % H;
+  const T *q = qb + int64_t(bh) * N * D + chunk * kDChunk;
+  const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D + chunk * kDChunk;
+  constexpr int stride = kMaxFFT / M;
+  for (int e = threadIdx.x; e < R; e += blockDim.x) {
+    if (e >= 1) {
+      const int hh = 1 << (31 - __clz(e)), kk = e - hh;
+      tin[e] = g_twiddle[kk * (M / (2 * hh)) * stride];
+    }
+  }
+  for (int e = threadIdx.x; e < 31 * R; e += blockDim.x) {
+    const int j = 31 - __clz(e / R + 1);
+    const int loc = e - R * ((1 << j) - 1);
+    const int r = loc >> j, m = loc & ((1 << j) - 1);
+    tx[e] = g_twiddle[(r + R * m) * (M / (2 * (R << j))) * stride];
+  }
+  // stage the chunk's 8 channels of q and k, channel-major
+  constexpr int V = Elem<T>::kVec;
+  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+#pragma unroll
+    for (int c0 = 0; c0 < kDChunk; c0 += V) {
+      const uint4 qv = *reinterpret_cast<const uint4 *>(q + int64_t(t) * D + c0);
+      const uint4 kv = *reinterpret_cast<const uint4 *>(k + int64_t(t) * D + c0);
+      const T *qe = reinterpret_cast<const T *>(&qv);
+      const T *ke = reinterpret_cast<const T *>(&kv);
+#pragma unroll
+      for (int c = 0; c < V; ++c) {
+        qs[(c0 + c) * N + t] = qe[c];
+        ks[(c0 + c) * N + t] = ke[c];
+      }
+    }
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lb = __brev(uint32_t(lane)) >> 27;
+  float re[R], im[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int t = (rev_bits(r, LR) << 5) | lb;  // bit reversal of i = lane * R + r
+    re[r] = t < N ? Elem<T>::to_f32(qs[warp * N + t]) : 0.0f;
+    im[r] = t < N ? Elem<T>::to_f32(ks[warp * N + t]) : 0.0f;
+  }
+  __syncthreads();  // the staging buffer becomes the cross-spectrum buffer
+#pragma unroll
+  for (int sp = 0; sp < LR; ++sp) {
+    const int hh = 1 << sp;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (!(r & hh)) butterfly(re[r], im[r], re[r + hh], im[r + hh], tin[hh + (r & (hh - 1))]);
+  }
+#pragma unroll
+  for (int j = 0; j < 5; ++j) {
+    const int hl = 1 << j;
+    const bool upper = lane & hl;
+    const int m = lane & (hl - 1);
+    const float2 *tw = tx + R * (hl - 1);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float sr = re[r], si = im[r];
+      if (upper) {
+        const float2 w = tw[r * hl + m];
+        const float p1 = __fmul_rn(w.x, sr), p2 = __fmul_rn(w.y, si);
+        const float p3 = __fmul_rn(w.x, si), p4 = __fmul_rn(w.y, sr);
+        sr = __fsub_rn(p1, p2);
+        si = __fadd_rn(p3, p4);
+      }
+      const float rr = __shfl_xor_sync(0xffffffffu, sr, hl);
+      const float ri = __shfl_xor_sync(0xffffffffu, si, hl);
+      if (upper) {
+        re[r] = __fsub_rn(rr, sr);
+        im[r] = __fsub_rn(ri, si);
+      } else {
+        re[r] = __fadd_rn(sr, rr);
+        im[r] = __fadd_rn(si, ri);
+      }
+    }
+  }
+  // X[f] sits at f = lane * R + r; its mirror (M - f) mod M at lane 31 - lane,
+  // register R - r (r > 0), or lane (32 - lane) mod 32, register 0 (r = 0)
+  float2 *cw = cs + warp * PS;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int src = r == 0 ? ((32 - lane) & 31) : 31 - lane;
+    const float br = __shfl_sync(0xffffffffu, re[r == 0 ? 0 : R - r], src);
+    const float bi = __shfl_sync(0xffffffffu, im[r == 0 ? 0 : R - r], src);
+    if (lane < 16 || (lane == 16 && r == 0)) {
+      const float qr = __fmul_rn(0.5f, __fadd_rn(re[r], br));
+      const float qi = __fmul_rn(0.5f, __fsub_rn(im[r], bi));
+      const float kr = __fmul_rn(0.5f, __fadd_rn(im[r], bi));
+      const float ki = __fmul_rn(0.5f, __fsub_rn(br, re[r]));
+      const float cr = __fadd_rn(__fmul_rn(qr, kr), __fmul_rn(qi, ki));
+      const float ci = __fsub_rn(__fmul_rn(qi, kr), __fmul_rn(qr, ki));
+      cw[r * 17 + lane] = make_float2(cr, ci);
+    }
+  }
+  __syncthreads();
+  float2 *out = partial + (int64_t(bh) * nchunk + chunk) * F;
+  for (int pos = threadIdx.x; pos < PS; pos += blockDim.x) {
+    const int r = pos / 17, L = pos - r * 17;
+    if (L == 16 && r != 0) continue;
+    float2 a = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int w = 0; w < kDChunk; ++w) {
+      const float2 c = cs[w * PS + pos];
+      a.x = __fadd_rn(a.x, c.x);
+      a.y = __fadd_rn(a.y, c.y);
+    }
+    out[L * R + r] = a;
+  }
+}
+
+template <typename T>
+static int launch_fft_warp(const T *qb, const T *kb, int64_t B, int64_t H, int64_t Hkv, int N, int64_t D, int M,
+                           int nchunk, float2 *partial, cudaStream_t stream) {
+  const unsigned grid = unsigned(B * H * nchunk);
+#define FFTS_FFT_CASE(RR)                                                                                       \
+  case 32 * RR: {                                                                                               \
+    const size_t smem = fft_warp_smem<RR>(N, sizeof(T));                                                        \
+    FFTS_CUDA(cudaFuncSetAttribute(fft_warp_kernel<T, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))); \
+    fft_warp_kernel<T, RR><<<grid, 256, smem, stream>>>(qb, kb, int(H), int(Hkv), N, int(D), nchunk, partial);  \
+    break;                                                                                                      \
+  }
+  switch (M) {
+    FFTS_FFT_CASE(1)
+    FFTS_FFT_CASE(2)
+    FFTS_FFT_CASE(4)
+    FFTS_FFT_CASE(8)
+    FFTS_FFT_CASE(16)
+    FFTS_FFT_CASE(32)
+    FFTS_FFT_CASE(64)
+    default:
+      set_error(FFTS_E_INVALID, "register FFT: unsupported length %d", M);
+      return FFTS_E_INVALID;
+  }
+#undef FFTS_FFT_CASE
+  FFTS_CUDA(cudaGetLastError());
+  return FFTS_OK;
+}
+
+
 // ------------------------------------------------------- block selection
 // Ascending-rank selection of 32-bit keys (keys[0..n)) by 8-bit radix passes.
 __device__ uint32_t block_select_rank(const uint32_t *keys, int n, int rank, int *hist, int *bc) {
@@ -570,13 +760,15 @@ static size_t colrow_smem(int N, int D) {
 
 // Stage 1 of the selection: every independent per-head job of the path in one
 // launch, so that these small latency-bound jobs run side by side across the
-// SMs: blocks [0, nF) compute FFT partial spectra (one per (b, h, 8-channel
-// chunk)), blocks [nF, nF+nD) the per-lag stripe statistics (one per (b, h,
-// sampled lag)), and the last B*H blocks the column and last-row selections.
+// SMs.  The longest jobs come first: blocks [0, BH) the column and last-row
+// selections (one per (b, h)), blocks [BH, BH+nD) the per-lag stripe statistics
+// (one per (b, h, sampled lag)), and the last nF blocks FFT partial spectra
+// (one per (b, h, 8-channel chunk); nF = 0 when the register FFT kernel runs
+// them instead).
 template <typename T>
 __global__ void __launch_bounds__(256) select_stage1_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
                                                             int H, int Hkv, int D, ffts_mask_params p, int M,
-                                                            int nf, int nchunk, int nF, int nD,
+                                                            int nf, int nchunk, int nBH, int nD,
                                                             float2 *__restrict__ partial, double *__restrict__ nv,
                                                             uint32_t *__restrict__ colsel,
                                                             uint32_t *__restrict__ lastsel) {
@@ -584,14 +776,15 @@ __global__ void __launch_bounds__(256) select_stage1_kernel(const T *__restrict_
   __shared__ int hist[256];
   __shared__ int bc[4];
   const int bid = blockIdx.x;
-  if (bid < nF) {
-    fft_partial_body<T>(qb, kb, H, Hkv, p.n_blocks, D, M, nf, partial, bid % nchunk, nchunk, bid / nchunk,
-                        smem_raw);
-  } else if (bid < nF + nD) {
-    const int e = bid - nF;
+  if (bid < nBH) {
+    colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid, smem_raw, hist, bc);
+  } else if (bid < nBH + nD) {
+    const int e = bid - nBH;
     diag_stats_body<T>(qb, kb, H, Hkv, D, p, nv, e % p.n_diag_samples, e / p.n_diag_samples, smem_raw);
   } else {
-    colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid - nF - nD, smem_raw, hist, bc);
+    const int f = bid - nBH - nD;
+    fft_partial_body<T>(qb, kb, H, Hkv, p.n_blocks, D, M, nf, partial, f % nchunk, nchunk, f / nchunk,
+                        smem_raw);
   }
 }
 
@@ -832,14 +1025,20 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   // stage 1: FFT partial spectra, per-lag stripe statistics, column and last-row selections
   int nf = kDChunk;
   while (nf > 1 && fft_partial_smem(M, nf) > 64 * 1024) nf >>= 1;
-  const int nF = p.corr_on ? nchunk * int(BH) : 0;
+  // spectra of up to 2048 points come from the register FFT kernel
+  const bool reg_fft = p.corr_on && M >= 32 && M <= 2048;
+  if (reg_fft) {
+    const int rc = launch_fft_warp(qb, kb, B, H, Hkv, N, D, M, nchunk, ws.partial, stream);
+    if (rc) return rc;
+  }
+  const int nF = (p.corr_on && !reg_fft) ? nchunk * int(BH) : 0;
   const int nD = (p.corr_on && !p.stripe_all_diffuse) ? p.n_diag_samples * int(BH) : 0;
   size_t smem1 = colrow_smem(N, int(D));
   if (nF) smem1 = std::max(smem1, fft_partial_smem(M, nf));
   if (nD) smem1 = std::max(smem1, diag_stats_smem(N));
   FFTS_CUDA(cudaFuncSetAttribute(select_stage1_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
   select_stage1_kernel<T><<<unsigned(nF + nD + BH), 256, smem1, stream>>>(
-      qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, nF, nD, ws.partial, ws.nv, ws.colsel, ws.lastsel);
+      qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, int(BH), nD, ws.partial, ws.nv, ws.colsel, ws.lastsel);
   FFTS_CUDA(cudaGetLastError());
   // stage 2: stripe decision, inverse FFT, lag selection
   const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
