@@ -217,29 +217,26 @@ __device__ __forceinline__ void butterfly(float &ar, float &ai, float &br, float
   ai = __fadd_rn(ai, ti);
 }
 
-template <int R>
-constexpr size_t fft_warp_smem(int N, size_t elem) {
+static size_t fft_warp_smem_rt(int R, int N, size_t elem) {
   const size_t stage = size_t(2) * kDChunk * size_t(N) * elem;
   const size_t sums = size_t(kDChunk) * R * 17 * sizeof(float2);
   return size_t(32 * R) * sizeof(float2) + (stage > sums ? stage : sums);
 }
 
 template <typename T, int R>
-__global__ void __launch_bounds__(256, 1) fft_warp_kernel(const T *__restrict__ qb, const T *__restrict__ kb, int H,
-                                                          int Hkv, int N, int D, int nchunk,
-                                                          float2 *__restrict__ partial) {
+__device__ void fft_warp_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int N, int D,
+                              int nchunk, float2 *__restrict__ partial, int f, unsigned char *smem_raw) {
   constexpr int LR = log2_exact(R);
   constexpr int M = 32 * R;
   constexpr int F = M / 2 + 1;
   constexpr int PS = R * 17;  // padded per-channel stride of the cross-spectrum buffer
-  extern __shared__ __align__(16) unsigned char smem_raw[];
   float2 *tin = reinterpret_cast<float2 *>(smem_raw);  // [R]: span h < R, index h + k
   float2 *tx = tin + R;                                 // [31 R]: span R << j at R (2^j - 1), index r 2^j + m
   unsigned char *uni = reinterpret_cast<unsigned char *>(tx + 31 * R);
   T *qs = reinterpret_cast<T *>(uni);                   // [8][N] staged channels (then reused)
   T *ks = qs + kDChunk * N;
   float2 *cs = reinterpret_cast<float2 *>(uni);         // [8][R][17] cross spectra
-  const int chunk = blockIdx.x % nchunk, bh = blockIdx.x / nchunk;
+  const int chunk = f % nchunk, bh = f / nchunk;
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D + chunk * kDChunk;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D + chunk * kDChunk;
@@ -351,33 +348,6 @@ __global__ void __launch_bounds__(256, 1) fft_warp_kernel(const T *__restrict__ 
   }
 }
 
-template <typename T>
-static int launch_fft_warp(const T *qb, const T *kb, int64_t B, int64_t H, int64_t Hkv, int N, int64_t D, int M,
-                           int nchunk, float2 *partial, cudaStream_t stream) {
-  const unsigned grid = unsigned(B * H * nchunk);
-#define FFTS_FFT_CASE(RR)                                                                                       \
-  case 32 * RR: {                                                                                               \
-    const size_t smem = fft_warp_smem<RR>(N, sizeof(T));                                                        \
-    FFTS_CUDA(cudaFuncSetAttribute(fft_warp_kernel<T, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem))); \
-    fft_warp_kernel<T, RR><<<grid, 256, smem, stream>>>(qb, kb, int(H), int(Hkv), N, int(D), nchunk, partial);  \
-    break;                                                                                                      \
-  }
-  switch (M) {
-    FFTS_FFT_CASE(1)
-    FFTS_FFT_CASE(2)
-    FFTS_FFT_CASE(4)
-    FFTS_FFT_CASE(8)
-    FFTS_FFT_CASE(16)
-    FFTS_FFT_CASE(32)
-    FFTS_FFT_CASE(64)
-    default:
-      set_error(FFTS_E_INVALID, "register FFT: unsupported length %d", M);
-      return FFTS_E_INVALID;
-  }
-#undef FFTS_FFT_CASE
-  FFTS_CUDA(cudaGetLastError());
-  return FFTS_OK;
-}
 
 
 // ------------------------------------------------------- block selection
@@ -632,159 +602,298 @@ __device__ double lane_tree(double v, double *part) {
 }
 
 // ------------------------------------------------------- stripe statistic
-// One CTA per (sampled lag, b, h): the normalised variance of the adjacent
-// differences along one block-score diagonal (my_attn_v7.py:342-351), written to
-// nv[bh * S + s].  corr_select_kernel averages the S values in sample order.
+// One CTA per (b, h, group of sampled lags whose lags lie within kDiagSpan
+// blocks of each other): the normalised variance of the adjacent differences
+// along each sampled block-score diagonal (my_attn_v7.py:342-351), written to
+// nv[bh * 64 + s]; corr_select_kernel averages them in sample order.  The k rows
+// of a 64-row tile and the q rows every lag of the group pairs them with are
+// staged in shared memory once per tile; each score is one fp64 FMA chain in d
+// order and the three reductions per lag are the 256-lane canonical ones.
+constexpr int kDiagTile = 64;
+constexpr int kDiagGroup = 8;
+
+// row stride (elements) of staged rows: an odd number of 32-bit words
 template <typename T>
-__device__ void diag_stats_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
-                                const ffts_mask_params &p, double *__restrict__ nv, int s, int bh,
-                                unsigned char *smem_raw) {
+__host__ __device__ constexpr int stage_stride(int D) { return D + (sizeof(T) == 2 ? 2 : 1); }
+
+struct DiagGroups {
+  int n;                     // groups per (b, h)
+  unsigned char first[64];   // first sample index of each group
+  unsigned char count[64];   // samples in each group
+};
+
+template <typename T>
+__device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
+                                const ffts_mask_params &p, double *__restrict__ nv, int first, int G, int bh,
+                                int gmax, unsigned char *smem_raw) {
   const int N = p.n_blocks;
-  double *part = reinterpret_cast<double *>(smem_raw);  // [256]
-  float *vals = reinterpret_cast<float *>(part + kLanes);  // [N]
+  const int QS = stage_stride<T>(D);
+  const int tid = threadIdx.x;
+  int lo = p.diag_taus[first], hi = lo;
+  for (int g = 1; g < G; ++g) {
+    lo = min(lo, p.diag_taus[first + g]);
+    hi = max(hi, p.diag_taus[first + g]);
+  }
+  const int wrows = kDiagTile + (hi - lo);
+  T *ks = reinterpret_cast<T *>(smem_raw);           // [kDiagTile][QS]
+  T *qw = ks + kDiagTile * QS;                        // [wrows][QS]
+  float *vals = reinterpret_cast<float *>(smem_raw + ((size_t(kDiagTile + wrows) * QS * sizeof(T) + 15) & ~size_t(15)));
+  double *part = reinterpret_cast<double *>(vals + gmax * N);  // [gmax][256]
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
   const double sqrtD = sqrt((double)D);
-  const int tau = p.diag_taus[s];
-  const int m = N - tau - 1, n = m - 1;
-  for (int t = threadIdx.x; t < m; t += blockDim.x)
-    vals[t] = __double2float_rn(__ddiv_rn(dot64_rows(q + int64_t(t + tau) * D, k + int64_t(t) * D, D), sqrtD));
-  __syncthreads();
-  double var;
-  if (n >= 2) {
-    double a = 0.0;
-    for (int e = threadIdx.x; e < n; e += blockDim.x) a = __dadd_rn(a, (double)__fsub_rn(vals[e + 1], vals[e]));
-    const double mean = __ddiv_rn(lane_tree(a, part), (double)n);
-    a = 0.0;
-    for (int e = threadIdx.x; e < n; e += blockDim.x) {
-      const double dv = __dsub_rn((double)__fsub_rn(vals[e + 1], vals[e]), mean);
-      a = __dadd_rn(a, __dmul_rn(dv, dv));
+  constexpr int V = Elem<T>::kVec;
+  const int vrow = D / V;
+  const int mmax = N - lo - 1;
+  for (int t0 = 0; t0 < mmax; t0 += kDiagTile) {
+    // k rows [t0, t0 + 64) and q rows [t0 + lo, t0 + hi + 64)
+    for (int idx = tid; idx < (kDiagTile + wrows) * vrow; idx += blockDim.x) {
+      const int rr = idx / vrow, v = idx - rr * vrow;
+      const bool isk = rr < kDiagTile;
+      const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
+      T *dst = isk ? ks + rr * QS : qw + (rr - kDiagTile) * QS;
+      if (row < N) {
+        const uint4 raw = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(row) * D + v * V);
+        const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+        for (int c = 0; c < V; ++c) dst[v * V + c] = e[c];
+      }
     }
-    var = __ddiv_rn(lane_tree(a, part), (double)(n - 1));
-  } else {
-    var = __longlong_as_double(0x7ff8000000000000ll);
+    __syncthreads();
+    for (int idx = tid; idx < G * kDiagTile; idx += 2 * blockDim.x) {
+      // two (lag, row) pairs per pass: idx and idx + blockDim.x
+      const int idx2 = idx + blockDim.x;
+      const int g1 = idx / kDiagTile, t1 = t0 + idx % kDiagTile;
+      const int g2 = idx2 / kDiagTile, t2 = t0 + idx2 % kDiagTile;
+      const int tau1 = p.diag_taus[first + g1];
+      const bool v1 = t1 < N - tau1 - 1;
+      const bool v2 = idx2 < G * kDiagTile && t2 < N - p.diag_taus[first + min(g2, G - 1)] - 1;
+      const int tau2 = v2 ? p.diag_taus[first + g2] : tau1;
+      const T *qa = qw + (t1 + tau1 - t0 - lo) * QS, *ka = ks + (t1 - t0) * QS;
+      const T *qb2 = qw + ((v2 ? t2 : t1) + tau2 - t0 - lo) * QS, *kb2 = ks + ((v2 ? t2 : t1) - t0) * QS;
+      double a1 = 0.0, a2 = 0.0;
+      for (int d = 0; d < D; ++d) {
+        a1 = __fma_rn((double)Elem<T>::to_f32(qa[d]), (double)Elem<T>::to_f32(ka[d]), a1);
+        a2 = __fma_rn((double)Elem<T>::to_f32(qb2[d]), (double)Elem<T>::to_f32(kb2[d]), a2);
+      }
+      if (v1) vals[g1 * N + t1] = __double2float_rn(__ddiv_rn(a1, sqrtD));
+      if (v2) vals[g2 * N + t2] = __double2float_rn(__ddiv_rn(a2, sqrtD));
+    }
+    __syncthreads();
   }
-  double a = 0.0;
-  for (int e = threadIdx.x; e < m; e += blockDim.x) a = __dadd_rn(a, fabs((double)vals[e]));
-  const double sabs = lane_tree(a, part);
-  double mabs = m > 0 ? __ddiv_rn(sabs, (double)m) : __longlong_as_double(0x7ff8000000000000ll);
-  const double floor6 = (double)1e-6f;
-  if (mabs < floor6) mabs = floor6;
-  if (threadIdx.x == 0) nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s] = __ddiv_rn(var, mabs);
+  // three canonical reductions per lag, the G lags side by side
+  auto tree = [&](double *a) {
+    for (int g = 0; g < G; ++g) part[g * kLanes + tid] = a[g];
+    __syncthreads();
+    for (int st = kLanes / 2; st >= 1; st >>= 1) {
+      for (int idx = tid; idx < G * st; idx += blockDim.x) {
+        const int g = idx / st, i = idx - g * st;
+        part[g * kLanes + i] = __dadd_rn(part[g * kLanes + i], part[g * kLanes + i + st]);
+      }
+      __syncthreads();
+    }
+    for (int g = 0; g < G; ++g) a[g] = part[g * kLanes];
+    __syncthreads();
+  };
+  double acc[kDiagGroup], mean[kDiagGroup], var[kDiagGroup];
+  for (int g = 0; g < G; ++g) {
+    const int n = N - p.diag_taus[first + g] - 2;
+    acc[g] = 0.0;
+    for (int e = tid; e < n; e += blockDim.x)
+      acc[g] = __dadd_rn(acc[g], (double)__fsub_rn(vals[g * N + e + 1], vals[g * N + e]));
+  }
+  tree(acc);
+  for (int g = 0; g < G; ++g) {
+    const int n = N - p.diag_taus[first + g] - 2;
+    mean[g] = n >= 2 ? __ddiv_rn(acc[g], (double)n) : 0.0;
+    acc[g] = 0.0;
+    for (int e = tid; e < n; e += blockDim.x) {
+      const double dv = __dsub_rn((double)__fsub_rn(vals[g * N + e + 1], vals[g * N + e]), mean[g]);
+      acc[g] = __dadd_rn(acc[g], __dmul_rn(dv, dv));
+    }
+  }
+  tree(acc);
+  for (int g = 0; g < G; ++g) {
+    const int n = N - p.diag_taus[first + g] - 2;
+    var[g] = n >= 2 ? __ddiv_rn(acc[g], (double)(n - 1)) : __longlong_as_double(0x7ff8000000000000ll);
+    const int m = n + 1;
+    acc[g] = 0.0;
+    for (int e = tid; e < m; e += blockDim.x) acc[g] = __dadd_rn(acc[g], fabs((double)vals[g * N + e]));
+  }
+  tree(acc);
+  if (tid == 0) {
+    const double floor6 = (double)1e-6f;
+    for (int g = 0; g < G; ++g) {
+      const int m = N - p.diag_taus[first + g] - 1;
+      double mabs = m > 0 ? __ddiv_rn(acc[g], (double)m) : __longlong_as_double(0x7ff8000000000000ll);
+      if (mabs < floor6) mabs = floor6;
+      nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + first + g] = __ddiv_rn(var[g], mabs);
+    }
+  }
 }
 
-static size_t diag_stats_smem(int N) { return size_t(kLanes) * 8 + size_t(N) * 4; }
+// Consecutive sampled lags grouped while their spread stays within the span the
+// staged q window covers and the lag values fit in shared memory.
+static DiagGroups make_diag_groups(const ffts_mask_params &p, int gmax, int span) {
+  DiagGroups gr{};
+  int s = 0;
+  while (s < p.n_diag_samples) {
+    int lo = p.diag_taus[s], hi = lo, c = 1;
+    while (s + c < p.n_diag_samples && c < gmax) {
+      const int t = p.diag_taus[s + c];
+      if (std::max(hi, t) - std::min(lo, t) > span) break;
+      lo = std::min(lo, t);
+      hi = std::max(hi, t);
+      ++c;
+    }
+    gr.first[gr.n] = (unsigned char)s;
+    gr.count[gr.n] = (unsigned char)c;
+    ++gr.n;
+    s += c;
+  }
+  return gr;
+}
 
 // ------------------------------------------------------------ head stats
 // Hot key columns (create_column_block_mask, my_attn_v7.py:403-437) and the last
 // query row's top-k (create_last_block_query_mask, :54-72) of one (b, h).
-// Column scores are produced for every head; the mask composition applies them
-// only where the reference does (stripe heads, or all heads without the lag mask).
-// The suffix sums over q run from row N-2 downwards in 32-row chunks staged
-// through shared memory (row strides padded by one element against bank
-// conflicts); each column's dot product is one fp64 FMA chain in d order.
+// Column scores are produced whenever the column mask is on; the mask
+// composition applies them only where the reference does (stripe heads, or all
+// heads without the lag mask).  The q and k rows are staged from row N-1
+// downwards in chunks of C rows (16-byte loads, odd-word row strides); the
+// suffix sums over q (rows <= N-2, fp64, in row order from N-2 down) are kept
+// per channel by D threads and stored per row; then one thread per row forms
+// the column score (fp64 FMA chain over d) while another forms the last query
+// row's score against the same staged k row.
+__host__ __device__ constexpr size_t colrow_smem_for(int C, int N, int D, int elem) {
+  return ((2 * size_t(C) * size_t(D + (elem == 2 ? 2 : 1)) * elem + 15) & ~size_t(15)) + size_t(C) * (D + 1) * 8 +
+         size_t(D) * 8 + size_t(N) * 8 + size_t((N + 31) / 32) * 4 + 16;
+}
+
+// rows per chunk: the largest of 128, 64, 32 whose buffers fit in 200 KB
+__host__ __device__ constexpr int colrow_rows(int N, int D, int elem) {
+  return colrow_smem_for(128, N, D, elem) <= 200 * 1024 ? 128 : (colrow_smem_for(64, N, D, elem) <= 200 * 1024 ? 64 : 32);
+}
+
+static size_t colrow_smem(int N, int D, size_t elem) {
+  return colrow_smem_for(colrow_rows(N, D, int(elem)), N, D, int(elem));
+}
+
 template <typename T>
 __device__ void colrow_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
                             const ffts_mask_params &p, uint32_t *__restrict__ colsel,
                             uint32_t *__restrict__ lastsel, int bh, unsigned char *smem_raw, int *hist, int *bc) {
   const int N = p.n_blocks;
   const int W = (N + 31) / 32;
-  const int QS = D + 1;  // padded row stride (elements)
-  float *qs = reinterpret_cast<float *>(smem_raw);      // [32][QS]
-  float *ks = qs + 32 * QS;                             // [32][QS]
-  double *pch = reinterpret_cast<double *>(ks + 32 * QS + (32 * QS & 1));  // [32][QS], 8-byte aligned
-  float *vals = reinterpret_cast<float *>(pch + 32 * QS);  // [N]
-  uint32_t *keys = reinterpret_cast<uint32_t *>(vals + N);  // [N]
-  uint32_t *words = keys + N;                               // [W]
+  const int C = colrow_rows(N, D, int(sizeof(T)));
+  const int QS = stage_stride<T>(D);
+  const int PS = D + 1;
+  const int tid = threadIdx.x;
+  T *qs = reinterpret_cast<T *>(smem_raw);                       // [C][QS]
+  T *ks = qs + C * QS;                                            // [C][QS]
+  double *pch = reinterpret_cast<double *>(smem_raw + ((2 * size_t(C) * QS * sizeof(T) + 15) & ~size_t(15)));
+  double *ql = pch + C * PS;                                      // [D] last q row
+  uint32_t *ckeys = reinterpret_cast<uint32_t *>(ql + D);         // [N]
+  uint32_t *lkeys = ckeys + N;                                    // [N]
+  uint32_t *words = lkeys + N;                                    // [W]
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
   const double sqrtD = sqrt((double)D);
+  const bool col = p.col_on && p.col_end > p.col_start;
+  const bool last = p.last_on != 0;
+  constexpr int V = Elem<T>::kVec;
+  const int vrow = D / V;
 
-  for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
-  __syncthreads();
-  if (p.col_on && p.col_end > p.col_start) {
-    double P = 0.0;
-    for (int jhi = N - 1; jhi >= 0; jhi -= 32) {
-      const int rows = min(32, jhi + 1);
-      for (int e = threadIdx.x; e < rows * D; e += blockDim.x) {
-        const int t = e / D, dd = e - t * D;
-        const int64_t off = int64_t(jhi - t) * D + dd;
-        qs[t * QS + dd] = Elem<T>::to_f32(q[off]);
-        ks[t * QS + dd] = Elem<T>::to_f32(k[off]);
+  for (int d = tid; d < D; d += blockDim.x) ql[d] = (double)Elem<T>::to_f32(q[int64_t(N - 1) * D + d]);
+  double P = 0.0;  // suffix sum of channel tid (tid < D)
+  if (col || last) {
+    for (int jhi = N - 1; jhi >= 0; jhi -= C) {
+      const int rows = min(C, jhi + 1);
+      for (int idx = tid; idx < 2 * rows * vrow; idx += blockDim.x) {
+        const bool isk = idx >= rows * vrow;
+        const int i2 = isk ? idx - rows * vrow : idx;
+        const int t = i2 / vrow, v = i2 - t * vrow;
+        const uint4 raw = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(jhi - t) * D + v * V);
+        const T *e = reinterpret_cast<const T *>(&raw);
+        T *dst = (isk ? ks : qs) + t * QS + v * V;
+#pragma unroll
+        for (int c = 0; c < V; ++c) dst[c] = e[c];
       }
       __syncthreads();
-      if (threadIdx.x < D) {
+      if (col && tid < D) {
         for (int t = 0; t < rows; ++t) {
-          if (jhi - t <= N - 2) P = __dadd_rn(P, (double)qs[t * QS + threadIdx.x]);
-          pch[t * QS + threadIdx.x] = P;
+          if (jhi - t <= N - 2) P = __dadd_rn(P, (double)Elem<T>::to_f32(qs[t * QS + tid]));
+          pch[t * PS + tid] = P;
         }
       }
       __syncthreads();
-      if (threadIdx.x < rows) {
-        const int t = threadIdx.x, j = jhi - t;
-        double acc = 0.0;
-        for (int d = 0; d < D; ++d) acc = __fma_rn(pch[t * QS + d], (double)ks[t * QS + d], acc);
-        const int cnt = max(1, N - j - 1);
-        vals[j] = __double2float_rn(__ddiv_rn(__ddiv_rn(acc, sqrtD), (double)cnt));
+      // threads [0, C): column scores; threads [C, 2C): last-row scores
+      const int t = tid < C ? tid : tid - C;
+      if (t < rows && tid < 2 * C) {
+        const int j = jhi - t;
+        const T *kr = ks + t * QS;
+        if (tid < C) {
+          if (col) {
+            double acc = 0.0;
+            for (int d = 0; d < D; ++d) acc = __fma_rn(pch[t * PS + d], (double)Elem<T>::to_f32(kr[d]), acc);
+            const int cnt = max(1, N - j - 1);
+            ckeys[j] = f32_key(__double2float_rn(__ddiv_rn(__ddiv_rn(acc, sqrtD), (double)cnt)));
+          }
+        } else if (last) {
+          double acc = 0.0;
+          for (int d = 0; d < D; ++d) acc = __fma_rn(ql[d], (double)Elem<T>::to_f32(kr[d]), acc);
+          lkeys[j] = f32_key(Elem<T>::round_f32(__double2float_rn(acc)));
+        }
       }
       __syncthreads();
     }
-    for (int j = threadIdx.x; j < N; j += blockDim.x) keys[j] = f32_key(vals[j]);
-    __syncthreads();
-    block_topk_bits(keys, p.col_start, p.col_end, p.col_topk, words, hist, bc);
   }
+  for (int w = tid; w < W; w += blockDim.x) words[w] = 0;
   __syncthreads();
-  for (int w = threadIdx.x; w < W; w += blockDim.x) colsel[int64_t(bh) * W + w] = words[w];
+  if (col) block_topk_bits(ckeys, p.col_start, p.col_end, p.col_topk, words, hist, bc);
   __syncthreads();
-
-  for (int w = threadIdx.x; w < W; w += blockDim.x) words[w] = 0;
+  for (int w = tid; w < W; w += blockDim.x) colsel[int64_t(bh) * W + w] = words[w];
   __syncthreads();
-  if (p.last_on) {
-    for (int j = threadIdx.x; j < N; j += blockDim.x) {
-      const double sc = dot64_rows(q + int64_t(N - 1) * D, k + int64_t(j) * D, D);
-      keys[j] = f32_key(Elem<T>::round_f32(__double2float_rn(sc)));
-    }
-    __syncthreads();
-    block_topk_bits(keys, 0, N, p.last_topk, words, hist, bc);
-  }
+  for (int w = tid; w < W; w += blockDim.x) words[w] = 0;
   __syncthreads();
-  for (int w = threadIdx.x; w < W; w += blockDim.x) lastsel[int64_t(bh) * W + w] = words[w];
-}
-
-static size_t colrow_smem(int N, int D) {
-  const size_t QS = size_t(D) + 1;
-  return (64 * QS + 1) * 4 + 32 * QS * 8 + size_t(N) * 8 + size_t((N + 31) / 32) * 4 + 16;
+  if (last) block_topk_bits(lkeys, 0, N, p.last_topk, words, hist, bc);
+  __syncthreads();
+  for (int w = tid; w < W; w += blockDim.x) lastsel[int64_t(bh) * W + w] = words[w];
 }
 
 // Stage 1 of the selection: every independent per-head job of the path in one
 // launch, so that these small latency-bound jobs run side by side across the
 // SMs.  The longest jobs come first: blocks [0, BH) the column and last-row
-// selections (one per (b, h)), blocks [BH, BH+nD) the per-lag stripe statistics
-// (one per (b, h, sampled lag)), and the last nF blocks FFT partial spectra
-// (one per (b, h, 8-channel chunk); nF = 0 when the register FFT kernel runs
-// them instead).
-template <typename T>
-__global__ void __launch_bounds__(256) select_stage1_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
-                                                            int H, int Hkv, int D, ffts_mask_params p, int M,
-                                                            int nf, int nchunk, int nBH, int nD,
-                                                            float2 *__restrict__ partial, double *__restrict__ nv,
-                                                            uint32_t *__restrict__ colsel,
-                                                            uint32_t *__restrict__ lastsel) {
+// selections (one per (b, h)), the next BH * groups the stripe statistics of
+// groups of sampled lags, and the last nF blocks the FFT partial spectra (one
+// per (b, h, 8-channel chunk)): the register FFT for R = M / 32 > 0, else the
+// shared-memory FFT.
+template <typename T, int R>
+__global__ void __launch_bounds__(256, 1) select_stage1_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
+                                                               int H, int Hkv, int D, ffts_mask_params p, int M,
+                                                               int nf, int nchunk, int nBH, int nDG,
+                                                               DiagGroups gr, int gmax,
+                                                               float2 *__restrict__ partial, double *__restrict__ nv,
+                                                               uint32_t *__restrict__ colsel,
+                                                               uint32_t *__restrict__ lastsel) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ int hist[256];
   __shared__ int bc[4];
   const int bid = blockIdx.x;
   if (bid < nBH) {
     colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid, smem_raw, hist, bc);
-  } else if (bid < nBH + nD) {
-    const int e = bid - nBH;
-    diag_stats_body<T>(qb, kb, H, Hkv, D, p, nv, e % p.n_diag_samples, e / p.n_diag_samples, smem_raw);
+  } else if (bid < nBH + nDG) {
+    const int e = bid - nBH, g = e % gr.n;
+    diag_group_body<T>(qb, kb, H, Hkv, D, p, nv, gr.first[g], gr.count[g], e / gr.n, gmax, smem_raw);
   } else {
-    const int f = bid - nBH - nD;
-    fft_partial_body<T>(qb, kb, H, Hkv, p.n_blocks, D, M, nf, partial, f % nchunk, nchunk, f / nchunk,
-                        smem_raw);
+    const int f = bid - nBH - nDG;
+    if constexpr (R > 0)
+      fft_warp_body<T, R>(qb, kb, H, Hkv, p.n_blocks, D, nchunk, partial, f, smem_raw);
+    else
+      fft_partial_body<T>(qb, kb, H, Hkv, p.n_blocks, D, M, nf, partial, f % nchunk, nchunk, f / nchunk,
+                          smem_raw);
   }
 }
 
@@ -1025,20 +1134,42 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   // stage 1: FFT partial spectra, per-lag stripe statistics, column and last-row selections
   int nf = kDChunk;
   while (nf > 1 && fft_partial_smem(M, nf) > 64 * 1024) nf >>= 1;
-  // spectra of up to 2048 points come from the register FFT kernel
-  const bool reg_fft = p.corr_on && M >= 32 && M <= 2048;
-  if (reg_fft) {
-    const int rc = launch_fft_warp(qb, kb, B, H, Hkv, N, D, M, nchunk, ws.partial, stream);
-    if (rc) return rc;
+  const size_t elem = sizeof(T);
+  const int R = (M >= 32 && M <= 2048) ? M / 32 : 0;  // register FFT up to 2048 points
+  const int nF = p.corr_on ? nchunk * int(BH) : 0;
+  const int gmax = std::max(1, std::min(kDiagGroup, 8192 / N));
+  const size_t st = size_t(D + (elem == 2 ? 2 : 1)) * elem;
+  const int64_t room = int64_t(200 * 1024) - int64_t(gmax) * N * 4 - int64_t(gmax) * kLanes * 8 - 64;
+  const int span = int(std::max<int64_t>(0, std::min<int64_t>(elem == 2 ? 192 : 64, room / int64_t(st) - 2 * kDiagTile)));
+  const DiagGroups gr = make_diag_groups(p, gmax, span);
+  const int nDG = (p.corr_on && !p.stripe_all_diffuse) ? gr.n * int(BH) : 0;
+  size_t smem1 = colrow_smem(N, int(D), elem);
+  if (nDG) smem1 = std::max(smem1, size_t(2 * kDiagTile + span) * st + size_t(gmax) * N * 4 + size_t(gmax) * kLanes * 8 + 64);
+  if (nF) smem1 = std::max(smem1, R ? fft_warp_smem_rt(R, N, elem) : fft_partial_smem(M, nf));
+  const unsigned grid1 = unsigned(nF + nDG + int(BH));
+#define FFTS_STAGE1(RR)                                                                                          \
+  case RR: {                                                                                                     \
+    FFTS_CUDA(cudaFuncSetAttribute(select_stage1_kernel<T, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                   int(smem1)));                                                                 \
+    select_stage1_kernel<T, RR><<<grid1, 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, \
+                                                               int(BH), nDG, gr, gmax, ws.partial, ws.nv,         \
+                                                               ws.colsel, ws.lastsel);                           \
+    break;                                                                                                       \
   }
-  const int nF = (p.corr_on && !reg_fft) ? nchunk * int(BH) : 0;
-  const int nD = (p.corr_on && !p.stripe_all_diffuse) ? p.n_diag_samples * int(BH) : 0;
-  size_t smem1 = colrow_smem(N, int(D));
-  if (nF) smem1 = std::max(smem1, fft_partial_smem(M, nf));
-  if (nD) smem1 = std::max(smem1, diag_stats_smem(N));
-  FFTS_CUDA(cudaFuncSetAttribute(select_stage1_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem1)));
-  select_stage1_kernel<T><<<unsigned(nF + nD + BH), 256, smem1, stream>>>(
-      qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, int(BH), nD, ws.partial, ws.nv, ws.colsel, ws.lastsel);
+  switch (R) {
+    FFTS_STAGE1(0)
+    FFTS_STAGE1(1)
+    FFTS_STAGE1(2)
+    FFTS_STAGE1(4)
+    FFTS_STAGE1(8)
+    FFTS_STAGE1(16)
+    FFTS_STAGE1(32)
+    FFTS_STAGE1(64)
+    default:
+      set_error(FFTS_E_INVALID, "selection: unsupported FFT length %d", M);
+      return FFTS_E_INVALID;
+  }
+#undef FFTS_STAGE1
   FFTS_CUDA(cudaGetLastError());
   // stage 2: stripe decision, inverse FFT, lag selection
   const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
@@ -1046,11 +1177,11 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   corr_select_kernel<<<BH, 512, smem2, stream>>>(ws.partial, nchunk, N, M, p, ws.nv, ws.stripe, is_stripe, svar,
                                                  corr, csum, ws.tausel);
   FFTS_CUDA(cudaGetLastError());
-  const int R = N <= 1024 ? 16 : max(1, 16384 / N);
-  const size_t smem4 = size_t(R) * D * 8 + size_t(R) * N * 4 + size_t(R) * W * 4 + 8 * 256 * 4 + size_t(R) * 4;
+  const int RT = N <= 1024 ? 16 : max(1, 16384 / N);  // mask rows per CTA
+  const size_t smem4 = size_t(RT) * D * 8 + size_t(RT) * N * 4 + size_t(RT) * W * 4 + 8 * 256 * 4 + size_t(RT) * 4;
   FFTS_CUDA(cudaFuncSetAttribute(mask_build_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem4)));
-  mask_build_kernel<T><<<dim3(unsigned(ceil_div(N, R)), BH), 256, smem4, stream>>>(
-      qb, kb, int(H), int(Hkv), int(D), p, R, ws.stripe, ws.tausel, ws.colsel, ws.lastsel, bits, row_count);
+  mask_build_kernel<T><<<dim3(unsigned(ceil_div(N, RT)), BH), 256, smem4, stream>>>(
+      qb, kb, int(H), int(Hkv), int(D), p, RT, ws.stripe, ws.tausel, ws.colsel, ws.lastsel, bits, row_count);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }
