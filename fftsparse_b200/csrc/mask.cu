@@ -255,17 +255,35 @@ __device__ void fft_warp_body(const T *__restrict__ qb, const T *__restrict__ kb
   }
   // stage the chunk's 8 channels of q and k, channel-major
   constexpr int V = Elem<T>::kVec;
-  for (int t = threadIdx.x; t < N; t += blockDim.x) {
+  constexpr int NV = kDChunk / V;  // 16-byte vectors per row and tensor
+  constexpr int U = 4;             // rows in flight per thread
+  for (int base = threadIdx.x; base < N; base += U * blockDim.x) {
+    uint4 qv[U][NV], kv[U][NV];
 #pragma unroll
-    for (int c0 = 0; c0 < kDChunk; c0 += V) {
-      const uint4 qv = *reinterpret_cast<const uint4 *>(q + int64_t(t) * D + c0);
-      const uint4 kv = *reinterpret_cast<const uint4 *>(k + int64_t(t) * D + c0);
-      const T *qe = reinterpret_cast<const T *>(&qv);
-      const T *ke = reinterpret_cast<const T *>(&kv);
+    for (int u = 0; u < U; ++u) {
+      const int t = base + u * blockDim.x;
+      if (t < N) {
 #pragma unroll
-      for (int c = 0; c < V; ++c) {
-        qs[(c0 + c) * N + t] = qe[c];
-        ks[(c0 + c) * N + t] = ke[c];
+        for (int c = 0; c < NV; ++c) {
+          qv[u][c] = *reinterpret_cast<const uint4 *>(q + int64_t(t) * D + c * V);
+          kv[u][c] = *reinterpret_cast<const uint4 *>(k + int64_t(t) * D + c * V);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = base + u * blockDim.x;
+      if (t < N) {
+#pragma unroll
+        for (int c0 = 0; c0 < NV; ++c0) {
+          const T *qe = reinterpret_cast<const T *>(&qv[u][c0]);
+          const T *ke = reinterpret_cast<const T *>(&kv[u][c0]);
+#pragma unroll
+          for (int c = 0; c < V; ++c) {
+            qs[(c0 * V + c) * N + t] = qe[c];
+            ks[(c0 * V + c) * N + t] = ke[c];
+          }
+        }
       }
     }
   }
@@ -648,16 +666,30 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   const int mmax = N - lo - 1;
   for (int t0 = 0; t0 < mmax; t0 += kDiagTile) {
     // k rows [t0, t0 + 64) and q rows [t0 + lo, t0 + hi + 64)
-    for (int idx = tid; idx < (kDiagTile + wrows) * vrow; idx += blockDim.x) {
-      const int rr = idx / vrow, v = idx - rr * vrow;
-      const bool isk = rr < kDiagTile;
-      const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
-      T *dst = isk ? ks + rr * QS : qw + (rr - kDiagTile) * QS;
-      if (row < N) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(row) * D + v * V);
-        const T *e = reinterpret_cast<const T *>(&raw);
+    constexpr int U = 8;  // 16-byte loads in flight per thread before their stores
+    const int total = (kDiagTile + wrows) * vrow;
+    for (int base = tid; base < total; base += U * blockDim.x) {
+      uint4 raw[U];
 #pragma unroll
-        for (int c = 0; c < V; ++c) dst[v * V + c] = e[c];
+      for (int u = 0; u < U; ++u) {
+        const int idx = base + u * blockDim.x;
+        const int rr = idx / vrow, v = idx - rr * vrow;
+        const bool isk = rr < kDiagTile;
+        const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
+        if (idx < total && row < N) raw[u] = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(row) * D + v * V);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int idx = base + u * blockDim.x;
+        const int rr = idx / vrow, v = idx - rr * vrow;
+        const bool isk = rr < kDiagTile;
+        const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
+        if (idx < total && row < N) {
+          T *dst = isk ? ks + rr * QS : qw + (rr - kDiagTile) * QS;
+          const T *e = reinterpret_cast<const T *>(&raw[u]);
+#pragma unroll
+          for (int c = 0; c < V; ++c) dst[v * V + c] = e[c];
+        }
       }
     }
     __syncthreads();
@@ -684,7 +716,9 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   }
   // three canonical reductions per lag, the G lags side by side
   auto tree = [&](double *a) {
-    for (int g = 0; g < G; ++g) part[g * kLanes + tid] = a[g];
+#pragma unroll
+    for (int g = 0; g < kDiagGroup; ++g)
+      if (g < G) part[g * kLanes + tid] = a[g];
     __syncthreads();
     for (int st = kLanes / 2; st >= 1; st >>= 1) {
       for (int idx = tid; idx < G * st; idx += blockDim.x) {
@@ -693,18 +727,24 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
       }
       __syncthreads();
     }
-    for (int g = 0; g < G; ++g) a[g] = part[g * kLanes];
+#pragma unroll
+    for (int g = 0; g < kDiagGroup; ++g)
+      if (g < G) a[g] = part[g * kLanes];
     __syncthreads();
   };
   double acc[kDiagGroup], mean[kDiagGroup], var[kDiagGroup];
-  for (int g = 0; g < G; ++g) {
+#pragma unroll
+  for (int g = 0; g < kDiagGroup; ++g) {
+    if (g >= G) break;
     const int n = N - p.diag_taus[first + g] - 2;
     acc[g] = 0.0;
     for (int e = tid; e < n; e += blockDim.x)
       acc[g] = __dadd_rn(acc[g], (double)__fsub_rn(vals[g * N + e + 1], vals[g * N + e]));
   }
   tree(acc);
-  for (int g = 0; g < G; ++g) {
+#pragma unroll
+  for (int g = 0; g < kDiagGroup; ++g) {
+    if (g >= G) break;
     const int n = N - p.diag_taus[first + g] - 2;
     mean[g] = n >= 2 ? __ddiv_rn(acc[g], (double)n) : 0.0;
     acc[g] = 0.0;
@@ -714,7 +754,9 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
     }
   }
   tree(acc);
-  for (int g = 0; g < G; ++g) {
+#pragma unroll
+  for (int g = 0; g < kDiagGroup; ++g) {
+    if (g >= G) break;
     const int n = N - p.diag_taus[first + g] - 2;
     var[g] = n >= 2 ? __ddiv_rn(acc[g], (double)(n - 1)) : __longlong_as_double(0x7ff8000000000000ll);
     const int m = n + 1;
@@ -724,7 +766,9 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   tree(acc);
   if (tid == 0) {
     const double floor6 = (double)1e-6f;
-    for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int g = 0; g < kDiagGroup; ++g) {
+      if (g >= G) break;
       const int m = N - p.diag_taus[first + g] - 1;
       double mabs = m > 0 ? __ddiv_rn(acc[g], (double)m) : __longlong_as_double(0x7ff8000000000000ll);
       if (mabs < floor6) mabs = floor6;
@@ -811,15 +855,33 @@ __device__ void colrow_body(const T *__restrict__ qb, const T *__restrict__ kb, 
   if (col || last) {
     for (int jhi = N - 1; jhi >= 0; jhi -= C) {
       const int rows = min(C, jhi + 1);
-      for (int idx = tid; idx < 2 * rows * vrow; idx += blockDim.x) {
-        const bool isk = idx >= rows * vrow;
-        const int i2 = isk ? idx - rows * vrow : idx;
-        const int t = i2 / vrow, v = i2 - t * vrow;
-        const uint4 raw = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(jhi - t) * D + v * V);
-        const T *e = reinterpret_cast<const T *>(&raw);
-        T *dst = (isk ? ks : qs) + t * QS + v * V;
+      // eight 16-byte loads in flight per thread before their stores
+      constexpr int U = 8;
+      for (int base = tid; base < 2 * rows * vrow; base += U * blockDim.x) {
+        uint4 raw[U];
 #pragma unroll
-        for (int c = 0; c < V; ++c) dst[c] = e[c];
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + u * blockDim.x;
+          if (idx < 2 * rows * vrow) {
+            const bool isk = idx >= rows * vrow;
+            const int i2 = isk ? idx - rows * vrow : idx;
+            const int t = i2 / vrow, v = i2 - t * vrow;
+            raw[u] = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(jhi - t) * D + v * V);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int idx = base + u * blockDim.x;
+          if (idx < 2 * rows * vrow) {
+            const bool isk = idx >= rows * vrow;
+            const int i2 = isk ? idx - rows * vrow : idx;
+            const int t = i2 / vrow, v = i2 - t * vrow;
+            const T *e = reinterpret_cast<const T *>(&raw[u]);
+            T *dst = (isk ? ks : qs) + t * QS + v * V;
+#pragma unroll
+            for (int c = 0; c < V; ++c) dst[c] = e[c];
+          }
+        }
       }
       __syncthreads();
       if (col && tid < D) {
