@@ -141,3 +141,9 @@ def test_repeated_calls_are_deterministic(lib):
     for _ in range(50):
         assert torch.equal(lib.sparse_attention(q, k, v, bits, bs, status=status), first)
     assert int(status.item()) == 0, "kernel reported a wait time-out"
+
+
+@pytest.mark.slow
+def test_max_tiles_subset(lib):
+    # L = 262144: 4096 key tiles of 64, the largest tile bitmask the kernel takes; check 3 query blocks
+    run_case(lib, 1, 2, 1, 262144, 128, 0.02, seed=17, heads=[1], rows=[0, 1000, 2047])

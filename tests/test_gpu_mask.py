@@ -108,3 +108,27 @@ def test_mask_bit_exact_128k(lib):
     m2 = lib.fft_block_mask(q.cuda(), k.cuda(), params=params2)
     assert 0 < int(ref2["is_stripe"].sum()) < 32
     assert torch.equal(m2.bits.cpu(), ref2["bits"])
+
+
+@pytest.mark.slow
+def test_mask_bit_exact_n2048(lib):
+    """N = 2048 blocks (L = 262144): FFT length 4096 takes the shared-memory FFT, the column pass
+    64-row chunks and the stripe statistics groups of at most 4 lags; stripe and diffuse heads."""
+    from oracle.synth import make_inputs
+    from fftsparse_b200.params import derive_mask_params
+    L = 262144
+    q, k, v = make_inputs(L, num_q_heads=4, num_kv_heads=1, dtype=torch.bfloat16)
+    del v
+    kw = dict(sink_ratio=0.01, recent_ratio=0.0, local_span_ratio=0.02, correlation_selection_mode="topk",
+              correlation_topk_ratio=0.05, qk_topk_ratio=0.05, column_topk_ratio=0.2)
+    params = derive_mask_params(L, **kw)
+    assert params.n_blocks == 2048
+    ref = O.prefill_mask(q, k, params)
+    m = lib.fft_block_mask(q.cuda(), k.cuda(), params=params)
+    assert torch.equal(m.bits.cpu(), ref["bits"])
+    assert _bits_equal(m.corr.cpu(), ref["corr"])
+    params2 = derive_mask_params(L, **dict(kw, stripe_threshold=float(ref["stripe_var"].median())))
+    ref2 = O.block_mask(ref["qb"], ref["kb"], params2, torch.bfloat16)
+    m2 = lib.fft_block_mask(q.cuda(), k.cuda(), params=params2)
+    assert 0 < int(ref2["is_stripe"].sum()) < 4
+    assert torch.equal(m2.bits.cpu(), ref2["bits"])
