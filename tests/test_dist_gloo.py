@@ -14,7 +14,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from fftsparse_b200.dist import gather_heads, kv_group_shard, local_views
+from fftsparse_b200.dist import gather_heads, kv_group_shard, local_views, unit_shard
 
 
 def _free_port() -> int:
@@ -34,6 +34,24 @@ def test_kv_group_shard_partitions_heads():
         assert seen == list(range(32))
     with pytest.raises(ValueError):
         kv_group_shard(28, 4, 8, 0)  # 4 KV groups cannot split over 8 ranks
+
+
+def test_unit_shard_sequences_by_kv_groups():
+    # 2 sequences x 4 KV groups (28 q-heads) over 8 ranks, one unit each
+    seen = set()
+    for r in range(8):
+        s = unit_shard(2, 28, 4, 8, r)
+        assert s.b_hi - s.b_lo == 1 and s.kv_hi - s.kv_lo == 1 and s.heads == 7
+        seen.add((s.b_lo, s.kv_lo))
+    assert seen == {(b, g) for b in range(2) for g in range(4)}
+    # KV groups split first when they divide over the ranks
+    s = unit_shard(4, 8, 2, 2, 1)
+    assert (s.b_lo, s.b_hi, s.kv_lo, s.kv_hi) == (0, -1, 1, 2)
+    # one KV group: whole sequences per rank
+    s = unit_shard(4, 4, 1, 2, 1)
+    assert (s.b_lo, s.b_hi, s.h_lo, s.h_hi) == (2, 4, 0, 4)
+    with pytest.raises(ValueError):
+        unit_shard(3, 28, 4, 8, 0)  # 12 units over 8 ranks
 
 
 def test_local_views_expanded_and_gqa():
@@ -90,6 +108,54 @@ def _worker(rank, world, port, result_q, kw):
                           out_local.view(torch.int16).numpy().tobytes()))
     finally:
         dist.destroy_process_group()
+
+
+def _worker_batch(rank, world, port, result_q, kw):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from fftsparse_b200.dist import sharded_prefill
+        from oracle.synth import make_inputs
+        _patch_kernels_with_oracle()
+        # 2 sequences x 1 KV group: the ranks split by sequence
+        q, k, v = make_inputs(1280, num_q_heads=4, num_kv_heads=1, dtype=torch.bfloat16, expand=False, batch=2)
+        out_full = sharded_prefill(q, k, v, 0, **kw)
+        s = unit_shard(2, 4, 1, world, rank)
+        ql, kl, vl = local_views(q, k, v, s)
+        out_local = sharded_prefill(ql.contiguous(), kl.contiguous(), vl.contiguous(), 0, inputs_are_local=True,
+                                    global_batch=2, num_heads=4, num_kv_heads=1, **kw)
+        if rank == 0:
+            result_q.put((out_full.view(torch.int16).numpy().tobytes(),
+                          out_local.view(torch.int16).numpy().tobytes()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_by_sequence_world2():
+    kw = dict(block_size=128, sink_ratio=0.01, recent_ratio=0.0, local_span_ratio=0.02,
+              correlation_selection_mode="topk", correlation_topk_ratio=0.2, qk_topk_ratio=0.2)
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_batch, args=(r, 2, port, q_out, kw)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got_full, got_local = q_out.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    import numpy as np
+
+    from oracle import oracle as O
+    from oracle.synth import make_inputs
+    from fftsparse_b200.params import derive_mask_params
+    q, k, v = make_inputs(1280, num_q_heads=4, num_kv_heads=1, dtype=torch.bfloat16, expand=False, batch=2)
+    params = derive_mask_params(1280, **kw)
+    m = O.prefill_mask(q, k, params)
+    ref = O.sparse_attention(q, k, v, O.unpack_bits(m["bits"], params.n_blocks), 128).to(torch.bfloat16)
+    for b in (got_full, got_local):
+        got = torch.from_numpy(np.frombuffer(b, dtype=np.int16).copy()).view(torch.bfloat16).view(2, 4, 1280, 128)
+        assert torch.equal(got, ref)
 
 
 def test_sharded_equals_unsharded_world2():

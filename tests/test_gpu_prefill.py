@@ -62,3 +62,30 @@ def test_unknown_mode_raises_value_error(lib):
     x = torch.zeros(1, 1, 2048, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):
         lib.myattn_prefill(x, x, x, 0, correlation_selection_mode="nope")
+
+
+def test_config5_shape(lib):
+    """BASELINE config 5 head shape: 2 sequences, 28 q-heads over 4 KV heads (groups of 7),
+    block 64, keep ratio 0.05, un-expanded k/v; L reduced to 8192."""
+    import bench
+    from fftsparse_b200.params import derive_mask_params
+    from oracle.synth import make_inputs
+    L = 8192
+    q, k, v = make_inputs(L, num_q_heads=28, num_kv_heads=4, dtype=torch.bfloat16, expand=False, batch=2, seed=5,
+                          rope_base=1e6)
+    kw = dict(bench.mask_kwargs(0.05), block_size=64)
+    params = derive_mask_params(L, **kw)
+    m = lib.fft_block_mask(q.cuda(), k.cuda(), **kw)
+    ref = O.prefill_mask(q, k, params)
+    assert torch.equal(m.bits.cpu(), ref["bits"])
+    out = lib.myattn_prefill(q.cuda(), k.cuda(), v.cuda(), 0, **kw)
+    torch.cuda.synchronize()
+    got = out.view(2, L, 28, 128).permute(0, 2, 1, 3).float().cpu()
+    mask = O.unpack_bits(ref["bits"], params.n_blocks)
+    heads, rows = [0, 6, 27], [0, 37, params.n_blocks - 1]
+    exp = O.sparse_attention(q, k, v, mask, 64, heads=heads, rows=rows)
+    for h in heads:
+        for i in rows:
+            sl = slice(i * 64, (i + 1) * 64)
+            err = (got[:, h, sl] - exp[:, h, sl]).abs()
+            assert float(err.max()) <= 2e-2 and float(err.mean()) <= 1e-3, (h, i, float(err.max()))
