@@ -349,6 +349,9 @@ def run_ours(args):
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
+        # NCCL's own log lines (e.g. its version banner) go to stderr unless the caller chose a
+        # file, so that rank 0's stdout carries only the JSON result line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     F.load_library()
     kw = mask_kwargs(args.keep_ratio)
