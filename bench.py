@@ -13,8 +13,9 @@ N = 1 calls the drop-in ``myattn_prefill`` with repeat_kv-expanded k/v, the
 exact call of the reference's benchmark
 (eval/efficiency/benchmark_attention_multilayer.py:146-157, :308).  N > 1
 (launched by torchrun, one rank per GPU, NCCL) shards the 8 KV groups over the
-ranks and all-gathers the head-major outputs (fftsparse_b200/dist.py); total
-work is fixed, so the scaling is strong.  ``--impl reference`` times the CPU
+ranks and all-gathers the head-major outputs on the copy engines, overlapped with
+the attention (fftsparse_b200/dist.py, PeerGather); total work is fixed, so the
+scaling is strong.  ``--impl reference`` times the CPU
 restatement of the reference path (oracle/) on the host cores instead.
 """
 from __future__ import annotations
@@ -206,7 +207,7 @@ def run_reference(args):
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "detail": info,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ------------------------------------------------------------- TTFT (cfg 4)
@@ -218,16 +219,17 @@ class Llama8BShape:
     layer's attention is fftsparse_b200's operator on un-expanded GQA k/v.
     With world > 1 each rank keeps only its KV groups' columns of the QKV
     projection, runs attention for its heads, and one all-gather per layer
-    assembles the head-major output that o_proj consumes (o_proj and the MLP
-    are replicated)."""
+    (on the copy engines when a PeerGather is given) assembles the head-major
+    output that o_proj consumes (o_proj and the MLP are replicated)."""
 
     H, HKV, D, HIDDEN, INTER, VOCAB = 32, 8, 128, 4096, 14336, 128256
 
-    def __init__(self, layers, device, world=1, rank=0, seed=0):
+    def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None):
         from fftsparse_b200.dist import kv_group_shard
         g = torch.Generator(device=device).manual_seed(seed)
         self.shard = kv_group_shard(self.H, self.HKV, world, rank)
         self.world = world
+        self.gather = gather  # dist.PeerGather of the (H, L) output, or None for NCCL
         D = self.D
 
         def w(*shape):
@@ -273,7 +275,6 @@ class Llama8BShape:
             return x * cos + torch.cat([-x2, x1], -1) * sin
 
         h = self.embed[ids]
-        full = None if self.world == 1 else torch.empty(1, self.H, L, D, dtype=torch.bfloat16, device=self.device)
         for lw in self.layers:
             x = self.rmsnorm(h)
             qkv = x @ lw["wqkv"]
@@ -284,7 +285,7 @@ class Llama8BShape:
             if self.world == 1:
                 attn = F.myattn_prefill(q, k, v, 0, **kw).view(L, self.H * D)
             else:
-                sharded_prefill(q, k, v, 0, out=full, inputs_are_local=True, **kw)
+                full = sharded_prefill(q, k, v, 0, inputs_are_local=True, gather=self.gather, **kw)
                 attn = full[0].transpose(0, 1).reshape(L, self.H * D)
             del q, k, v
             h = h + attn @ lw["wo"]
@@ -296,12 +297,12 @@ class Llama8BShape:
         return self.rmsnorm(h[-1:]) @ self.lm_head  # logits of the last position only
 
 
-def run_ttft(args, dev, world, rank, stream, barrier):
+def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
     """Prefill TTFT of the 8B-shape decoder: token ids already on the device to
     the last position's logits, device-timed with CUDA events, max over ranks."""
     import torch.distributed as dist
     L = args.seq_len
-    model = Llama8BShape(args.ttft_layers, dev, world, rank)
+    model = Llama8BShape(args.ttft_layers, dev, world, rank, gather=gather)
     g = torch.Generator(device=dev).manual_seed(0)
     ids = torch.randint(0, model.VOCAB, (L,), generator=g, device=dev)
     kw = mask_kwargs(args.keep_ratio)
@@ -337,7 +338,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import fftsparse_b200 as F
-    from fftsparse_b200.dist import kv_group_shard, local_views, sharded_prefill
+    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views, sharded_prefill
     from fftsparse_b200.synthetic import make_inputs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -349,9 +350,6 @@ def run_ours(args):
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        # NCCL's own log lines (e.g. its version banner) go to stderr unless the caller chose a
-        # file, so that rank 0's stdout carries only the JSON result line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     F.load_library()
     kw = mask_kwargs(args.keep_ratio)
@@ -361,10 +359,13 @@ def run_ours(args):
     q, k, v = make_inputs(L, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16, device=str(dev))
     torch.cuda.synchronize(dev)
 
+    # N > 1: the output all-gather runs on the copy engines, overlapped with the attention
+    pg = PeerGather(HQ, L, HEAD_DIM, device=dev) if world > 1 else None
+
     def step():
         if world == 1:
             return F.myattn_prefill(q, k, v, 0, **kw)
-        return sharded_prefill(q, k, v, 0, num_kv_heads=HKV, **kw)
+        return sharded_prefill(q, k, v, 0, num_kv_heads=HKV, gather=pg, **kw)
 
     def barrier():
         if world > 1:
@@ -396,13 +397,13 @@ def run_ours(args):
     k8 = k[:, ::HQ // HKV].contiguous()
     v8 = v[:, ::HQ // HKV].contiguous()
     for _ in range(2):
-        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, **kw)
+        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, gather=pg, **kw)
     torch.cuda.synchronize(dev)
     barrier()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     g0.record(stream)
     for _ in range(args.steps):
-        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, **kw)
+        F.myattn_prefill(q, k8, v8, 0, **kw) if world == 1 else sharded_prefill(q, k8, v8, 0, gather=pg, **kw)
     g1.record(stream)
     torch.cuda.synchronize(dev)
     tg = torch.tensor([g0.elapsed_time(g1) / args.steps], device=dev)
@@ -515,7 +516,9 @@ def run_ours(args):
 
     ttft = None
     if not args.no_ttft:
-        ttft = run_ttft(args, dev, world, rank, stream, barrier)
+        ttft = run_ttft(args, dev, world, rank, stream, barrier, pg)
+    if pg is not None and int(pg.status.item()) != 0:
+        raise RuntimeError("the copy-engine all-gather reported a wait time-out (a peer never delivered its rows)")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -535,7 +538,7 @@ def run_ours(args):
             "config": {"workload": f"cfg3: L={L}, Hq={HQ}, Hkv={HKV}, D={HEAD_DIM}, block {BLOCK}, keep ratio "
                                    f"{args.keep_ratio} (topk mode, efficiency-script ratios); "
                                    + ("drop-in myattn_prefill with repeat_kv-expanded k/v" if world == 1 else
-                                      f"KV groups sharded {HKV // world} per rank + NCCL all-gather of outputs"),
+                                      f"KV groups sharded {HKV // world} per rank; output all-gather on the copy engines, overlapped"),
                        "model": "Llama-3.1-8B attention-layer shape", "seq_len": L, "global_batch": 1,
                        "parallelism": "single GPU" if world == 1 else f"kv-group x{world}",
                        "l2": "inputs (3.2 GB) larger than L2; no flush"},
@@ -548,13 +551,29 @@ def run_ours(args):
             "gqa_native_ms_per_layer": round(gqa_native_ms, 4),
             "ttft": ttft,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 
 
+# The JSON result line goes to the process's real stdout; everything else written
+# to file descriptor 1 (library banners such as NCCL's version line included) is
+# sent to stderr, so that stdout carries the result line alone.
+_RESULT = None
+
+
+def emit(line: dict) -> None:
+    out = _RESULT if _RESULT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _RESULT
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         run_reference(args)

@@ -293,6 +293,8 @@ struct Params {
   const uint32_t *bits;
   __nv_bfloat16 *out;
   int64_t os_b, os_h, os_l;  // output strides (elements)
+  int qt_lo, qt_cnt;         // query tiles [qt_lo, qt_lo + qt_cnt) are computed
+  int out_row0;              // query row written at output row 0
   float scale_log2;
   int *status;
 };
@@ -354,8 +356,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   int x = blockIdx.x;
   const int hg = x % G;
   x /= G;
-  const int qt = prm.nq - 1 - (x % prm.nq);
-  x /= prm.nq;
+  const int qt = prm.qt_lo + prm.qt_cnt - 1 - (x % prm.qt_cnt);
+  x /= prm.qt_cnt;
   const int kvh = x % prm.Hkv;
   const int b = x / prm.Hkv;
   const int h = kvh * G + hg;
@@ -681,7 +683,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_after();
     // epilogue: O / l -> bf16 -> out[b, row, h, :]
     const bool store = row_g < prm.L;
-    __nv_bfloat16 *dst = prm.out + int64_t(b) * prm.os_b + int64_t(row_g) * prm.os_l + int64_t(h) * prm.os_h;
+    __nv_bfloat16 *dst =
+        prm.out + int64_t(b) * prm.os_b + int64_t(row_g - prm.out_row0) * prm.os_l + int64_t(h) * prm.os_h;
     const float inv_l = (ok && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
@@ -756,7 +759,8 @@ __device__ int g_attn_status_sink;
 
 int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv, int64_t L,
                     int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs, const uint32_t *bits, int bs,
-                    int causal, void *out, const int64_t *os, int32_t *status, cudaStream_t stream) {
+                    int causal, void *out, const int64_t *os, int64_t row_lo, int64_t row_hi, int32_t *status,
+                    cudaStream_t stream) {
   using namespace attn;
   FFTS_REQUIRE(q && k && v && bits && out && qs && ks && vs && os, "sparse_attn: NULL argument");
   FFTS_REQUIRE(D == kD, "sparse_attn: head_dim must be 128 (got %lld)", (long long)D);
@@ -773,6 +777,9 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
                    (reinterpret_cast<uintptr_t>(v) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
                "sparse_attn: tensors must be 16-byte aligned");
   FFTS_REQUIRE(os[0] % 8 == 0 && os[1] % 8 == 0 && os[2] % 8 == 0, "sparse_attn: output strides must be 16-byte multiples");
+  FFTS_REQUIRE(row_lo >= 0 && row_lo < row_hi && row_hi <= L && row_lo % kBM == 0 && (row_hi % kBM == 0 || row_hi == L),
+               "sparse_attn: query rows [%lld, %lld) must lie in [0, L) on %d-row boundaries", (long long)row_lo,
+               (long long)row_hi, kBM);
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, q, L, H, B, qs, kBM);
   if (!rc) rc = make_map(&mk, k, L, Hkv, B, ks, kBN);
@@ -785,6 +792,9 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   p.bits = bits;
   p.out = static_cast<__nv_bfloat16 *>(out);
   p.os_b = os[0]; p.os_h = os[1]; p.os_l = os[2];
+  p.qt_lo = int(row_lo / kBM);
+  p.qt_cnt = int(ceil_div(row_hi, kBM) - row_lo / kBM);
+  p.out_row0 = int(row_lo);
   p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
   if (status) {
     p.status = status;
@@ -797,7 +807,7 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   // the largest shared-memory carveout, so that two CTAs fit on an SM
   FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  int(cudaSharedmemCarveoutMaxShared)));
-  const unsigned grid = unsigned(B * H * nq);
+  const unsigned grid = unsigned(B * H * p.qt_cnt);
   sparse_attn_kernel<<<grid, kThreads, SmemLayout::bytes, stream>>>(mq, mk, mv, p);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;

@@ -656,7 +656,8 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   T *ks = reinterpret_cast<T *>(smem_raw);           // [kDiagTile][QS]
   T *qw = ks + kDiagTile * QS;                        // [wrows][QS]
   float *vals = reinterpret_cast<float *>(smem_raw + ((size_t(kDiagTile + wrows) * QS * sizeof(T) + 15) & ~size_t(15)));
-  double *part = reinterpret_cast<double *>(vals + gmax * N);  // [gmax][256]
+  // [gmax][256], 16-byte aligned whatever gmax * N is
+  double *part = reinterpret_cast<double *>((reinterpret_cast<uintptr_t>(vals + gmax * N) + 15) & ~uintptr_t(15));
   const int b = bh / H, h = bh % H;
   const T *q = qb + int64_t(bh) * N * D;
   const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;

@@ -115,9 +115,128 @@ def gather_heads(local_out: torch.Tensor, full_out: torch.Tensor, group=None, sh
     return full_out
 
 
+def row_chunks(L: int, parts: int = 4, tile: int = 128):
+    """Query-row chunks [lo, hi) of about equal causal work (boundaries at
+    L * sqrt(i / parts), on tile-row boundaries), in increasing row order; one
+    chunk for short sequences."""
+    if parts <= 1 or L < parts * 8 * tile:
+        return [(0, L)]
+    cuts = [0]
+    for i in range(1, parts):
+        c = int(round(L * (i / parts) ** 0.5 / tile)) * tile
+        if cuts[-1] < c < L:
+            cuts.append(c)
+    cuts.append(L)
+    return list(zip(cuts[:-1], cuts[1:]))
+
+
+class PeerGather:
+    """The all-gather of the sharded attention output on the GPUs' copy engines.
+
+    Created once per (heads, sequence length) by every rank of the group (it is
+    collective).  Each rank holds two full head-major output buffers [1, H, L, D]
+    and maps its peers' buffers and flag words through CUDA IPC.  A call computes
+    the rank's heads in row chunks of about equal causal work directly into its
+    own buffer; after each chunk a copy stream pushes those rows into every peer's
+    buffer (cudaMemcpy2DAsync over NVLink) while the SMs compute the next chunk;
+    then it stores the call's epoch number into each peer's flag, and the calling
+    stream waits (bounded) until every rank's flag reached the epoch.  NCCL's
+    all-gather cannot overlap this way: it runs as SM kernels, and the attention
+    kernel holds every SM's shared memory and TMEM.
+
+    The two buffers alternate between calls, so the tensor a call returns stays
+    valid until the call after next; consume it (o_proj) before that.  One
+    sequence (B = 1), KV-group shards, bf16 output.  ``status`` is nonzero after a
+    wait that timed out (a peer never delivered its rows)."""
+
+    def __init__(self, num_heads: int, seq_len: int, head_dim: int = 128, group=None, device=None):
+        import ctypes
+
+        from . import _lib
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.H, self.L, self.D = num_heads, seq_len, head_dim
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.lib = _lib.load()
+        self.bufs = [torch.empty(1, num_heads, seq_len, head_dim, dtype=torch.bfloat16, device=self.device)
+                     for _ in range(2)]
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+
+        def handle(t):
+            h = (ctypes.c_ubyte * 64)()
+            off = ctypes.c_int64()
+            _lib.check(self.lib.ffts_ipc_handle(t.data_ptr(), h, ctypes.byref(off)))
+            return bytes(h), off.value
+
+        mine = [handle(b) for b in self.bufs] + [handle(self.flags)]
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.peer_bufs = {}
+        self.peer_flags = {}
+        self._opened = []
+        for p in range(self.world):
+            if p == self.rank:
+                continue
+            ptrs = []
+            for hb, off in everyone[p]:
+                ptr = ctypes.c_void_p()
+                _lib.check(self.lib.ffts_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb), off,
+                                                  ctypes.byref(ptr)))
+                ptrs.append(ptr.value)
+                self._opened.append((ptr.value, off))
+            self.peer_bufs[p] = ptrs[:2]
+            self.peer_flags[p] = ptrs[2]
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.epoch = 0
+        dist.barrier(group)  # every rank has mapped every buffer before the first push
+
+    def run(self, ql, kl, vl, bits, block_size: int, causal: bool, shard: Shard) -> torch.Tensor:
+        from . import _lib
+        from .prefill import sparse_attention
+
+        lib, dev = self.lib, self.device
+        cur = torch.cuda.current_stream(dev)
+        # the buffer used now was last read by this rank's pushes two calls ago
+        cur.wait_stream(self.stream)
+        self.epoch += 1
+        e, slot = self.epoch, self.epoch % 2
+        buf = self.bufs[slot]
+        L, D, Hl = self.L, self.D, shard.heads
+        row_bytes = D * buf.element_size()
+        pitch = L * row_bytes
+        local = buf.data_ptr() + shard.h_lo * pitch
+        side = self.stream.cuda_stream
+        for lo, hi in row_chunks(L):
+            sparse_attention(ql, kl, vl, bits, block_size, causal=causal,
+                             out=buf[:, shard.h_lo:shard.h_hi, lo:hi].permute(0, 2, 1, 3), rows=(lo, hi))
+            done = torch.cuda.Event()
+            done.record(cur)
+            self.stream.wait_event(done)
+            for p, dst in self.peer_bufs.items():
+                _lib.check(lib.ffts_copy_rows(dst[slot] + shard.h_lo * pitch + lo * row_bytes, local + lo * row_bytes,
+                                              pitch, (hi - lo) * row_bytes, Hl, side))
+        for p, flag in self.peer_flags.items():
+            _lib.check(lib.ffts_signal(flag + 4 * self.rank, e, side))
+        _lib.check(lib.ffts_signal(self.flags.data_ptr() + 4 * self.rank, e, cur.cuda_stream))
+        _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
+                                       cur.cuda_stream))
+        return buf
+
+    def close(self):
+        """Unmap the peers' buffers (after every rank's last call has completed)."""
+        torch.cuda.synchronize(self.device)
+        for ptr, off in self._opened:
+            self.lib.ffts_ipc_close(ptr, off)
+        self._opened = []
+
+
 def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx: int = 0, *,
                     group=None, out: Optional[torch.Tensor] = None, inputs_are_local: bool = False,
-                    global_batch: Optional[int] = None, **kwargs) -> torch.Tensor:
+                    global_batch: Optional[int] = None, gather: Optional["PeerGather"] = None,
+                    **kwargs) -> torch.Tensor:
     """FFTSparse prefill of the rank's KV groups followed by the output all-gather.
 
     Returns the head-major output [B, H, L, D] (bf16) on every rank.  The mask
@@ -126,7 +245,10 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx
     order), as when each rank computes its own columns of the QKV projection;
     ``global_batch`` then gives the total number of sequences (default: the local
     count, no split by sequence), and a split by sequence also needs the global
-    ``num_heads`` and ``num_kv_heads``.
+    ``num_heads`` and ``num_kv_heads``.  With ``gather`` (a PeerGather of this
+    group), one sequence split by KV group is gathered on the copy engines,
+    overlapped with the attention, and the result is the gather's buffer (valid
+    until the call after next) unless ``out`` is given.
     """
     from .prefill import fft_block_mask, sparse_attention
 
@@ -157,6 +279,13 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx
     block_size = kwargs.pop("block_size", 128)
     is_causal = kwargs.pop("is_causal", True)
     mask = fft_block_mask(ql, kl, block_size=block_size, **kwargs)
+    whole_batch = all(sh.b_lo == 0 and sh.b_hi in (-1, B) for sh in shards)
+    if gather is not None and world > 1 and B == 1 and whole_batch:
+        res = gather.run(ql, kl, vl, mask.bits, block_size, is_causal, shard)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
     if out is None:
         out = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=q.device)
     Bl = ql.shape[0]

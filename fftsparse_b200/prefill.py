@@ -177,11 +177,13 @@ def _dense_causal_bits(B: int, H: int, N: int, device) -> torch.Tensor:
 
 def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: torch.Tensor,
                      block_size: int, causal: bool = True, out: Optional[torch.Tensor] = None,
-                     status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     status: Optional[torch.Tensor] = None, rows=None) -> torch.Tensor:
     """Block-sparse attention (ffts_sparse_attn_fwd).
 
     q [B, H, L, D], k/v [B, Hkv, L, D] bf16; bits [B, H, N, W] packed mask.
-    Returns (or fills) ``out`` of shape [B, L, H, D] bf16.
+    Returns (or fills) ``out`` of shape [B, L, H, D] bf16.  With ``rows = (lo, hi)``
+    only query rows [lo, hi) are computed (lo a multiple of 128, hi a multiple of
+    128 or L; ffts_sparse_attn_fwd_rows) and ``out`` has shape [B, hi - lo, H, D].
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_4d(name, t)
@@ -189,17 +191,23 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: to
             raise TypeError(f"block-sparse attention supports bfloat16 inputs only (got {name} {t.dtype})")
     B, H, L, D = q.shape
     Hkv = k.shape[1]
+    lo, hi = (0, L) if rows is None else (int(rows[0]), int(rows[1]))
     if out is None:
-        out = torch.empty(B, L, H, D, dtype=torch.bfloat16, device=q.device)
+        out = torch.empty(B, hi - lo, H, D, dtype=torch.bfloat16, device=q.device)
     lib = _lib.load()
     qs = _lib.i64_array([q.stride(0), q.stride(1), q.stride(2)])
     ks = _lib.i64_array([k.stride(0), k.stride(1), k.stride(2)])
     vs = _lib.i64_array([v.stride(0), v.stride(1), v.stride(2)])
     os_ = _lib.i64_array([out.stride(0), out.stride(2), out.stride(1)])
-    _lib.check(lib.ffts_sparse_attn_fwd(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
-        block_size, int(bool(causal)), out.data_ptr(), os_,
-        status.data_ptr() if status is not None else None, _stream_ptr(q.device)))
+    st = status.data_ptr() if status is not None else None
+    if rows is None:
+        _lib.check(lib.ffts_sparse_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
+            block_size, int(bool(causal)), out.data_ptr(), os_, st, _stream_ptr(q.device)))
+    else:
+        _lib.check(lib.ffts_sparse_attn_fwd_rows(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
+            block_size, int(bool(causal)), lo, hi, out.data_ptr(), os_, st, _stream_ptr(q.device)))
     return out
 
 

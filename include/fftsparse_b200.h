@@ -184,6 +184,48 @@ FFTS_API int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *
                              const int64_t *out_strides /* b,h,l */,
                              int32_t *status, void *stream);
 
+/*
+ * ffts_sparse_attn_fwd for the query rows [row_lo, row_hi) only (row_lo a
+ * multiple of 128; row_hi a multiple of 128 or L).  The mask, q/k/v and all
+ * other arguments are those of the whole call; query row t is written at
+ * output row t - row_lo.  No counterpart in the reference: a sharded caller
+ * computes the output in row chunks so that the all-gather of one chunk runs
+ * while the next is computed.
+ */
+FFTS_API int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const void *v, int64_t B,
+                             int64_t H, int64_t Hkv, int64_t L, int64_t D,
+                             const int64_t *q_strides /* b,h,l */,
+                             const int64_t *k_strides /* b,h,l */,
+                             const int64_t *v_strides /* b,h,l */,
+                             const uint32_t *mask_bits, int32_t block_size,
+                             int32_t causal, int64_t row_lo, int64_t row_hi, void *out,
+                             const int64_t *out_strides /* b,h,l */,
+                             int32_t *status, void *stream);
+
+/*
+ * Copy-engine all-gather support for the sharded prefill (fftsparse_b200/dist.py,
+ * PeerGather).  No counterpart in the reference, which runs on one GPU: a rank
+ * maps its peers' output buffers (CUDA IPC), pushes each finished row chunk of
+ * its heads into them with a strided copy on a copy stream while the next chunk
+ * is computed, then stores an epoch number into each peer's flag; the consumer
+ * waits until every flag reached the epoch.
+ *
+ * ffts_ipc_handle: a 64-byte IPC handle of the allocation holding ptr, and ptr's
+ *   offset inside it.  ffts_ipc_open: the peer-side address of that buffer.
+ * ffts_copy_rows: height rows of width bytes, pitch bytes apart on both sides.
+ * ffts_signal: store value into *flag (release, system scope) after the stream's
+ *   earlier work.  ffts_wait_flags: wait until flags[0..n) >= epoch (acquire);
+ *   bounded at about 2 s, after which *status = 5 and the wait returns.
+ */
+FFTS_API int32_t ffts_ipc_handle(const void *ptr, void *handle, int64_t *offset);
+FFTS_API int32_t ffts_ipc_open(const void *handle, int64_t offset, void **ptr);
+FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset);
+FFTS_API int32_t ffts_copy_rows(void *dst, const void *src, int64_t pitch, int64_t width,
+                               int64_t height, void *stream);
+FFTS_API int32_t ffts_signal(int32_t *flag, int32_t value, void *stream);
+FFTS_API int32_t ffts_wait_flags(const int32_t *flags, int32_t n, int32_t epoch, int32_t *status,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

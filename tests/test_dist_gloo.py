@@ -80,9 +80,12 @@ def _patch_kernels_with_oracle():
         m = O.prefill_mask(q.contiguous(), k.contiguous(), params)
         return SimpleNamespace(bits=O.unpack_bits(m["bits"], params.n_blocks))
 
-    def fake_attn(q, k, v, dense, bs, causal=True, out=None, status=None):
-        res = O.sparse_attention(q, k, v, dense, bs, causal=causal).to(torch.bfloat16)  # [B, H, L, D]
-        out.copy_(res.permute(0, 2, 1, 3))
+    def fake_attn(q, k, v, dense, bs, causal=True, out=None, status=None, rows=None):
+        L = q.shape[2]
+        lo, hi = (0, L) if rows is None else rows
+        blocks = list(range(lo // bs, (hi + bs - 1) // bs))
+        res = O.sparse_attention(q, k, v, dense, bs, causal=causal, rows=blocks).to(torch.bfloat16)  # [B, H, L, D]
+        out.copy_(res[:, :, lo:hi].permute(0, 2, 1, 3))
         return out
 
     P.fft_block_mask = fake_mask

@@ -147,3 +147,23 @@ def test_repeated_calls_are_deterministic(lib):
 def test_max_tiles_subset(lib):
     # L = 262144: 4096 key tiles of 64, the largest tile bitmask the kernel takes; check 3 query blocks
     run_case(lib, 1, 2, 1, 262144, 128, 0.02, seed=17, heads=[1], rows=[0, 1000, 2047])
+
+
+def test_row_range_equals_full_call(lib):
+    # ffts_sparse_attn_fwd_rows computes exactly the rows of the whole call it covers
+    g = torch.Generator().manual_seed(23)
+    B, H, L, bs = 1, 4, 3000, 128
+    q = torch.randn(B, H, L, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(B, 2, L, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(B, 2, L, 128, generator=g).bfloat16().cuda()
+    N = (L + bs - 1) // bs
+    bits = O.pack_bool(random_mask(B, H, N, 0.3, g)).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    full = lib.sparse_attention(q, k, v, bits, bs, status=status)
+    for lo, hi in ((0, 1024), (1024, 2304), (2304, L)):
+        part = lib.sparse_attention(q, k, v, bits, bs, status=status, rows=(lo, hi))
+        assert part.shape == (B, hi - lo, H, 128)
+        assert torch.equal(part, full[:, lo:hi])
+    assert int(status.item()) == 0
+    with pytest.raises(ValueError):
+        lib.sparse_attention(q, k, v, bits, bs, rows=(100, 1024))  # not on a 128-row boundary
