@@ -81,9 +81,16 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """nvidia-smi clock / throttle-reason sampling around the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler is started (and its first sample awaited) before the warm-up and
+    stopped after the last measurement; `mark_begin`/`mark_end` bracket the timed
+    loop.  The summary uses the samples taken inside that window when there are
+    any; a timed loop shorter than the sampling period (the 8-GPU layer takes a
+    few ms) falls back to every sample taken under load during the bench and says
+    so in `window`."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -91,6 +98,7 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.path = os.path.join(HERE, "gpurun_out", f"clocks_gpu{index}.csv")
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -98,10 +106,19 @@ class ClockSampler:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 10.0  # nvidia-smi takes a moment to start
+            while time.time() < deadline and os.path.getsize(self.path) == 0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
+
+    def mark_begin(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -113,25 +130,32 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
+        from datetime import datetime
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]) if parts[3] not in ("[N/A]", "") else 0.0,
-                             parts[5:9]))
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]),
+                             float(parts[4]) if parts[4] not in ("[N/A]", "") else 0.0, parts[6:10]))
             except ValueError:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [r for r in rows if r[2] > 200.0] or rows
+        window = "timed region"
+        use = [r for r in rows if self.t0 is not None and self.t1 is not None and self.t0 <= r[0] <= self.t1]
+        if not use:
+            window = "whole bench under load (timed region shorter than the sampling period)"
+            use = [r for r in rows if r[3] > 200.0] or rows
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        reasons = sorted({names[i] for r in use for i, v in enumerate(r[4]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[1] for r in use), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": reasons, "samples": len(use), "window": window,
+                "power_w": round(statistics.median(r[3] for r in use), 1)}
 
 
 def causal_pairs(bits: torch.Tensor, L: int, bs: int) -> int:
@@ -338,7 +362,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import fftsparse_b200 as F
-    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views, sharded_prefill
+    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views, row_chunks, sharded_prefill
     from fftsparse_b200.synthetic import make_inputs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -373,20 +397,25 @@ def run_ours(args):
 
     stream = torch.cuda.current_stream(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # clocks are sampled from the first warm-up step to the end of the timed loop
-    with ClockSampler(local_rank) as clocks:
-        for _ in range(max(3, args.warmup)):
-            step()
-        torch.cuda.synchronize(dev)
-        barrier()
-        torch.cuda.synchronize(dev)
-        start.record(stream)
-        for _ in range(args.steps):
-            step()
-        end.record(stream)
-        torch.cuda.synchronize(dev)
-        barrier()
+    # clocks are sampled from before the first warm-up step to the last measurement
+    clocks = ClockSampler(local_rank).__enter__()
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    clocks.mark_begin()
+    start.record(stream)
+    h0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to issue one step
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.mark_end()
+    barrier()
     ms = start.elapsed_time(end) / args.steps
+    launches_per_step = 6 if world == 1 else 5 + len(row_chunks(L)) + 3
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -471,6 +500,10 @@ def run_ours(args):
         del q, k, v
         torch.cuda.empty_cache()
 
+        # N = 1: the drop-in operator on the whole layer.  N > 1: each rank receives
+        # its own q/k/v heads, runs its shard with the copy-engine all-gather, and
+        # reads back its own heads of the gathered output (all ranks together read
+        # the whole output once).
         def e2e_step():
             qd = qh.to(dev, non_blocking=True)
             kd = kh.to(dev, non_blocking=True)
@@ -479,23 +512,9 @@ def run_ours(args):
                 o = F.myattn_prefill(qd, kd, vd, 0, **kw)
                 res_h.copy_(o, non_blocking=True)
             else:
-                from fftsparse_b200.dist import gather_heads  # noqa: F401
-                full = sharded_prefill(qd, kd, vd, 0, num_kv_heads=HKV // world, **kw)
+                full = sharded_prefill(qd, kd, vd, 0, num_heads=HQ, num_kv_heads=HKV, inputs_are_local=True,
+                                      gather=pg, **kw)
                 res_h.copy_(full[:, shard.h_lo:shard.h_hi], non_blocking=True)
-
-        # note: for N > 1 each rank receives only its own q/k/v heads
-        if world > 1:
-            def e2e_step():  # noqa: F811
-                qd = qh.to(dev, non_blocking=True)
-                kd = kh.to(dev, non_blocking=True)
-                vd = vh.to(dev, non_blocking=True)
-                m = F.fft_block_mask(qd, kd, **kw)
-                lo = torch.empty(1, shard.heads, L, HEAD_DIM, dtype=torch.bfloat16, device=dev)
-                F.sparse_attention(qd, kd, vd, m.bits, BLOCK, out=lo.permute(0, 2, 1, 3))
-                full = torch.empty(1, HQ, L, HEAD_DIM, dtype=torch.bfloat16, device=dev)
-                from fftsparse_b200.dist import gather_heads
-                gather_heads(lo, full)
-                res_h.copy_(lo, non_blocking=True)
 
         e2e_step()
         torch.cuda.synchronize(dev)
@@ -511,14 +530,17 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": round(float(te.item()), 3), "unit": UNIT,
-               "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 2),
-               "d2h_bytes_per_step": int(res_h.numel() * 2), "steps": args.e2e_steps}
+               "h2d_bytes_per_step": int((qh.numel() + kh.numel() + vh.numel()) * 2) * world,
+               "d2h_bytes_per_step": int(res_h.numel() * 2) * world, "steps": args.e2e_steps,
+               "bytes": "whole job (every rank copies its own heads)" if world > 1 else "one GPU"}
 
     ttft = None
     if not args.no_ttft:
         ttft = run_ttft(args, dev, world, rank, stream, barrier, pg)
     if pg is not None and int(pg.status.item()) != 0:
         raise RuntimeError("the copy-engine all-gather reported a wait time-out (a peer never delivered its rows)")
+    torch.cuda.synchronize(dev)
+    clocks.__exit__(None, None, None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -544,11 +566,14 @@ def run_ours(args):
                        "l2": "inputs (3.2 GB) larger than L2; no flush"},
             "clocks": clocks.summary(),
             "e2e": e2e,
-            "gpu_launches": 6 * args.steps,  # 2 pool + select stage 1 + stage 2 + mask build + attention
+            # per layer: 2 pool + select stage 1 + stage 2 + mask build + attention; N > 1
+            # runs the attention as row chunks and adds two flag stores and one wait
+            "gpu_launches": launches_per_step * args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "stages": stages,
             "gqa_native_ms_per_layer": round(gqa_native_ms, 4),
+            "host_issue_ms_per_step": round(host_ms, 4),
             "ttft": ttft,
         }
         emit(line)

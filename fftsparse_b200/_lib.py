@@ -43,8 +43,8 @@ EXPORTS = {
     "ffts_ipc_handle": (_I32, [_P, _P, _P]),
     "ffts_ipc_open": (_I32, [_P, _I64, _P]),
     "ffts_ipc_close": (_I32, [_P, _I64]),
-    "ffts_copy_rows": (_I32, [_P, _P, _I64, _I64, _I64, _P]),
-    "ffts_signal": (_I32, [_P, _I32, _P]),
+    "ffts_copy_rows": (_I32, [_P, _I32, _P, _I64, _I64, _I64, _P]),
+    "ffts_signal": (_I32, [_P, _I32, _I32, _P]),
     "ffts_wait_flags": (_I32, [_P, _I32, _I32, _P, _P]),
 }
 

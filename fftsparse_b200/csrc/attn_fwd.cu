@@ -803,10 +803,10 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
     FFTS_CUDA(cudaGetSymbolAddress(&sink, g_attn_status_sink));
     p.status = static_cast<int *>(sink);
   }
-  FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes));
   // the largest shared-memory carveout, so that two CTAs fit on an SM
-  FFTS_CUDA(cudaFuncSetAttribute(sparse_attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 int(cudaSharedmemCarveoutMaxShared)));
+  rc = ensure_func_smem(reinterpret_cast<const void *>(&sparse_attn_kernel), SmemLayout::bytes,
+                        int(cudaSharedmemCarveoutMaxShared));
+  if (rc) return rc;
   const unsigned grid = unsigned(B * H * p.qt_cnt);
   sparse_attn_kernel<<<grid, kThreads, SmemLayout::bytes, stream>>>(mq, mk, mv, p);
   FFTS_CUDA(cudaGetLastError());

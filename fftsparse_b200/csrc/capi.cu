@@ -7,6 +7,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <map>
+#include <mutex>
 #include <string>
 
 #include "ffts_common.cuh"
@@ -27,6 +29,20 @@ void set_error(int code, const char *fmt, ...) {
 int cuda_status(cudaError_t e, const char *what) {
   set_error(FFTS_E_CUDA, "%s failed: %s", what, cudaGetErrorString(e));
   return FFTS_E_CUDA;
+}
+
+int ensure_func_smem(const void *func, int bytes, int carveout) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, int>, int> done;  // (function, device) -> limit set
+  int dev = 0;
+  FFTS_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({func, dev});
+  if (it != done.end() && it->second >= bytes) return FFTS_OK;
+  FFTS_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (carveout >= 0) FFTS_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, carveout));
+  done[{func, dev}] = bytes;
+  return FFTS_OK;
 }
 
 int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t sb,

@@ -14,6 +14,10 @@ namespace ffts {
 // ------------------------------------------------------------ error state
 void set_error(int code, const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
+// Raise func's dynamic shared-memory limit to at least bytes (and, if carveout >= 0,
+// set its preferred carveout) on the current device; the attribute calls are made
+// only when the value grows, so per-call launches skip them.
+int ensure_func_smem(const void *func, int bytes, int carveout = -1);
 
 #define FFTS_REQUIRE(cond, ...)                          \
   do {                                                   \

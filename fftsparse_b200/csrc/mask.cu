@@ -1212,8 +1212,10 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   const unsigned grid1 = unsigned(nF + nDG + int(BH));
 #define FFTS_STAGE1(RR)                                                                                          \
   case RR: {                                                                                                     \
-    FFTS_CUDA(cudaFuncSetAttribute(select_stage1_kernel<T, RR>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
-                                   int(smem1)));                                                                 \
+    {                                                                                                            \
+      const int rc1 = ensure_func_smem(reinterpret_cast<const void *>(&select_stage1_kernel<T, RR>), int(smem1)); \
+      if (rc1) return rc1;                                                                                       \
+    }                                                                                                            \
     select_stage1_kernel<T, RR><<<grid1, 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, \
                                                                int(BH), nDG, gr, gmax, ws.partial, ws.nv,         \
                                                                ws.colsel, ws.lastsel);                           \
@@ -1236,13 +1238,19 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   FFTS_CUDA(cudaGetLastError());
   // stage 2: stripe decision, inverse FFT, lag selection
   const size_t smem2 = size_t(M / 2 + M) * sizeof(float2) + size_t(N) * 8;
-  FFTS_CUDA(cudaFuncSetAttribute(corr_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem2)));
+  {
+    const int rc2 = ensure_func_smem(reinterpret_cast<const void *>(&corr_select_kernel), int(smem2));
+    if (rc2) return rc2;
+  }
   corr_select_kernel<<<BH, 512, smem2, stream>>>(ws.partial, nchunk, N, M, p, ws.nv, ws.stripe, is_stripe, svar,
                                                  corr, csum, ws.tausel);
   FFTS_CUDA(cudaGetLastError());
   const int RT = N <= 1024 ? 16 : max(1, 16384 / N);  // mask rows per CTA
   const size_t smem4 = size_t(RT) * D * 8 + size_t(RT) * N * 4 + size_t(RT) * W * 4 + 8 * 256 * 4 + size_t(RT) * 4;
-  FFTS_CUDA(cudaFuncSetAttribute(mask_build_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem4)));
+  {
+    const int rc4 = ensure_func_smem(reinterpret_cast<const void *>(&mask_build_kernel<T>), int(smem4));
+    if (rc4) return rc4;
+  }
   mask_build_kernel<T><<<dim3(unsigned(ceil_div(N, RT)), BH), 256, smem4, stream>>>(
       qb, kb, int(H), int(Hkv), int(D), p, RT, ws.stripe, ws.tausel, ws.colsel, ws.lastsel, bits, row_count);
   FFTS_CUDA(cudaGetLastError());

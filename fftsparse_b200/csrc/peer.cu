@@ -13,15 +13,15 @@
 //       IPC; the offset of the buffer inside its allocation travels with the
 //       handle, so buffers from torch's caching allocator work);
 //   ffts_copy_rows   one strided copy (height rows of width bytes, same pitch on
-//       both sides) on the caller's stream;
-//   ffts_signal      a one-thread kernel storing an epoch number into a peer's flag
-//       with release semantics at system scope, queued after the copies;
+//       both sides) to each of n destinations, on the caller's stream;
+//   ffts_signal      one kernel storing an epoch number into each of n flags with
+//       release semantics at system scope, queued after the copies;
 //   ffts_wait_flags  a one-warp kernel that waits, with acquire loads, until every
 //       flag holds at least the epoch; the wait is bounded (about 2 s of SM
 //       cycles) and on a time-out writes status 5 and returns.
 //
-// Peers' memory is only ever touched by copy engines and by the single flag
-// store: no TMA copy, and no multicast, reads another GPU's memory.
+// Peers' memory is only ever touched by copy engines and by the flag stores: no
+// TMA copy, and no multicast, reads another GPU's memory.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -34,8 +34,15 @@ namespace peer {
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.965 GHz
 constexpr int kErrPeerTimeout = 5;
 
-__global__ void signal_kernel(int32_t *flag, int32_t value) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
+constexpr int kMaxPeers = 32;
+
+struct FlagList {
+  int32_t *flag[kMaxPeers];
+};
+
+__global__ void signal_kernel(FlagList flags, int n, int32_t value) {
+  if (int(threadIdx.x) < n)
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.flag[threadIdx.x]), "r"(value) : "memory");
 }
 
 __global__ void wait_kernel(const int32_t *flags, int n, int32_t epoch, int32_t *status) {
@@ -109,17 +116,23 @@ FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset) {
   return FFTS_OK;
 }
 
-FFTS_API int32_t ffts_copy_rows(void *dst, const void *src, int64_t pitch, int64_t width, int64_t height,
-                                void *stream) {
-  FFTS_REQUIRE(dst && src && width > 0 && height > 0 && pitch >= width, "copy_rows: bad argument");
-  FFTS_CUDA(cudaMemcpy2DAsync(dst, size_t(pitch), src, size_t(pitch), size_t(width), size_t(height),
-                              cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+FFTS_API int32_t ffts_copy_rows(void *const *dsts, int32_t n, const void *src, int64_t pitch, int64_t width,
+                                int64_t height, void *stream) {
+  FFTS_REQUIRE(dsts && src && n >= 0 && width > 0 && height > 0 && pitch >= width, "copy_rows: bad argument");
+  for (int i = 0; i < n; ++i)
+    FFTS_CUDA(cudaMemcpy2DAsync(dsts[i], size_t(pitch), src, size_t(pitch), size_t(width), size_t(height),
+                                cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
   return FFTS_OK;
 }
 
-FFTS_API int32_t ffts_signal(int32_t *flag, int32_t value, void *stream) {
-  FFTS_REQUIRE(flag && (reinterpret_cast<uintptr_t>(flag) & 3) == 0, "signal: bad flag address");
-  peer::signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, value);
+FFTS_API int32_t ffts_signal(int32_t *const *flags, int32_t n, int32_t value, void *stream) {
+  FFTS_REQUIRE(flags && n >= 1 && n <= peer::kMaxPeers, "signal: bad argument");
+  peer::FlagList fl{};
+  for (int i = 0; i < n; ++i) {
+    FFTS_REQUIRE(flags[i] && (reinterpret_cast<uintptr_t>(flags[i]) & 3) == 0, "signal: bad flag address");
+    fl.flag[i] = flags[i];
+  }
+  peer::signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, n, value);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }

@@ -190,6 +190,16 @@ class PeerGather:
             self.peer_bufs[p] = ptrs[:2]
             self.peer_flags[p] = ptrs[2]
         self.stream = torch.cuda.Stream(device=self.device)
+        self.chunks = row_chunks(seq_len)
+        self.events = [torch.cuda.Event() for _ in self.chunks]
+        peers = sorted(self.peer_bufs)
+        # destination bases per buffer slot and the peers' flag words for this rank
+        self._dst = [(ctypes.c_void_p * max(1, len(peers)))(*[self.peer_bufs[p][slot] for p in peers])
+                     for slot in range(2)]
+        self._flags = (ctypes.c_void_p * max(1, len(peers)))(*[self.peer_flags[p] + 4 * self.rank for p in peers])
+        self._npeers = len(peers)
+        self._own_flag = (ctypes.c_void_p * 1)(self.flags.data_ptr() + 4 * self.rank)
+        self._ctypes = ctypes
         self.epoch = 0
         dist.barrier(group)  # every rank has mapped every buffer before the first push
 
@@ -197,7 +207,7 @@ class PeerGather:
         from . import _lib
         from .prefill import sparse_attention
 
-        lib, dev = self.lib, self.device
+        lib, dev, ct = self.lib, self.device, self._ctypes
         cur = torch.cuda.current_stream(dev)
         # the buffer used now was last read by this rank's pushes two calls ago
         cur.wait_stream(self.stream)
@@ -208,19 +218,20 @@ class PeerGather:
         row_bytes = D * buf.element_size()
         pitch = L * row_bytes
         local = buf.data_ptr() + shard.h_lo * pitch
+        bases = self._dst[slot]
         side = self.stream.cuda_stream
-        for lo, hi in row_chunks(L):
+        for (lo, hi), done in zip(self.chunks, self.events):
             sparse_attention(ql, kl, vl, bits, block_size, causal=causal,
                              out=buf[:, shard.h_lo:shard.h_hi, lo:hi].permute(0, 2, 1, 3), rows=(lo, hi))
-            done = torch.cuda.Event()
             done.record(cur)
             self.stream.wait_event(done)
-            for p, dst in self.peer_bufs.items():
-                _lib.check(lib.ffts_copy_rows(dst[slot] + shard.h_lo * pitch + lo * row_bytes, local + lo * row_bytes,
-                                              pitch, (hi - lo) * row_bytes, Hl, side))
-        for p, flag in self.peer_flags.items():
-            _lib.check(lib.ffts_signal(flag + 4 * self.rank, e, side))
-        _lib.check(lib.ffts_signal(self.flags.data_ptr() + 4 * self.rank, e, cur.cuda_stream))
+            off = shard.h_lo * pitch + lo * row_bytes
+            dsts = (ct.c_void_p * max(1, self._npeers))(*[b + off for b in bases])
+            _lib.check(lib.ffts_copy_rows(dsts, self._npeers, local + lo * row_bytes, pitch, (hi - lo) * row_bytes,
+                                          Hl, side))
+        if self._npeers:
+            _lib.check(lib.ffts_signal(self._flags, self._npeers, e, side))
+        _lib.check(lib.ffts_signal(self._own_flag, 1, e, cur.cuda_stream))
         _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
                                        cur.cuda_stream))
         return buf

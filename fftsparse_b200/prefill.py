@@ -146,8 +146,9 @@ def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, bloc
     Hkv = k.shape[1]
     if k.shape[0] != B or k.shape[2] != L or k.shape[3] != D or H % Hkv:
         raise ValueError(f"key_states {tuple(k.shape)} incompatible with query_states {tuple(q.shape)}")
+    cp = None
     if params is None:
-        params = derive_mask_params(L, block_size=block_size, **kwargs)
+        params, cp = _cached_params(L, block_size, kwargs)
     lib = _lib.load()
     qb = pool_blocks(q, params.block_size)
     kb = pool_blocks(k, params.block_size)
@@ -162,12 +163,34 @@ def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, bloc
     stripe_var = torch.empty(B, H, dtype=torch.float32, device=dev)
     ws_bytes = int(lib.ffts_mask_workspace_bytes(B, H, N, D))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    cp = params.to_c()
+    if cp is None:
+        cp = params.to_c()
     _lib.check(lib.ffts_block_mask(qb.data_ptr(), kb.data_ptr(), _DTYPES[q.dtype], B, H, Hkv, D,
                                    _lib.ctypes.addressof(cp), bits.data_ptr(), row_count.data_ptr(),
                                    corr.data_ptr(), corr_sum.data_ptr(), is_stripe.data_ptr(),
                                    stripe_var.data_ptr(), ws.data_ptr(), ws_bytes, _stream_ptr(dev)))
     return BlockMask(bits, row_count, corr, corr_sum, is_stripe, stripe_var, params, qb, kb)
+
+
+_PARAM_CACHE = {}
+
+
+def _cached_params(L: int, block_size: int, kwargs: dict):
+    """derive_mask_params and its C struct, reused across calls with the same length
+    and arguments (a prefill calls the operator once per layer with the same ones)."""
+    try:
+        key = (L, block_size, tuple(sorted(kwargs.items())))
+        hit = _PARAM_CACHE.get(key)
+    except TypeError:  # an unhashable argument: derive afresh
+        key, hit = None, None
+    if hit is None:
+        params = derive_mask_params(L, block_size=block_size, **kwargs)
+        hit = (params, params.to_c())
+        if key is not None:
+            if len(_PARAM_CACHE) > 256:
+                _PARAM_CACHE.clear()
+            _PARAM_CACHE[key] = hit
+    return hit
 
 
 def _dense_causal_bits(B: int, H: int, N: int, device) -> torch.Tensor:

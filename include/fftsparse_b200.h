@@ -212,17 +212,19 @@ FFTS_API int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const v
  *
  * ffts_ipc_handle: a 64-byte IPC handle of the allocation holding ptr, and ptr's
  *   offset inside it.  ffts_ipc_open: the peer-side address of that buffer.
- * ffts_copy_rows: height rows of width bytes, pitch bytes apart on both sides.
- * ffts_signal: store value into *flag (release, system scope) after the stream's
- *   earlier work.  ffts_wait_flags: wait until flags[0..n) >= epoch (acquire);
+ * ffts_copy_rows: height rows of width bytes, pitch bytes apart on both sides,
+ *   from src to each of dsts[0..n).
+ * ffts_signal: store value into *flags[i], i < n <= 32 (release, system scope),
+ *   after the stream's earlier work.  ffts_wait_flags: wait until flags[0..n) >=
+ *   epoch (acquire);
  *   bounded at about 2 s, after which *status = 5 and the wait returns.
  */
 FFTS_API int32_t ffts_ipc_handle(const void *ptr, void *handle, int64_t *offset);
 FFTS_API int32_t ffts_ipc_open(const void *handle, int64_t offset, void **ptr);
 FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset);
-FFTS_API int32_t ffts_copy_rows(void *dst, const void *src, int64_t pitch, int64_t width,
-                               int64_t height, void *stream);
-FFTS_API int32_t ffts_signal(int32_t *flag, int32_t value, void *stream);
+FFTS_API int32_t ffts_copy_rows(void *const *dsts, int32_t n, const void *src, int64_t pitch,
+                               int64_t width, int64_t height, void *stream);
+FFTS_API int32_t ffts_signal(int32_t *const *flags, int32_t n, int32_t value, void *stream);
 FFTS_API int32_t ffts_wait_flags(const int32_t *flags, int32_t n, int32_t epoch, int32_t *status,
                                  void *stream);
 

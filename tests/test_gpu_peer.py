@@ -1,6 +1,9 @@
-"""The copy-engine all-gather of the sharded prefill (dist.PeerGather) on two GPUs:
-its output equals the NCCL all-gather path bit for bit, on consecutive calls
-(both of its alternating buffers, and a reuse).  Skipped on a box with one GPU."""
+"""The copy-engine all-gather of the sharded prefill (dist.PeerGather).
+
+On two GPUs its output equals the NCCL all-gather path bit for bit, on
+consecutive calls (both of its alternating buffers, and a reuse); skipped on a
+box with one GPU.  On one GPU: the row copy, flag store and bounded wait entry
+points, including a wait that runs out on a flag nothing sets."""
 import os
 import socket
 
@@ -64,3 +67,51 @@ def test_peer_gather_equals_nccl_gather():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert results == {0: True, 1: True}
+
+
+def _ptrs(*addrs):
+    import ctypes
+    return (ctypes.c_void_p * len(addrs))(*addrs)
+
+
+def test_copy_rows_signal_wait_one_gpu():
+    """The copy, flag-store and wait entry points on one GPU: a strided row copy
+    to two destinations, an epoch stored into two flags, and a wait that sees it
+    (status stays 0)."""
+    from fftsparse_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    H, L, D = 3, 640, 128
+    src = torch.randn(H, L, D, device=dev).to(torch.bfloat16)
+    dst = [torch.zeros(H, L, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    pitch, row = L * D * 2, D * 2
+    lo, hi = 128, 512
+    _lib.check(lib.ffts_copy_rows(_ptrs(*[d.data_ptr() + lo * row for d in dst]), 2, src.data_ptr() + lo * row,
+                                  pitch, (hi - lo) * row, H, stream))
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(lib.ffts_signal(_ptrs(flags.data_ptr(), flags.data_ptr() + 4), 2, 7, stream))
+    _lib.check(lib.ffts_wait_flags(flags.data_ptr(), 2, 7, status.data_ptr(), stream))
+    torch.cuda.synchronize(dev)
+    for d in dst:
+        assert torch.equal(d[:, lo:hi], src[:, lo:hi])
+        assert not d[:, :lo].any() and not d[:, hi:].any()
+    assert flags.tolist() == [7, 7]
+    assert int(status.item()) == 0
+
+
+def test_wait_flags_times_out_with_status():
+    """A wait on a flag that nothing sets ends by itself (about 2 s of SM cycles)
+    with status 5; the context stays usable afterwards."""
+    from fftsparse_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    flags = torch.tensor([3, 0], dtype=torch.int32, device=dev)  # flag 1 never reaches epoch 3
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(lib.ffts_wait_flags(flags.data_ptr(), 2, 3, status.data_ptr(), stream))
+    torch.cuda.synchronize(dev)
+    assert int(status.item()) == 5
+    x = torch.ones(4, device=dev)
+    assert float((x + 1).sum().item()) == 8.0
