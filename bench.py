@@ -13,8 +13,9 @@ N = 1 calls the drop-in ``myattn_prefill`` with repeat_kv-expanded k/v, the
 exact call of the reference's benchmark
 (eval/efficiency/benchmark_attention_multilayer.py:146-157, :308).  N > 1
 (launched by torchrun, one rank per GPU, NCCL) shards the 8 KV groups over the
-ranks and all-gathers the head-major outputs on the copy engines, overlapped with
-the attention (fftsparse_b200/dist.py, PeerGather); total work is fixed, so the
+ranks; the attention kernel's epilogue stores each output tile into every
+peer's head-major buffer over NVLink, so the all-gather runs alongside the math
+(fftsparse_b200/dist.py, PeerGather); total work is fixed, so the
 scaling is strong.  ``--impl reference`` times the CPU
 restatement of the reference path (oracle/) on the host cores instead.
 """
@@ -243,7 +244,7 @@ class Llama8BShape:
     layer's attention is fftsparse_b200's operator on un-expanded GQA k/v.
     With world > 1 each rank keeps only its KV groups' columns of the QKV
     projection, runs attention for its heads, and one all-gather per layer
-    (on the copy engines when a PeerGather is given) assembles the head-major
+    (in the attention epilogue when a PeerGather is given) assembles the head-major
     output that o_proj consumes (o_proj and the MLP are replicated)."""
 
     H, HKV, D, HIDDEN, INTER, VOCAB = 32, 8, 128, 4096, 14336, 128256
@@ -362,7 +363,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import fftsparse_b200 as F
-    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views, row_chunks, sharded_prefill
+    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views, sharded_prefill
     from fftsparse_b200.synthetic import make_inputs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -383,7 +384,7 @@ def run_ours(args):
     q, k, v = make_inputs(L, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16, device=str(dev))
     torch.cuda.synchronize(dev)
 
-    # N > 1: the output all-gather runs on the copy engines, overlapped with the attention
+    # N > 1: the attention epilogue pushes the output rows to every peer over NVLink
     pg = PeerGather(HQ, L, HEAD_DIM, device=dev) if world > 1 else None
 
     def step():
@@ -415,7 +416,7 @@ def run_ours(args):
     clocks.mark_end()
     barrier()
     ms = start.elapsed_time(end) / args.steps
-    launches_per_step = 6 if world == 1 else 5 + len(row_chunks(L)) + 3
+    launches_per_step = 6 if world == 1 else 8
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -501,7 +502,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
 
         # N = 1: the drop-in operator on the whole layer.  N > 1: each rank receives
-        # its own q/k/v heads, runs its shard with the copy-engine all-gather, and
+        # its own q/k/v heads, runs its shard with the peer-memory all-gather, and
         # reads back its own heads of the gathered output (all ranks together read
         # the whole output once).
         def e2e_step():
@@ -538,7 +539,7 @@ def run_ours(args):
     if not args.no_ttft:
         ttft = run_ttft(args, dev, world, rank, stream, barrier, pg)
     if pg is not None and int(pg.status.item()) != 0:
-        raise RuntimeError("the copy-engine all-gather reported a wait time-out (a peer never delivered its rows)")
+        raise RuntimeError("the peer-memory all-gather reported a wait time-out (a peer never delivered its rows)")
     torch.cuda.synchronize(dev)
     clocks.__exit__(None, None, None)
 
@@ -560,14 +561,15 @@ def run_ours(args):
             "config": {"workload": f"cfg3: L={L}, Hq={HQ}, Hkv={HKV}, D={HEAD_DIM}, block {BLOCK}, keep ratio "
                                    f"{args.keep_ratio} (topk mode, efficiency-script ratios); "
                                    + ("drop-in myattn_prefill with repeat_kv-expanded k/v" if world == 1 else
-                                      f"KV groups sharded {HKV // world} per rank; output all-gather on the copy engines, overlapped"),
+                                      f"KV groups sharded {HKV // world} per rank; output all-gather fused into the "
+                                      f"attention epilogue (peer stores over NVLink)"),
                        "model": "Llama-3.1-8B attention-layer shape", "seq_len": L, "global_batch": 1,
                        "parallelism": "single GPU" if world == 1 else f"kv-group x{world}",
                        "l2": "inputs (3.2 GB) larger than L2; no flush"},
             "clocks": clocks.summary(),
             "e2e": e2e,
             # per layer: 2 pool + select stage 1 + stage 2 + mask build + attention; N > 1
-            # runs the attention as row chunks and adds two flag stores and one wait
+            # adds one flag store and one bounded wait
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roofline,
             "cpu_baseline": cpu,

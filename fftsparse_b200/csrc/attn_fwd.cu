@@ -285,6 +285,8 @@ constexpr int BDRAIN = BPF + 2;
 // is issued): with a single P barrier it could complete two phases before the
 // issuer observes the first, and the parity wait would alias.
 
+constexpr int kMaxPeerOut = 15;  // peer output buffers one launch also writes
+
 struct Params {
   int B, H, Hkv, L, bs, bs_shift, causal;
   int nq;         // query tiles (128 rows) per head
@@ -297,6 +299,11 @@ struct Params {
   int out_row0;              // query row written at output row 0
   float scale_log2;
   int *status;
+  // Peer GPUs' output buffers (CUDA IPC mappings, same strides as out): every
+  // output tile is also stored into each of them, so a sharded prefill's
+  // all-gather rides on the epilogue over NVLink.
+  int n_peers;
+  __nv_bfloat16 *peer_out[kMaxPeerOut];
 };
 
 // Bits of 32 consecutive 64-key tiles [32*tw, 32*tw+32) of one mask row: a
@@ -333,7 +340,7 @@ struct TileCursor {
 
 __global__ void __launch_bounds__(kThreads, 2)
     sparse_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, Params prm) {
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params prm) {
   extern __shared__ __align__(16) uint8_t smem_dyn[];
   uint8_t *smem = smem_dyn;
   // SWIZZLE_128B TMA boxes and MMA descriptors need 1024-byte aligned tiles
@@ -681,22 +688,26 @@ __global__ void __launch_bounds__(kThreads, 2)
       atomicCAS(prm.status, 0, kErrTimeoutSoftmax);
     }
     fence_after();
-    // epilogue: O / l -> bf16 -> out[b, row, h, :]
-    const bool store = row_g < prm.L;
-    __nv_bfloat16 *dst =
-        prm.out + int64_t(b) * prm.os_b + int64_t(row_g - prm.out_row0) * prm.os_l + int64_t(h) * prm.os_h;
+    // epilogue: O / l -> bf16 -> out[b, row, h, :] (and the same rows of every
+    // peer buffer).  The bf16 tile is staged in the Q tile's shared memory: with
+    // ok, every MMA has completed (the last PV commit covers them all) and no
+    // copy is in flight, and with no tiles Q was never loaded.  Row r's 16-byte
+    // chunk j sits at r * 256 + ((j ^ (r & 15)) << 4), so the row-per-thread
+    // writes and the row-contiguous reads below are both free of bank conflicts.
+    const int tile_rows = min(kBM, prm.L - qt * kBM);
     const float inv_l = (ok && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+    uint8_t *stage = smem + SmemLayout::q;
+    if (ok) {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float o[32];
-      if (ntiles > 0 && ok) {
-        tmem_ld32(tm_o + lane_off + c * 32, o);
-        tmem_wait_ld();
-      } else {
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (ntiles > 0) {
+          tmem_ld32(tm_o + lane_off + c * 32, o);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0.0f;
-      }
-      if (store) {
+          for (int e = 0; e < 32; ++e) o[e] = 0.0f;
+        }
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           uint32_t w[4];
@@ -706,9 +717,42 @@ __global__ void __launch_bounds__(kThreads, 2)
                 __floats2bfloat162_rn(o[q4 * 8 + 2 * e] * inv_l, o[q4 * 8 + 2 * e + 1] * inv_l);
             w[e] = *reinterpret_cast<const uint32_t *>(&pr);
           }
-          *reinterpret_cast<uint4 *>(dst + c * 32 + q4 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          const int j = c * 4 + q4;
+          *reinterpret_cast<uint4 *>(stage + r * 256 + ((j ^ (r & 15)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+    }
+    // every softmax thread arrives here; the tile is copied out only if all four
+    // warps completed (ok is uniform within a warp, not across the warps)
+    int all_ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(all_ok)
+        : "r"(int(ok))
+        : "memory");
+    if (all_ok) {
+      // each warp instruction stores two whole 256-byte rows
+      const int64_t off = int64_t(b) * prm.os_b + int64_t(qt * kBM - prm.out_row0) * prm.os_l + int64_t(h) * prm.os_h;
+#pragma unroll 1
+      for (int d = -1; d < prm.n_peers; ++d) {
+        __nv_bfloat16 *base = (d < 0 ? prm.out : prm.peer_out[d]) + off;
+#pragma unroll 4
+        for (int k = r; k < tile_rows * 16; k += kBM) {
+          const int row = k >> 4, j = k & 15;
+          const uint4 val = *reinterpret_cast<const uint4 *>(stage + row * 256 + ((j ^ (row & 15)) << 4));
+          *reinterpret_cast<uint4 *>(base + int64_t(row) * prm.os_l + j * 8) = val;
+        }
+      }
+      // the peers learn of these rows from a flag a later kernel on this
+      // stream stores; make them visible system-wide before the CTA retires
+      if (prm.n_peers > 0) __threadfence_system();
+    } else if (row_g < prm.L) {
+      // after a time-out copies may still land in shared memory: zeros, row per thread
+      __nv_bfloat16 *dst =
+          prm.out + int64_t(b) * prm.os_b + int64_t(row_g - prm.out_row0) * prm.os_l + int64_t(h) * prm.os_h;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4 *>(dst + c * 8) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
 
@@ -759,8 +803,8 @@ __device__ int g_attn_status_sink;
 
 int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv, int64_t L,
                     int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs, const uint32_t *bits, int bs,
-                    int causal, void *out, const int64_t *os, int64_t row_lo, int64_t row_hi, int32_t *status,
-                    cudaStream_t stream) {
+                    int causal, void *out, const int64_t *os, int64_t row_lo, int64_t row_hi,
+                    void *const *peer_out, int n_peers, int32_t *status, cudaStream_t stream) {
   using namespace attn;
   FFTS_REQUIRE(q && k && v && bits && out && qs && ks && vs && os, "sparse_attn: NULL argument");
   FFTS_REQUIRE(D == kD, "sparse_attn: head_dim must be 128 (got %lld)", (long long)D);
@@ -780,6 +824,11 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   FFTS_REQUIRE(row_lo >= 0 && row_lo < row_hi && row_hi <= L && row_lo % kBM == 0 && (row_hi % kBM == 0 || row_hi == L),
                "sparse_attn: query rows [%lld, %lld) must lie in [0, L) on %d-row boundaries", (long long)row_lo,
                (long long)row_hi, kBM);
+  FFTS_REQUIRE(n_peers >= 0 && n_peers <= kMaxPeerOut && (n_peers == 0 || peer_out),
+               "sparse_attn: at most %d peer outputs", kMaxPeerOut);
+  for (int i = 0; i < n_peers; ++i)
+    FFTS_REQUIRE(peer_out[i] && (reinterpret_cast<uintptr_t>(peer_out[i]) & 15) == 0,
+                 "sparse_attn: peer output %d must be non-NULL and 16-byte aligned", i);
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, q, L, H, B, qs, kBM);
   if (!rc) rc = make_map(&mk, k, L, Hkv, B, ks, kBN);
@@ -796,6 +845,8 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   p.qt_cnt = int(ceil_div(row_hi, kBM) - row_lo / kBM);
   p.out_row0 = int(row_lo);
   p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
+  p.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) p.peer_out[i] = static_cast<__nv_bfloat16 *>(peer_out[i]);
   if (status) {
     p.status = status;
   } else {

@@ -57,7 +57,8 @@ int ensure_tables();
 int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
                     int64_t L, int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs,
                     const uint32_t *bits, int bs, int causal, void *out, const int64_t *os,
-                    int64_t row_lo, int64_t row_hi, int32_t *status, cudaStream_t stream);
+                    int64_t row_lo, int64_t row_hi, void *const *peer_out, int n_peers, int32_t *status,
+                    cudaStream_t stream);
 
 static int check_device() {
   int dev = 0;
@@ -134,7 +135,7 @@ int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_
   int rc = check_device();
   if (rc) return rc;
   return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
-                         causal, out, out_strides, 0, L, status, static_cast<cudaStream_t>(stream));
+                         causal, out, out_strides, 0, L, nullptr, 0, status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
@@ -146,7 +147,22 @@ int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const void *v, i
   int rc = check_device();
   if (rc) return rc;
   return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
-                         causal, out, out_strides, row_lo, row_hi, status, static_cast<cudaStream_t>(stream));
+                         causal, out, out_strides, row_lo, row_hi, nullptr, 0, status,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_sparse_attn_fwd_push(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
+                                  int64_t L, int64_t D, const int64_t *q_strides, const int64_t *k_strides,
+                                  const int64_t *v_strides, const uint32_t *mask_bits, int32_t block_size,
+                                  int32_t causal, int64_t row_lo, int64_t row_hi, void *out,
+                                  const int64_t *out_strides, void *const *peer_out, int32_t n_peers,
+                                  int32_t *status, void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
+                         causal, out, out_strides, row_lo, row_hi, peer_out, n_peers, status,
+                         static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -7,15 +7,19 @@
 // the next row chunk's attention does not overlap it.  These entry points let
 // the host side (fftsparse_b200/dist.py, PeerGather) push each finished row chunk
 // straight into the peers' output buffers with cudaMemcpy2DAsync over NVLink: the
-// copy engines move the data while the SMs compute the next chunk.
+// copy engines move the data while the SMs compute the next chunk.  Each peer's
+// copies go on a stream of their own, so that the pushes to different peers run
+// side by side on different copy engines (one stream's copies run one at a time).
 //
 //   ffts_ipc_handle / ffts_ipc_open / ffts_ipc_close  map a peer's buffer (CUDA
 //       IPC; the offset of the buffer inside its allocation travels with the
 //       handle, so buffers from torch's caching allocator work);
 //   ffts_copy_rows   one strided copy (height rows of width bytes, same pitch on
-//       both sides) to each of n destinations, on the caller's stream;
-//   ffts_signal      one kernel storing an epoch number into each of n flags with
-//       release semantics at system scope, queued after the copies;
+//       both sides) to each of n destinations, copy i on stream i, each stream
+//       first waiting for an event (the chunk's attention) when one is given;
+//   ffts_signal      a small kernel storing an epoch number into flags with
+//       release semantics at system scope, flag i queued on stream i after the
+//       copies there (one launch per run of flags that share a stream);
 //   ffts_wait_flags  a one-warp kernel that waits, with acquire loads, until every
 //       flag holds at least the epoch; the wait is bounded (about 2 s of SM
 //       cycles) and on a time-out writes status 5 and returns.
@@ -116,24 +120,34 @@ FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset) {
   return FFTS_OK;
 }
 
-FFTS_API int32_t ffts_copy_rows(void *const *dsts, int32_t n, const void *src, int64_t pitch, int64_t width,
-                                int64_t height, void *stream) {
-  FFTS_REQUIRE(dsts && src && n >= 0 && width > 0 && height > 0 && pitch >= width, "copy_rows: bad argument");
-  for (int i = 0; i < n; ++i)
+FFTS_API int32_t ffts_copy_rows(void *const *dsts, void *const *streams, int32_t n, const void *src, int64_t pitch,
+                                int64_t width, int64_t height, void *after) {
+  FFTS_REQUIRE(dsts && streams && src && n >= 0 && width > 0 && height > 0 && pitch >= width,
+               "copy_rows: bad argument");
+  for (int i = 0; i < n; ++i) {
+    FFTS_REQUIRE(dsts[i], "copy_rows: NULL destination %d", i);
+    const cudaStream_t st = static_cast<cudaStream_t>(streams[i]);
+    if (after) FFTS_CUDA(cudaStreamWaitEvent(st, static_cast<cudaEvent_t>(after), 0));
     FFTS_CUDA(cudaMemcpy2DAsync(dsts[i], size_t(pitch), src, size_t(pitch), size_t(width), size_t(height),
-                                cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+                                cudaMemcpyDeviceToDevice, st));
+  }
   return FFTS_OK;
 }
 
-FFTS_API int32_t ffts_signal(int32_t *const *flags, int32_t n, int32_t value, void *stream) {
-  FFTS_REQUIRE(flags && n >= 1 && n <= peer::kMaxPeers, "signal: bad argument");
-  peer::FlagList fl{};
-  for (int i = 0; i < n; ++i) {
-    FFTS_REQUIRE(flags[i] && (reinterpret_cast<uintptr_t>(flags[i]) & 3) == 0, "signal: bad flag address");
-    fl.flag[i] = flags[i];
+FFTS_API int32_t ffts_signal(int32_t *const *flags, void *const *streams, int32_t n, int32_t value) {
+  FFTS_REQUIRE(flags && streams && n >= 1 && n <= 1024, "signal: bad argument");
+  for (int i = 0; i < n;) {
+    peer::FlagList fl{};
+    int c = 0;
+    for (; i + c < n && c < peer::kMaxPeers && streams[i + c] == streams[i]; ++c) {
+      int32_t *f = flags[i + c];
+      FFTS_REQUIRE(f && (reinterpret_cast<uintptr_t>(f) & 3) == 0, "signal: bad flag address");
+      fl.flag[c] = f;
+    }
+    peer::signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(streams[i])>>>(fl, c, value);
+    FFTS_CUDA(cudaGetLastError());
+    i += c;
   }
-  peer::signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fl, n, value);
-  FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }
 

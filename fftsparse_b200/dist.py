@@ -131,29 +131,43 @@ def row_chunks(L: int, parts: int = 4, tile: int = 128):
 
 
 class PeerGather:
-    """The all-gather of the sharded attention output on the GPUs' copy engines.
+    """The all-gather of the sharded attention output over NVLink peer memory,
+    overlapped with the attention itself.
 
     Created once per (heads, sequence length) by every rank of the group (it is
     collective).  Each rank holds two full head-major output buffers [1, H, L, D]
-    and maps its peers' buffers and flag words through CUDA IPC.  A call computes
-    the rank's heads in row chunks of about equal causal work directly into its
-    own buffer; after each chunk a copy stream pushes those rows into every peer's
-    buffer (cudaMemcpy2DAsync over NVLink) while the SMs compute the next chunk;
-    then it stores the call's epoch number into each peer's flag, and the calling
-    stream waits (bounded) until every rank's flag reached the epoch.  NCCL's
-    all-gather cannot overlap this way: it runs as SM kernels, and the attention
-    kernel holds every SM's shared memory and TMEM.
+    and maps its peers' buffers and flag words through CUDA IPC.  NCCL's
+    all-gather cannot overlap with the attention: it runs as SM kernels, and the
+    attention kernel holds every SM's shared memory and TMEM.  Two ways to push
+    the rank's heads into every peer's buffer instead:
+
+    * ``push="epilogue"`` (default): one attention launch whose epilogue stores
+      each finished output tile into the own buffer and, over NVLink, into every
+      peer's (ffts_sparse_attn_fwd_push), so the transfer runs tile by tile
+      alongside the math;
+    * ``push="copy"``: the rows are computed in ``chunks`` row chunks of about
+      equal causal work (row_chunks); after each chunk one copy stream per peer
+      pushes those rows with cudaMemcpy2DAsync (the copy engines) while the SMs
+      compute the next chunk.
+
+    Then the call's epoch number is stored into each peer's flag after the
+    pushes, and the calling stream waits (bounded) until every rank's flag
+    reached the epoch.
 
     The two buffers alternate between calls, so the tensor a call returns stays
     valid until the call after next; consume it (o_proj) before that.  One
-    sequence (B = 1), KV-group shards, bf16 output.  ``status`` is nonzero after a
-    wait that timed out (a peer never delivered its rows)."""
+    sequence (B = 1), KV-group shards, bf16 output.  ``status`` is nonzero after
+    a wait that timed out (a peer never delivered its rows)."""
 
-    def __init__(self, num_heads: int, seq_len: int, head_dim: int = 128, group=None, device=None):
+    def __init__(self, num_heads: int, seq_len: int, head_dim: int = 128, group=None, device=None,
+                 push: str = "epilogue", chunks: int = 4):
         import ctypes
 
         from . import _lib
 
+        if push not in ("epilogue", "copy"):
+            raise ValueError(f"push must be 'epilogue' or 'copy', got {push!r}")
+        self.push = push
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.H, self.L, self.D = num_heads, seq_len, head_dim
@@ -189,16 +203,23 @@ class PeerGather:
                 self._opened.append((ptr.value, off))
             self.peer_bufs[p] = ptrs[:2]
             self.peer_flags[p] = ptrs[2]
-        self.stream = torch.cuda.Stream(device=self.device)
-        self.chunks = row_chunks(seq_len)
-        self.events = [torch.cuda.Event() for _ in self.chunks]
         peers = sorted(self.peer_bufs)
+        # one copy stream per peer: one stream's copies run one after another, so
+        # pushes to different peers on different streams use several copy engines
+        self.streams = [torch.cuda.Stream(device=self.device) for _ in peers]
+        self.chunks = row_chunks(seq_len, chunks)
+        self.events = [torch.cuda.Event() for _ in self.chunks]
+        n = max(1, len(peers))
         # destination bases per buffer slot and the peers' flag words for this rank
-        self._dst = [(ctypes.c_void_p * max(1, len(peers)))(*[self.peer_bufs[p][slot] for p in peers])
-                     for slot in range(2)]
-        self._flags = (ctypes.c_void_p * max(1, len(peers)))(*[self.peer_flags[p] + 4 * self.rank for p in peers])
+        self._dst = [(ctypes.c_void_p * n)(*[self.peer_bufs[p][slot] for p in peers]) for slot in range(2)]
+        self._flags = (ctypes.c_void_p * n)(*[self.peer_flags[p] + 4 * self.rank for p in peers])
+        self._streams = (ctypes.c_void_p * n)(*[st.cuda_stream for st in self.streams])
         self._npeers = len(peers)
         self._own_flag = (ctypes.c_void_p * 1)(self.flags.data_ptr() + 4 * self.rank)
+        # epilogue pushes: every flag (the peers' words for this rank, then its own)
+        # is stored by one kernel on the calling stream after the attention
+        self._all_flags = (ctypes.c_void_p * (len(peers) + 1))(*list(self._flags)[:len(peers)],
+                                                                self.flags.data_ptr() + 4 * self.rank)
         self._ctypes = ctypes
         self.epoch = 0
         dist.barrier(group)  # every rank has mapped every buffer before the first push
@@ -209,8 +230,6 @@ class PeerGather:
 
         lib, dev, ct = self.lib, self.device, self._ctypes
         cur = torch.cuda.current_stream(dev)
-        # the buffer used now was last read by this rank's pushes two calls ago
-        cur.wait_stream(self.stream)
         self.epoch += 1
         e, slot = self.epoch, self.epoch % 2
         buf = self.bufs[slot]
@@ -219,19 +238,29 @@ class PeerGather:
         pitch = L * row_bytes
         local = buf.data_ptr() + shard.h_lo * pitch
         bases = self._dst[slot]
-        side = self.stream.cuda_stream
+        mine = buf[:, shard.h_lo:shard.h_hi].permute(0, 2, 1, 3)
+        if self.push == "epilogue":
+            sparse_attention(ql, kl, vl, bits, block_size, causal=causal, out=mine,
+                             peers=[b + shard.h_lo * pitch for b in bases[:self._npeers]])
+            n = self._npeers + 1
+            _lib.check(lib.ffts_signal(self._all_flags, (ct.c_void_p * n)(*([cur.cuda_stream] * n)), n, e))
+            _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
+                                           cur.cuda_stream))
+            return buf
+        # the buffer used now was last read by this rank's pushes two calls ago
+        for st in self.streams:
+            cur.wait_stream(st)
         for (lo, hi), done in zip(self.chunks, self.events):
             sparse_attention(ql, kl, vl, bits, block_size, causal=causal,
                              out=buf[:, shard.h_lo:shard.h_hi, lo:hi].permute(0, 2, 1, 3), rows=(lo, hi))
             done.record(cur)
-            self.stream.wait_event(done)
             off = shard.h_lo * pitch + lo * row_bytes
             dsts = (ct.c_void_p * max(1, self._npeers))(*[b + off for b in bases])
-            _lib.check(lib.ffts_copy_rows(dsts, self._npeers, local + lo * row_bytes, pitch, (hi - lo) * row_bytes,
-                                          Hl, side))
+            _lib.check(lib.ffts_copy_rows(dsts, self._streams, self._npeers, local + lo * row_bytes, pitch,
+                                          (hi - lo) * row_bytes, Hl, done.cuda_event))
         if self._npeers:
-            _lib.check(lib.ffts_signal(self._flags, self._npeers, e, side))
-        _lib.check(lib.ffts_signal(self._own_flag, 1, e, cur.cuda_stream))
+            _lib.check(lib.ffts_signal(self._flags, self._streams, self._npeers, e))
+        _lib.check(lib.ffts_signal(self._own_flag, (ct.c_void_p * 1)(cur.cuda_stream), 1, e))
         _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
                                        cur.cuda_stream))
         return buf

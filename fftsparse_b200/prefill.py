@@ -200,13 +200,16 @@ def _dense_causal_bits(B: int, H: int, N: int, device) -> torch.Tensor:
 
 def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: torch.Tensor,
                      block_size: int, causal: bool = True, out: Optional[torch.Tensor] = None,
-                     status: Optional[torch.Tensor] = None, rows=None) -> torch.Tensor:
+                     status: Optional[torch.Tensor] = None, rows=None, peers=None) -> torch.Tensor:
     """Block-sparse attention (ffts_sparse_attn_fwd).
 
     q [B, H, L, D], k/v [B, Hkv, L, D] bf16; bits [B, H, N, W] packed mask.
     Returns (or fills) ``out`` of shape [B, L, H, D] bf16.  With ``rows = (lo, hi)``
     only query rows [lo, hi) are computed (lo a multiple of 128, hi a multiple of
     128 or L; ffts_sparse_attn_fwd_rows) and ``out`` has shape [B, hi - lo, H, D].
+    With ``peers`` (device addresses of other GPUs' buffers laid out like ``out``,
+    mapped into this process) every output row is also stored there by the
+    kernel's epilogue (ffts_sparse_attn_fwd_push).
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_4d(name, t)
@@ -223,7 +226,13 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: to
     vs = _lib.i64_array([v.stride(0), v.stride(1), v.stride(2)])
     os_ = _lib.i64_array([out.stride(0), out.stride(2), out.stride(1)])
     st = status.data_ptr() if status is not None else None
-    if rows is None:
+    if peers:
+        arr = (_lib.ctypes.c_void_p * len(peers))(*peers)
+        _lib.check(lib.ffts_sparse_attn_fwd_push(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
+            block_size, int(bool(causal)), lo, hi, out.data_ptr(), os_, arr, len(peers), st,
+            _stream_ptr(q.device)))
+    elif rows is None:
         _lib.check(lib.ffts_sparse_attn_fwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
             block_size, int(bool(causal)), out.data_ptr(), os_, st, _stream_ptr(q.device)))

@@ -203,6 +203,26 @@ FFTS_API int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const v
                              int32_t *status, void *stream);
 
 /*
+ * ffts_sparse_attn_fwd_rows that also stores every output row into each of
+ * peer_out[0..n_peers), n_peers <= 15: other GPUs' buffers mapped into this
+ * process (CUDA IPC; ffts_ipc_open) with the strides of out, 16-byte aligned.
+ * The stores are made visible system-wide before the kernel completes, so a
+ * flag stored after it on the same stream (ffts_signal) tells a peer that its
+ * rows have arrived.  No counterpart in the reference: the sharded prefill's
+ * output all-gather, fused into the attention epilogue over NVLink.
+ */
+FFTS_API int32_t ffts_sparse_attn_fwd_push(const void *q, const void *k, const void *v, int64_t B,
+                             int64_t H, int64_t Hkv, int64_t L, int64_t D,
+                             const int64_t *q_strides /* b,h,l */,
+                             const int64_t *k_strides /* b,h,l */,
+                             const int64_t *v_strides /* b,h,l */,
+                             const uint32_t *mask_bits, int32_t block_size,
+                             int32_t causal, int64_t row_lo, int64_t row_hi, void *out,
+                             const int64_t *out_strides /* b,h,l */,
+                             void *const *peer_out, int32_t n_peers,
+                             int32_t *status, void *stream);
+
+/*
  * Copy-engine all-gather support for the sharded prefill (fftsparse_b200/dist.py,
  * PeerGather).  No counterpart in the reference, which runs on one GPU: a rank
  * maps its peers' output buffers (CUDA IPC), pushes each finished row chunk of
@@ -213,18 +233,19 @@ FFTS_API int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const v
  * ffts_ipc_handle: a 64-byte IPC handle of the allocation holding ptr, and ptr's
  *   offset inside it.  ffts_ipc_open: the peer-side address of that buffer.
  * ffts_copy_rows: height rows of width bytes, pitch bytes apart on both sides,
- *   from src to each of dsts[0..n).
- * ffts_signal: store value into *flags[i], i < n <= 32 (release, system scope),
- *   after the stream's earlier work.  ffts_wait_flags: wait until flags[0..n) >=
- *   epoch (acquire);
- *   bounded at about 2 s, after which *status = 5 and the wait returns.
+ *   from src to dsts[i] on streams[i] (cudaStream_t), i < n; with a non-NULL
+ *   `after` (cudaEvent_t) every stream first waits for that event.
+ * ffts_signal: store value into *flags[i] (release, system scope) on streams[i],
+ *   after that stream's earlier work, i < n <= 1024.  ffts_wait_flags: wait
+ *   until flags[0..n) >= epoch (acquire), n <= 32; bounded at about 2 s, after
+ *   which *status = 5 and the wait returns.
  */
 FFTS_API int32_t ffts_ipc_handle(const void *ptr, void *handle, int64_t *offset);
 FFTS_API int32_t ffts_ipc_open(const void *handle, int64_t offset, void **ptr);
 FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset);
-FFTS_API int32_t ffts_copy_rows(void *const *dsts, int32_t n, const void *src, int64_t pitch,
-                               int64_t width, int64_t height, void *stream);
-FFTS_API int32_t ffts_signal(int32_t *const *flags, int32_t n, int32_t value, void *stream);
+FFTS_API int32_t ffts_copy_rows(void *const *dsts, void *const *streams, int32_t n, const void *src,
+                               int64_t pitch, int64_t width, int64_t height, void *after);
+FFTS_API int32_t ffts_signal(int32_t *const *flags, void *const *streams, int32_t n, int32_t value);
 FFTS_API int32_t ffts_wait_flags(const int32_t *flags, int32_t n, int32_t epoch, int32_t *status,
                                  void *stream);
 

@@ -167,3 +167,40 @@ def test_row_range_equals_full_call(lib):
     assert int(status.item()) == 0
     with pytest.raises(ValueError):
         lib.sparse_attention(q, k, v, bits, bs, rows=(100, 1024))  # not on a 128-row boundary
+
+
+def test_push_to_peer_buffers_equals_own_output(lib):
+    # ffts_sparse_attn_fwd_push: the epilogue also stores every output row into
+    # each peer buffer (here two more buffers on this GPU, which the kernel
+    # addresses the same way); ragged L, a row range, both output layouts
+    g = torch.Generator().manual_seed(29)
+    B, H, L, bs = 2, 4, 3000, 64
+    q = torch.randn(B, H, L, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(B, 2, L, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(B, 2, L, 128, generator=g).bfloat16().cuda()
+    N = (L + bs - 1) // bs
+    bits = O.pack_bool(random_mask(B, H, N, 0.3, g)).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    full = lib.sparse_attention(q, k, v, bits, bs, status=status)
+    # [B, L, H, D] output
+    peers = [torch.full((B, L, H, 128), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    own = lib.sparse_attention(q, k, v, bits, bs, status=status, peers=[p.data_ptr() for p in peers])
+    assert torch.equal(own, full)
+    for p in peers:
+        assert torch.equal(p, full)
+    # head-major [B, H, L, D] buffers (rows contiguous), rows [1024, L) of heads 1..2
+    lo = 1024
+    bufs = [torch.zeros(B, H, L, 128, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    pitch_h = L * 128 * 2
+    out = bufs[0][:, 1:3, lo:].permute(0, 2, 1, 3)
+    part = lib.sparse_attention(q[:, 1:3], k[:, :1], v[:, :1], bits[:, 1:3].contiguous(), bs, status=status,
+                                out=out, rows=(lo, L),
+                                peers=[b.data_ptr() + 1 * pitch_h + lo * 256 for b in bufs[1:]])
+    torch.cuda.synchronize()
+    ref = lib.sparse_attention(q[:, 1:3], k[:, :1], v[:, :1], bits[:, 1:3].contiguous(), bs, status=status)
+    for b in bufs:
+        assert torch.equal(b[:, 1:3, lo:], ref[:, lo:].permute(0, 2, 1, 3))
+        assert not b[:, :, :lo].any() and not b[:, 0].any() and not b[:, 3].any()
+    assert int(status.item()) == 0
+    with pytest.raises(ValueError):
+        lib.sparse_attention(q, k, v, bits, bs, peers=[0])  # a NULL peer buffer

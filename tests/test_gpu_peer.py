@@ -1,8 +1,8 @@
 """The copy-engine all-gather of the sharded prefill (dist.PeerGather).
 
-On two GPUs its output equals the NCCL all-gather path bit for bit, on
-consecutive calls (both of its alternating buffers, and a reuse); skipped on a
-box with one GPU.  On one GPU: the row copy, flag store and bounded wait entry
+On two GPUs its output equals the NCCL all-gather path bit for bit, with the
+pushes in the attention epilogue and on the copy engines, on consecutive calls
+(both of its alternating buffers, and a reuse); skipped on a box with one GPU.  On one GPU: the row copy, flag store and bounded wait entry
 points, including a wait that runs out on a flag nothing sets."""
 import os
 import socket
@@ -39,16 +39,18 @@ def _worker(rank, world, port, q_out):
         q, k, v = make_inputs(L, num_q_heads=8, num_kv_heads=2, dtype=torch.bfloat16, device=str(dev),
                               expand=False)
         kw = bench.mask_kwargs(0.1)
-        pg = PeerGather(8, L, 128, device=dev)
         ref = sharded_prefill(q, k, v, 0, **kw).clone()
         ok = True
-        for _ in range(3):
-            got = sharded_prefill(q, k, v, 0, gather=pg, **kw)
-            torch.cuda.synchronize(dev)
-            ok &= bool(torch.equal(got, ref))
-        ok &= int(pg.status.item()) == 0
-        dist.barrier()
-        pg.close()
+        for push in ("epilogue", "copy"):
+            pg = PeerGather(8, L, 128, device=dev, push=push)
+            for _ in range(3):
+                got = sharded_prefill(q, k, v, 0, gather=pg, **kw)
+                torch.cuda.synchronize(dev)
+                ok &= bool(torch.equal(got, ref))
+            ok &= int(pg.status.item()) == 0
+            dist.barrier()
+            pg.close()
+            dist.barrier()
         q_out.put((rank, ok))
     finally:
         dist.destroy_process_group()
@@ -76,8 +78,8 @@ def _ptrs(*addrs):
 
 def test_copy_rows_signal_wait_one_gpu():
     """The copy, flag-store and wait entry points on one GPU: a strided row copy
-    to two destinations, an epoch stored into two flags, and a wait that sees it
-    (status stays 0)."""
+    to two destinations on two streams, an epoch stored into two flags, and a
+    wait that sees it (status stays 0)."""
     from fftsparse_b200 import _lib
     lib = _lib.load()
     dev = torch.device("cuda", 0)
@@ -87,11 +89,16 @@ def test_copy_rows_signal_wait_one_gpu():
     dst = [torch.zeros(H, L, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     pitch, row = L * D * 2, D * 2
     lo, hi = 128, 512
-    _lib.check(lib.ffts_copy_rows(_ptrs(*[d.data_ptr() + lo * row for d in dst]), 2, src.data_ptr() + lo * row,
-                                  pitch, (hi - lo) * row, H, stream))
+    side = torch.cuda.Stream(device=dev)
+    ready = torch.cuda.Event()
+    ready.record(torch.cuda.current_stream(dev))
+    # copy 0 on the current stream, copy 1 on a second stream that waits for `ready`
+    _lib.check(lib.ffts_copy_rows(_ptrs(*[d.data_ptr() + lo * row for d in dst]), _ptrs(stream, side.cuda_stream),
+                                  2, src.data_ptr() + lo * row, pitch, (hi - lo) * row, H, ready.cuda_event))
     flags = torch.zeros(2, dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    _lib.check(lib.ffts_signal(_ptrs(flags.data_ptr(), flags.data_ptr() + 4), 2, 7, stream))
+    _lib.check(lib.ffts_signal(_ptrs(flags.data_ptr(), flags.data_ptr() + 4), _ptrs(stream, side.cuda_stream), 2, 7))
+    torch.cuda.current_stream(dev).wait_stream(side)
     _lib.check(lib.ffts_wait_flags(flags.data_ptr(), 2, 7, status.data_ptr(), stream))
     torch.cuda.synchronize(dev)
     for d in dst:
