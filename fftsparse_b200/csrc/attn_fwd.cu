@@ -358,12 +358,20 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // ---- tile coordinates: (b, kv head, query tile descending, head in group)
+  // ---- tile coordinates: (b, kv head, query tile, head in group).  Query tiles
+  // run heaviest (last) first, so the light ones fill the end of the grid.  When
+  // the epilogue also pushes every tile to peers, the push volume per tile is
+  // fixed while the causal work grows with the tile index: heavy and light tiles
+  // then alternate (last, first, second last, second, ...), which spreads the
+  // NVLink traffic over the whole kernel instead of bunching it where the light
+  // tiles run.
   const int G = prm.H / prm.Hkv;
   int x = blockIdx.x;
   const int hg = x % G;
   x /= G;
-  const int qt = prm.qt_lo + prm.qt_cnt - 1 - (x % prm.qt_cnt);
+  const int qi = x % prm.qt_cnt;
+  const int qt = (prm.n_peers > 0 && (qi & 1)) ? prm.qt_lo + (qi >> 1)
+                                               : prm.qt_lo + prm.qt_cnt - 1 - (prm.n_peers > 0 ? qi >> 1 : qi);
   x /= prm.qt_cnt;
   const int kvh = x % prm.Hkv;
   const int b = x / prm.Hkv;
@@ -734,9 +742,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (all_ok) {
       // each warp instruction stores two whole 256-byte rows
       const int64_t off = int64_t(b) * prm.os_b + int64_t(qt * kBM - prm.out_row0) * prm.os_l + int64_t(h) * prm.os_h;
+      // the peers in an order rotated per CTA, so that the CTAs' stores spread
+      // over all peers rather than reaching them one at a time
+      const int rot = prm.n_peers > 0 ? int(blockIdx.x % unsigned(prm.n_peers)) : 0;
 #pragma unroll 1
       for (int d = -1; d < prm.n_peers; ++d) {
-        __nv_bfloat16 *base = (d < 0 ? prm.out : prm.peer_out[d]) + off;
+        int pd = d + rot;
+        if (pd >= prm.n_peers) pd -= prm.n_peers;
+        __nv_bfloat16 *base = (d < 0 ? prm.out : prm.peer_out[pd]) + off;
 #pragma unroll 4
         for (int k = r; k < tile_rows * 16; k += kBM) {
           const int row = k >> 4, j = k & 15;
