@@ -447,6 +447,8 @@ def run_ours(args):
     ql, kl, vl = local_views(q, k, v, shard)
     mask = F.fft_block_mask(ql, kl, **kw)
     torch.cuda.synchronize(dev)
+    barrier()  # no rank still pushes rows of the previous loop into this one's memory
+    torch.cuda.synchronize(dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     reps = max(3, args.steps)
     ev[0].record(stream)
