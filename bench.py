@@ -240,20 +240,30 @@ class Llama8BShape:
     """Random-init decoder with Llama-3.1-8B shapes: hidden
     4096, 32 q / 8 kv heads of 128, SwiGLU 14336, RMSNorm, RoPE base 500000,
     vocab 128256, bf16.  Weights ~ N(0, 0.02) drawn with one seed (identical on
-    every rank), norm weights 1.  The dense parts are torch/cuBLAS; every
-    layer's attention is fftsparse_b200's operator on un-expanded GQA k/v.
-    With world > 1 each rank keeps only its KV groups' columns of the QKV
-    projection, runs attention for its heads, and one all-gather per layer
-    (in the attention epilogue when a PeerGather is given) assembles the head-major
-    output that o_proj consumes (o_proj and the MLP are replicated)."""
+    every rank), norm weights 1.  The dense parts are torch/cuBLAS.  Per layer:
+    RMSNorm and the QKV projection; fftsparse_b200's rope_pool (the caller's
+    RoPE, head-major layout and the pooling of q and k in one pass); its
+    attention on un-expanded GQA k/v, given the pooled blocks.
+
+    With world > 1 the layer is split two ways:
+    - attention by KV group: each rank keeps only its KV groups' columns of the
+      QKV projection and runs attention for its heads; the head-major output is
+      all-gathered (in the attention epilogue when a PeerGather is given);
+    - o_proj and the MLP by sequence: each rank takes its contiguous slice of
+      token rows of the gathered output, applies o_proj, the residual, RMSNorm
+      and the MLP to those rows, and one all-gather of the hidden states gives
+      every rank all rows for the next layer's QKV projection.
+    ``dims`` overrides (H, HKV, D, HIDDEN, INTER, VOCAB) for small test models."""
 
     H, HKV, D, HIDDEN, INTER, VOCAB = 32, 8, 128, 4096, 14336, 128256
 
-    def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None):
+    def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None, dims=None):
         from fftsparse_b200.dist import kv_group_shard
+        if dims is not None:
+            self.H, self.HKV, self.D, self.HIDDEN, self.INTER, self.VOCAB = dims
         g = torch.Generator(device=device).manual_seed(seed)
         self.shard = kv_group_shard(self.H, self.HKV, world, rank)
-        self.world = world
+        self.world, self.rank = world, rank
         self.gather = gather  # dist.PeerGather of the (H, L) output, or None for NCCL
         D = self.D
 
@@ -284,10 +294,16 @@ class Llama8BShape:
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.bfloat16)
 
     def forward(self, ids, kw):
+        import torch.distributed as dist
+
         import fftsparse_b200 as F
         from fftsparse_b200.dist import sharded_prefill
-        L, D = ids.shape[0], self.D
+        L, D, H, INTER = ids.shape[0], self.D, self.H, self.INTER
         Hl, Hkvl = self.shard.heads, self.shard.kv_hi - self.shard.kv_lo
+        if L % self.world:
+            raise ValueError(f"sequence length {L} does not split over {self.world} ranks")
+        r0, r1 = self.rank * (L // self.world), (self.rank + 1) * (L // self.world)  # this rank's rows
+        bs = kw.get("block_size", 128)
         if self._rope is None or self._rope[0].shape[0] != L:
             inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
             fr = torch.arange(L, device=self.device, dtype=torch.float64)[:, None] * inv[None]
@@ -295,30 +311,34 @@ class Llama8BShape:
             self._rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16))
         cos, sin = self._rope
 
-        def rope(x):  # x [1, h, L, D]
-            x1, x2 = x[..., :D // 2], x[..., D // 2:]
-            return x * cos + torch.cat([-x2, x1], -1) * sin
-
         h = self.embed[ids]
         for lw in self.layers:
             x = self.rmsnorm(h)
             qkv = x @ lw["wqkv"]
-            q = rope(qkv[:, :Hl * D].view(L, Hl, D).transpose(0, 1)[None])
-            k = rope(qkv[:, Hl * D:(Hl + Hkvl) * D].view(L, Hkvl, D).transpose(0, 1)[None])
-            v = qkv[:, (Hl + Hkvl) * D:].view(L, Hkvl, D).transpose(0, 1)[None].contiguous()
+            del x
+            q, k, v, qb, kb = F.rope_pool(qkv[:, :Hl * D], qkv[:, Hl * D:(Hl + Hkvl) * D],
+                                          qkv[:, (Hl + Hkvl) * D:], Hl, Hkvl, cos, sin, bs)
             del qkv
             if self.world == 1:
-                attn = F.myattn_prefill(q, k, v, 0, **kw).view(L, self.H * D)
+                attn = F.myattn_prefill(q, k, v, 0, pooled=(qb, kb), **kw).view(L, H * D)
             else:
-                full = sharded_prefill(q, k, v, 0, inputs_are_local=True, gather=self.gather, **kw)
-                attn = full[0].transpose(0, 1).reshape(L, self.H * D)
-            del q, k, v
-            h = h + attn @ lw["wo"]
+                full = sharded_prefill(q, k, v, 0, inputs_are_local=True, gather=self.gather, pooled=(qb, kb),
+                                       **kw)
+                attn = full[0, :, r0:r1].transpose(0, 1).reshape(r1 - r0, H * D)
+            del q, k, v, qb, kb
+            hr = h[r0:r1] + attn @ lw["wo"]
             del attn
-            x = self.rmsnorm(h)
+            x = self.rmsnorm(hr)
             gu = x @ lw["wgu"]
-            h = h + (torch.nn.functional.silu(gu[:, :self.INTER]) * gu[:, self.INTER:]) @ lw["wd"]
+            del x
+            hr = hr + (torch.nn.functional.silu(gu[:, :INTER]) * gu[:, INTER:]) @ lw["wd"]
             del gu
+            if self.world == 1:
+                h = hr
+            else:
+                h = torch.empty_like(h)
+                dist.all_gather_into_tensor(h, hr)
+            del hr
         return self.rmsnorm(h[-1:]) @ self.lm_head  # logits of the last position only
 
 
@@ -352,9 +372,10 @@ def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
             "workload": f"cfg4: Llama-3.1-8B-shape decoder, {args.ttft_layers} layers, random N(0,0.02) weights "
                         f"(seed 0), bf16; prefill of {L} uniform random token ids (seed 0) to the last-token "
                         f"logits; FFTSparse attention (keep ratio {args.keep_ratio}) in every layer, GQA k/v "
-                        f"un-expanded; dense parts torch/cuBLAS"
+                        f"un-expanded, RoPE + layout + q/k pooling fused (rope_pool); dense parts torch/cuBLAS"
                         + ("" if world == 1 else f"; QKV columns and attention sharded by KV group over {world} "
-                                                 f"ranks, o_proj/MLP replicated"),
+                                                 f"ranks, o_proj/MLP sharded by token rows, hidden states "
+                                                 f"all-gathered per layer"),
             "logits_finite": finite, "reps": reps}
 
 

@@ -6,8 +6,9 @@ Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
   fft_block_mask(q, k, ...)                 the selected block mask + statistics
   sparse_attention(q, k, v, bits, bs)       block-sparse attention on packed bits
   pool_blocks(x, bs)                        block mean pooling
+  rope_pool(q_proj, k_proj, v_proj, ...)    the caller's RoPE + head-major layout + pooling, one pass
   derive_mask_params(L, ...)                host-side parameter derivation
-  dist.sharded_prefill(...)                 KV-group sharded prefill over NCCL
+  dist.sharded_prefill(...)                 KV-group sharded prefill (peer-memory all-gather)
 """
 from .params import derive_mask_params, MaskParams  # noqa: F401
 from .prefill import (  # noqa: F401
@@ -17,6 +18,7 @@ from .prefill import (  # noqa: F401
     fft_block_mask,
     myattn_prefill,
     pool_blocks,
+    rope_pool,
     sparse_attention,
 )
 from ._lib import load as load_library, LIB_PATH  # noqa: F401

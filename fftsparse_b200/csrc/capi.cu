@@ -47,6 +47,10 @@ int ensure_func_smem(const void *func, int bytes, int carveout) {
 
 int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t sb,
                 int64_t sh, int64_t sl, int bs, void *out, cudaStream_t stream);
+int launch_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t k_ld, const void *v_src,
+                     int64_t v_ld, int64_t L, int64_t Hq, int64_t Hkv, int64_t D, const void *cos, const void *sin,
+                     int64_t cs_ld, int bs, void *q_out, void *k_out, void *v_out, void *q_pooled, void *k_pooled,
+                     cudaStream_t stream);
 int64_t mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
                const ffts_mask_params *params, uint32_t *bits, int32_t *row_count, float *corr,
@@ -102,6 +106,17 @@ int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L,
   if (rc) return rc;
   return launch_pool(x, dtype, B, H, L, D, stride_b, stride_h, stride_l, block_size, out,
                      static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t k_ld, const void *v_src,
+                       int64_t v_ld, int64_t L, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
+                       const void *sin, int64_t cs_ld, int32_t block_size, void *q_out, void *k_out, void *v_out,
+                       void *q_pooled, void *k_pooled, void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_rope_pool(q_src, q_ld, k_src, k_ld, v_src, v_ld, L, Hq, Hkv, D, cos, sin, cs_ld, block_size,
+                          q_out, k_out, v_out, q_pooled, k_pooled, static_cast<cudaStream_t>(stream));
 }
 
 int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D) {

@@ -85,6 +85,50 @@ def pool_blocks(x: torch.Tensor, block_size: int) -> torch.Tensor:
     return out
 
 
+def rope_pool(q_proj: torch.Tensor, k_proj: torch.Tensor, v_proj: Optional[torch.Tensor], num_heads: int,
+              num_kv_heads: int, cos: torch.Tensor, sin: torch.Tensor, block_size: int = 128):
+    """The caller's rotary embedding, head-major layout and the block pooling of
+    q and k in one pass (ffts_rope_pool).
+
+    q_proj [L, >= num_heads * 128], k_proj / v_proj [L, >= num_kv_heads * 128]:
+    token-major bf16 projections (rows may be strided, e.g. column slices of one
+    fused QKV product); v_proj may be None.  cos / sin: bf16 [L, 128] (HF's
+    position embeddings for one sequence).  Returns (q, k, v, q_pooled,
+    k_pooled): q [1, num_heads, L, 128] and k, v [1, num_kv_heads, L, 128]
+    contiguous, q rotated as HF apply_rotary_pos_emb rotates it in bf16, and
+    the pooled blocks that ``fft_block_mask(q, k, pooled=(q_pooled, k_pooled))``
+    takes instead of pooling q and k again.
+    """
+    for name, t in (("q_proj", q_proj), ("k_proj", k_proj), ("v_proj", v_proj), ("cos", cos), ("sin", sin)):
+        if t is None and name == "v_proj":
+            continue
+        if t.dim() != 2 or t.stride(1) != 1 or t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be a 2-D bf16 tensor with unit column stride")
+    L, D = cos.shape
+    if sin.shape != cos.shape or sin.stride() != cos.stride():
+        raise ValueError("cos and sin must have the same shape and strides")
+    if q_proj.shape[0] != L or k_proj.shape[0] != L or (v_proj is not None and v_proj.shape[0] != L):
+        raise ValueError("projections and cos/sin must have the same number of rows")
+    if q_proj.shape[1] < num_heads * D or k_proj.shape[1] < num_kv_heads * D or \
+            (v_proj is not None and v_proj.shape[1] < num_kv_heads * D):
+        raise ValueError("a projection has fewer columns than its heads need")
+    dev = q_proj.device
+    N = (L + block_size - 1) // block_size
+    q = torch.empty(1, num_heads, L, D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(1, num_kv_heads, L, D, dtype=torch.bfloat16, device=dev)
+    v = None if v_proj is None else torch.empty(1, num_kv_heads, L, D, dtype=torch.bfloat16, device=dev)
+    qb = torch.empty(1, num_heads, N, D, dtype=torch.bfloat16, device=dev)
+    kb = torch.empty(1, num_kv_heads, N, D, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.ffts_rope_pool(
+        q_proj.data_ptr(), q_proj.stride(0), k_proj.data_ptr(), k_proj.stride(0),
+        None if v_proj is None else v_proj.data_ptr(), 0 if v_proj is None else v_proj.stride(0),
+        L, num_heads, num_kv_heads, D, cos.data_ptr(), sin.data_ptr(), cos.stride(0), block_size,
+        q.data_ptr(), k.data_ptr(), None if v is None else v.data_ptr(), qb.data_ptr(), kb.data_ptr(),
+        _stream_ptr(dev)))
+    return q, k, v, qb, kb
+
+
 @dataclass
 class BlockMask:
     """Result of the block-mask selection for a [B, H, L, D] prefill."""
@@ -128,12 +172,14 @@ class BlockMask:
 
 
 def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, block_size: int = 128,
-                   params: Optional[MaskParams] = None, **kwargs) -> BlockMask:
+                   params: Optional[MaskParams] = None, pooled=None, **kwargs) -> BlockMask:
     """Select the FFTSparse block mask for q [B, H, L, D] and k [B, Hkv, L, D].
 
     ``kwargs`` are the mask arguments of myattn_prefill (sink_ratio,
     recent_ratio, local_span_ratio, enable_correlation_mask,
-    correlation_selection_mode, ...).
+    correlation_selection_mode, ...).  ``pooled = (q_pooled, k_pooled)``, the
+    [B, H, N, D] / [B, Hkv, N, D] block means already computed (rope_pool),
+    skips the pooling pass.
     """
     q, k = query_states, key_states
     _check_4d("query_states", q)
@@ -150,9 +196,16 @@ def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, bloc
     if params is None:
         params, cp = _cached_params(L, block_size, kwargs)
     lib = _lib.load()
-    qb = pool_blocks(q, params.block_size)
-    kb = pool_blocks(k, params.block_size)
     N = params.n_blocks
+    if pooled is None:
+        qb = pool_blocks(q, params.block_size)
+        kb = pool_blocks(k, params.block_size)
+    else:
+        qb, kb = pooled
+        if qb.shape != (B, H, N, D) or kb.shape != (B, Hkv, N, D) or qb.dtype != q.dtype or \
+                kb.dtype != q.dtype or not (qb.is_contiguous() and kb.is_contiguous()):
+            raise ValueError(f"pooled blocks must be contiguous [B, H, N, D] / [B, Hkv, N, D] with N = {N} "
+                             f"in the input dtype")
     W = (N + 31) // 32
     dev = q.device
     bits = torch.empty(B, H, N, W, dtype=torch.int32, device=dev)
@@ -272,6 +325,7 @@ def myattn_prefill(
         qk_topk_ratio: float = 0.2,
         attention_vis_heads=(0,),
         attention_vis_dir=None,
+        pooled=None,
 ):
     """Block-sparse prefill attention with FFT-correlation block selection.
 
@@ -284,6 +338,10 @@ def myattn_prefill(
     ``collect_corr_stats`` and the visualisation arguments are accepted and
     ignored, a non-CUDA input raises AssertionError (:502) and an unknown
     selection mode raises ValueError (:210).
+
+    ``pooled`` (not in the reference's signature; default None) takes the
+    (q_pooled, k_pooled) block means a caller already computed with rope_pool,
+    so the selection skips its pooling pass.
     """
     assert query_states.is_cuda, "input tensors must be on CUDA"
     q, k, v = query_states, key_states, value_states
@@ -309,7 +367,7 @@ def myattn_prefill(
         column_end_exclude_ratio=column_end_exclude_ratio,
         enable_last_block_mask=enable_last_block_mask, diag_sample_ratio=diag_sample_ratio,
         min_diag_samples=min_diag_samples, max_diag_samples=max_diag_samples,
-        stripe_threshold=stripe_threshold, qk_topk_ratio=qk_topk_ratio)
+        stripe_threshold=stripe_threshold, qk_topk_ratio=qk_topk_ratio, pooled=pooled)
 
     collector = getattr(sys.modules[__name__], "_sparsity_collector", None)
     if collector is not None:

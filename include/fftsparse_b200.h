@@ -107,6 +107,28 @@ FFTS_API int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, i
                   int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_l,
                   int32_t block_size, void *out, void *stream);
 
+/*
+ * The caller's rotary embedding, head-major layout and block pooling in one
+ * pass, for one sequence.  Replaces, ahead of myattn_prefill, HF
+ * apply_rotary_pos_emb on q and k as the caller applies it
+ * (eval/LongBench/pred.py:191-194), the views of q/k/v as [1, H, L, D], and
+ * the pooling of q and k (ffts_pool; my_attn_v7.py:105-114 at :554-555), so
+ * that ffts_block_mask can take the pooled blocks directly.
+ *   q_src [L, q_ld], k_src [L, k_ld], v_src [L, v_ld]: token-major bf16
+ *     projections (head h in columns [h*D, h*D + D)); v_src may be NULL.
+ *   cos, sin: bf16 [L, D] with row stride cs_ld.
+ *   q_out [Hq, L, D], k_out / v_out [Hkv, L, D]: head-major, contiguous.
+ *   q_pooled [Hq, N, D], k_pooled [Hkv, N, D], N = ceil(L / block_size).
+ * out = bf16(bf16(x * cos) + bf16(rotate_half(x) * sin)), each operation in
+ * fp32 (the torch bf16 expression op by op); pooled blocks are exactly those
+ * ffts_pool computes from q_out / k_out.  D must be 128; bf16 only.
+ */
+FFTS_API int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t k_ld,
+                  const void *v_src, int64_t v_ld, int64_t L, int64_t Hq, int64_t Hkv, int64_t D,
+                  const void *cos, const void *sin, int64_t cs_ld, int32_t block_size,
+                  void *q_out, void *k_out, void *v_out, void *q_pooled, void *k_pooled,
+                  void *stream);
+
 /* Bytes of device workspace ffts_block_mask / ffts_prefill need. */
 FFTS_API int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 

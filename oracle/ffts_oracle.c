@@ -105,6 +105,35 @@ int ffo_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t 
   return 0;
 }
 
+/* ------------------------------------------------------------------- RoPE */
+
+/* The rotary embedding the caller of myattn_prefill applies to q and k before
+ * the call (eval/LongBench/pred.py:191-194, HF apply_rotary_pos_emb):
+ * out = x * cos + rotate_half(x) * sin with rotate_half(x) = cat(-x[D/2:], x[:D/2]),
+ * evaluated as torch evaluates that bf16 expression op by op: each product in
+ * fp32 rounded to bf16, then the sum in fp32 rounded to bf16 (the negation is
+ * exact).  x is token-major (head h of token t at x + t * ld + h * D), cos and
+ * sin are bf16 [L, D] with row stride cs_ld, out is head-major [H, L, D]. */
+int ffo_rope(const uint16_t *x, int64_t ld, int64_t L, int64_t H, int64_t D, const uint16_t *cos_t,
+             const uint16_t *sin_t, int64_t cs_ld, uint16_t *out) {
+  if (D % 2) return -1;
+  const int64_t half = D / 2;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t h = 0; h < H; ++h) {
+    for (int64_t t = 0; t < L; ++t) {
+      const uint16_t *row = x + t * ld + h * D;
+      for (int64_t d = 0; d < D; ++d) {
+        const float xv = bf16_to_f32(row[d]);
+        const float rv = d < half ? -bf16_to_f32(row[d + half]) : bf16_to_f32(row[d - half]);
+        const float a = bf16_to_f32(f32_to_bf16_rne(xv * bf16_to_f32(cos_t[t * cs_ld + d])));
+        const float b = bf16_to_f32(f32_to_bf16_rne(rv * bf16_to_f32(sin_t[t * cs_ld + d])));
+        out[(h * L + t) * D + d] = f32_to_bf16_rne(a + b);
+      }
+    }
+  }
+  return 0;
+}
+
 /* -------------------------------------------------------------------- FFT */
 
 static int ilog2(int64_t m) {

@@ -10,6 +10,8 @@ cpu_baseline leg.  The product path (fftsparse_b200) never imports this.
   causal, scale 1/sqrt(D), head h uses mask plane h (head_mask_type all 1,
   :772), rows with nothing selected give zeros.
 * ``prefill_mask`` chains pooling and selection for [B, H, L, D] inputs.
+* ``rope`` / ``rope_pool`` restate the caller's rotary embedding (C ffo_rope)
+  and the fused RoPE + layout + pooling pass (ffts_rope_pool).
 """
 from __future__ import annotations
 
@@ -38,6 +40,9 @@ def lib():
         L.ffo_pool.restype = ctypes.c_int
         L.ffo_pool.argtypes = [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_int64] * 7 + [
             ctypes.c_int, ctypes.c_void_p]
+        L.ffo_rope.restype = ctypes.c_int
+        L.ffo_rope.argtypes = [ctypes.c_void_p] + [ctypes.c_int64] * 4 + [ctypes.c_void_p] * 2 + [
+            ctypes.c_int64, ctypes.c_void_p]
         L.ffo_block_mask.restype = ctypes.c_int
         L.ffo_block_mask.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
@@ -65,6 +70,31 @@ def pool(x: torch.Tensor, block_size: int) -> torch.Tensor:
     if rc != 0:
         raise ValueError(f"ffo_pool rejected shape (rc={rc})")
     return out
+
+
+def rope(x: torch.Tensor, num_heads: int, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """The caller's rotary embedding (C restatement ffo_rope) of token-major bf16
+    projections x [L, >= num_heads * D] (row stride x.stride(0)) with bf16 cos/sin
+    [L, D] -> head-major [1, num_heads, L, D] bf16."""
+    assert x.device.type == "cpu" and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+    assert cos.dtype == sin.dtype == torch.bfloat16 and cos.stride() == sin.stride() and cos.stride(1) == 1
+    L, D = cos.shape
+    out = torch.empty(1, num_heads, L, D, dtype=torch.bfloat16)
+    rc = lib().ffo_rope(x.data_ptr(), x.stride(0), L, num_heads, D, cos.data_ptr(), sin.data_ptr(),
+                        cos.stride(0), out.data_ptr())
+    if rc != 0:
+        raise ValueError(f"ffo_rope rejected shape (rc={rc})")
+    return out
+
+
+def rope_pool(q_src, k_src, v_src, num_heads, num_kv_heads, cos, sin, block_size):
+    """Checker of ffts_rope_pool: RoPE'd head-major q and k, head-major v, and the
+    canonical block means of the RoPE'd q and k."""
+    q = rope(q_src, num_heads, cos, sin)
+    k = rope(k_src, num_kv_heads, cos, sin)
+    L, D = cos.shape
+    v = None if v_src is None else v_src[:, :num_kv_heads * D].reshape(L, num_kv_heads, D).transpose(0, 1)[None]
+    return q, k, None if v is None else v.contiguous(), pool(q, block_size), pool(k, block_size)
 
 
 def block_mask(qb: torch.Tensor, kb: torch.Tensor, params, dtype: torch.dtype):
