@@ -27,7 +27,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from .params import derive_mask_params, MaskParams
+from .params import SEL_TOPK, derive_mask_params, MaskParams
 
 __all__ = ["myattn_prefill", "fft_block_mask", "sparse_attention", "pool_blocks", "BlockMask",
            "AttentionCache", "_attention_cache"]
@@ -246,6 +246,37 @@ def _cached_params(L: int, block_size: int, kwargs: dict):
     return hit
 
 
+def corr_mask_fraction(corr: torch.Tensor, params: MaskParams) -> float:
+    """Kept fraction of the reference's correlation block mask, the value its
+    calibration hook records under "corr" (my_attn_v7.py:713-717).
+
+    The mask (create_correlation_block_mask, :160-227) keeps block (i, j) of a
+    head when the lag i - j is a selected remote lag and j >= keep_sink.  The
+    lags are selected from the fp32 lag scores ``corr`` [B, H, N] exactly as the
+    reference selects them (:193-206): corr >= torch.quantile(remote scores,
+    1 - topk_ratio) in top-k mode, corr / max(remote scores, 1e-6) >= threshold
+    in threshold mode.  Lag t then contributes max(0, N - t - keep_sink) blocks;
+    the fraction is over all B * H * N * N blocks.  Calibration only: it reads
+    the scores back to the host.
+    """
+    N, rs, ks = params.n_blocks, params.remote_start, params.keep_sink
+    B, H = corr.shape[0], corr.shape[1]
+    if rs >= N:
+        return 0.0
+    remote = corr[..., rs:].float()
+    if params.corr_mode == SEL_TOPK:
+        # corr_quantile is 1 - topk_ratio rounded to fp32, as torch.quantile rounds it
+        thr = torch.quantile(remote, params.corr_quantile, dim=-1, keepdim=True)
+        sel = remote >= thr
+    else:
+        mx = remote.max(dim=-1, keepdim=True).values.clamp(min=1e-6)
+        sel = (remote / mx) >= params.corr_threshold
+    taus = torch.arange(rs, N, device=corr.device)
+    per_lag = (N - taus - ks).clamp(min=0)
+    kept = int((sel.to(torch.int64) * per_lag).sum().item())
+    return kept / (B * H * N * N)
+
+
 def _dense_causal_bits(B: int, H: int, N: int, device) -> torch.Tensor:
     W = (N + 31) // 32
     return torch.full((B, H, N, W), -1, dtype=torch.int32, device=device)
@@ -372,6 +403,8 @@ def myattn_prefill(
     collector = getattr(sys.modules[__name__], "_sparsity_collector", None)
     if collector is not None:
         N = mask.n_blocks
+        if mask.params.corr_on:
+            collector.setdefault("corr", []).append(corr_mask_fraction(mask.corr, mask.params))
         collector.setdefault("final", []).append(float(mask.row_count.sum()) / (B * H * N * N))
 
     out = sparse_attention(q, k, v, mask.bits, block_size, causal=is_causal)
