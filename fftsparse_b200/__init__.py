@@ -8,6 +8,7 @@ Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
   pool_blocks(x, bs)                        block mean pooling
   rope_pool(q_proj, k_proj, v_proj, ...)    the caller's RoPE + head-major layout + pooling, one pass
   derive_mask_params(L, ...)                host-side parameter derivation
+  calibrate.calibrate_from_qk(layers, t)    target-sparsity calibration on the device
   dist.sharded_prefill(...)                 KV-group sharded prefill (peer-memory all-gather)
 """
 from .params import derive_mask_params, MaskParams  # noqa: F401
