@@ -515,6 +515,35 @@ def run_ours(args):
               "block_density": round(mask.density(), 5),
               "stripe_heads": int(mask.is_stripe.sum().item())}
 
+    # ---- keep-ratio sweep: BASELINE config 3 sweeps {0.02, 0.05, 0.1}; the timed loop
+    # above is the headline ratio.  The same step at each other ratio, 3 timed steps
+    # after one untimed, max over ranks.  A failure is reported in the field instead
+    # of ending the run (every rank runs the same code, so all ranks take the same path).
+    sweep = {str(args.keep_ratio): round(ms_max, 4)}
+    for r in sorted({0.02, 0.05, 0.1} - {args.keep_ratio}):
+        kwr = mask_kwargs(r)
+
+        def step_r():
+            if world == 1:
+                return F.myattn_prefill(q, k, v, 0, **kwr)
+            return sharded_prefill(q, k, v, 0, num_kv_heads=HKV, gather=pg, **kwr)
+        try:
+            step_r()
+            torch.cuda.synchronize(dev)
+            barrier()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(3):
+                step_r()
+            s1.record(stream)
+            torch.cuda.synchronize(dev)
+            tr = torch.tensor([s0.elapsed_time(s1) / 3], device=dev)
+            if world > 1:
+                dist.all_reduce(tr, op=dist.ReduceOp.MAX)
+            sweep[str(r)] = round(float(tr.item()), 4)
+        except Exception as exc:  # noqa: BLE001
+            sweep[str(r)] = f"error: {exc}"[:200]
+
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
@@ -599,6 +628,7 @@ def run_ours(args):
             "stages": stages,
             "gqa_native_ms_per_layer": round(gqa_native_ms, 4),
             "host_issue_ms_per_step": round(host_ms, 4),
+            "keep_ratio_sweep_ms_per_layer": dict(sorted(sweep.items())),
             "ttft": ttft,
         }
         emit(line)
