@@ -1,4 +1,4 @@
-"""(Sequence, KV-group) sharded FFTSparse prefill over NCCL (one process per GPU).
+"""(Sequence, KV-group) sharded FFTSparse prefill, one process per GPU.
 
 The reference has no distributed path: multi-GPU use there is accelerate's
 ``device_map="auto"`` layer placement (eval/LongBench/pred.py:520).  Every step
@@ -6,7 +6,9 @@ of the operator is independent per head, and heads that share a key/value head
 (a GQA group) also share its K/V tiles, so the unit of work is the
 (sequence, KV group).  Each rank runs pooling, mask selection and attention
 for its contiguous slice of KV groups with no communication, and one
-all-gather assembles the head-major output [B, H, L, D] that o_proj consumes.
+all-gather assembles the head-major output [B, H, L, D] that o_proj consumes:
+through peer memory, fused into the attention kernel's epilogue (PeerGather),
+or as an NCCL all-gather (gather_heads).
 When the KV groups are fewer than the ranks (2 sequences x
 4 KV groups on 8 GPUs), the units are (sequence, KV group) pairs, ordered
 sequence-major, and a rank owns a contiguous run of them.
@@ -16,6 +18,7 @@ the rank's heads as views; nothing is copied before the kernels run.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Optional
 
@@ -161,14 +164,16 @@ class PeerGather:
 
     def __init__(self, num_heads: int, seq_len: int, head_dim: int = 128, group=None, device=None,
                  push: str = "epilogue", chunks: int = 4):
-        import ctypes
-
         from . import _lib
 
         if push not in ("epilogue", "copy"):
             raise ValueError(f"push must be 'epilogue' or 'copy', got {push!r}")
         self.push = push
         self.world = dist.get_world_size(group)
+        # the epilogue stores to at most 15 peers; the wait kernel watches at most 32 flags
+        limit = 16 if push == "epilogue" else 32
+        if self.world > limit:
+            raise ValueError(f"PeerGather(push={push!r}) supports at most {limit} ranks, got {self.world}")
         self.rank = dist.get_rank(group)
         self.H, self.L, self.D = num_heads, seq_len, head_dim
         self.device = device or torch.device("cuda", torch.cuda.current_device())
@@ -220,7 +225,6 @@ class PeerGather:
         # is stored by one kernel on the calling stream after the attention
         self._all_flags = (ctypes.c_void_p * (len(peers) + 1))(*list(self._flags)[:len(peers)],
                                                                 self.flags.data_ptr() + 4 * self.rank)
-        self._ctypes = ctypes
         self.epoch = 0
         dist.barrier(group)  # every rank has mapped every buffer before the first push
 
@@ -228,7 +232,7 @@ class PeerGather:
         from . import _lib
         from .prefill import sparse_attention
 
-        lib, dev, ct = self.lib, self.device, self._ctypes
+        lib, dev, ct = self.lib, self.device, ctypes
         cur = torch.cuda.current_stream(dev)
         self.epoch += 1
         e, slot = self.epoch, self.epoch % 2
@@ -238,8 +242,8 @@ class PeerGather:
         pitch = L * row_bytes
         local = buf.data_ptr() + shard.h_lo * pitch
         bases = self._dst[slot]
-        mine = buf[:, shard.h_lo:shard.h_hi].permute(0, 2, 1, 3)
         if self.push == "epilogue":
+            mine = buf[:, shard.h_lo:shard.h_hi].permute(0, 2, 1, 3)
             sparse_attention(ql, kl, vl, bits, block_size, causal=causal, out=mine,
                              peers=[b + shard.h_lo * pitch for b in bases[:self._npeers]])
             n = self._npeers + 1
