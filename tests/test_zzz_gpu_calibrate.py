@@ -1,7 +1,7 @@
-"""On-device calibration on the GPU (sorted last: added without a B200 run yet, so a
-failure here cannot stop the other GPU tests under -x): the bisection run as device tensor code
+"""On-device calibration on the GPU: the bisection run as device tensor code
 (calibrate_from_qk, one read-back) picks the value the reference's host loop
-picks over the same GPU lag scores (corr_mask_fraction at each step)."""
+picks over the same GPU lag scores (corr_mask_fraction at each step).  The file
+sorts after the kernel tests, so under -x they run first."""
 import pytest
 import torch
 
