@@ -63,7 +63,11 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-ttft", action="store_true")
-    ap.add_argument("--ttft-layers", type=int, default=32)
+    ap.add_argument("--ttft-layers", type=int, default=0, help="0: the config's own layer count")
+    ap.add_argument("--ttft-config", type=int, choices=[4, 5], default=4,
+                    help="BASELINE config of the TTFT decoder (4: Llama-3.1-8B shape, 1 x seq-len tokens; "
+                         "5: Qwen2.5-7B shape, 2 x 65536 tokens, block 64)")
+    ap.add_argument("--ttft-seq-len", type=int, default=0, help="config 5 sequence length (0: 65536)")
     return ap.parse_args()
 
 
@@ -236,33 +240,40 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------- TTFT (cfg 4)
-class Llama8BShape:
-    """Random-init decoder with Llama-3.1-8B shapes: hidden
-    4096, 32 q / 8 kv heads of 128, SwiGLU 14336, RMSNorm, RoPE base 500000,
-    vocab 128256, bf16.  Weights ~ N(0, 0.02) drawn with one seed (identical on
-    every rank), norm weights 1.  The dense parts are torch/cuBLAS.  Per layer:
-    RMSNorm and the QKV projection; fftsparse_b200's rope_pool (the caller's
-    RoPE, head-major layout and the pooling of q and k in one pass); its
-    attention on un-expanded GQA k/v, given the pooled blocks.
+class DecoderShape:
+    """Random-init decoder with the shapes of BASELINE configs 4 and 5, bf16.
+
+    ``LLAMA31_8B`` (config 4): hidden 4096, 32 q / 8 kv heads of 128, SwiGLU
+    14336, RMSNorm, RoPE base 500000, vocab 128256, 32 layers.  ``QWEN25_7B``
+    (config 5): hidden 3584, 28 q / 4 kv heads of 128, SwiGLU 18944, RoPE base
+    1e6, vocab 152064, 28 layers (shape only: no QKV bias).  Weights ~ N(0, 0.02)
+    drawn with one seed (identical on every rank), norm weights 1.  The dense
+    parts are torch/cuBLAS.  Per layer: RMSNorm and the QKV projection;
+    fftsparse_b200's rope_pool per sequence (the caller's RoPE, head-major layout
+    and the pooling of q and k in one pass); its attention on un-expanded GQA k/v,
+    given the pooled blocks.
 
     With world > 1 the layer is split two ways:
-    - attention by KV group: each rank keeps only its KV groups' columns of the
-      QKV projection and runs attention for its heads; the head-major output is
-      all-gathered (in the attention epilogue when a PeerGather is given);
-    - o_proj and the MLP by sequence: each rank takes its contiguous slice of
-      token rows of the gathered output, applies o_proj, the residual, RMSNorm
-      and the MLP to those rows, and one all-gather of the hidden states gives
+    - attention by (sequence, KV group) unit (unit_shard): each rank computes
+      its units' QKV columns for its sequences and runs attention for its heads;
+      the head-major output is all-gathered (in the attention epilogue when a
+      PeerGather is given and the batch is one sequence, else NCCL);
+    - o_proj and the MLP by token rows: each rank takes its contiguous slice of
+      the B * L rows of the gathered output, applies o_proj, the residual,
+      RMSNorm and the MLP to them, and one all-gather of the hidden states gives
       every rank all rows for the next layer's QKV projection.
     ``dims`` overrides (H, HKV, D, HIDDEN, INTER, VOCAB) for small test models."""
 
-    H, HKV, D, HIDDEN, INTER, VOCAB = 32, 8, 128, 4096, 14336, 128256
+    LLAMA31_8B = dict(dims=(32, 8, 128, 4096, 14336, 128256), rope_base=500000.0, layers=32)
+    QWEN25_7B = dict(dims=(28, 4, 128, 3584, 18944, 152064), rope_base=1e6, layers=28)
 
-    def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None, dims=None):
-        from fftsparse_b200.dist import kv_group_shard
-        if dims is not None:
-            self.H, self.HKV, self.D, self.HIDDEN, self.INTER, self.VOCAB = dims
+    def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None, dims=None, batch=1,
+                 rope_base=500000.0):
+        from fftsparse_b200.dist import unit_shard
+        self.H, self.HKV, self.D, self.HIDDEN, self.INTER, self.VOCAB = dims or self.LLAMA31_8B["dims"]
+        self.B, self.rope_base = batch, rope_base
         g = torch.Generator(device=device).manual_seed(seed)
-        self.shard = kv_group_shard(self.H, self.HKV, world, rank)
+        self.shard = unit_shard(batch, self.H, self.HKV, world, rank)
         self.world, self.rank = world, rank
         self.gather = gather  # dist.PeerGather of the (H, L) output, or None for NCCL
         D = self.D
@@ -294,37 +305,57 @@ class Llama8BShape:
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.bfloat16)
 
     def forward(self, ids, kw):
+        """ids [B, L] (or [L] for one sequence) -> logits [B, VOCAB] of each sequence's
+        last position."""
         import torch.distributed as dist
 
         import fftsparse_b200 as F
         from fftsparse_b200.dist import sharded_prefill
-        L, D, H, INTER = ids.shape[0], self.D, self.H, self.INTER
-        Hl, Hkvl = self.shard.heads, self.shard.kv_hi - self.shard.kv_lo
-        if L % self.world:
-            raise ValueError(f"sequence length {L} does not split over {self.world} ranks")
-        r0, r1 = self.rank * (L // self.world), (self.rank + 1) * (L // self.world)  # this rank's rows
+        ids = ids.view(self.B, -1)
+        B, L = ids.shape
+        D, H, INTER, HID = self.D, self.H, self.INTER, self.HIDDEN
+        sh = self.shard
+        Hl, Hkvl = sh.heads, sh.kv_hi - sh.kv_lo
+        b_lo, b_hi = sh.b_lo, (B if sh.b_hi == -1 else sh.b_hi)  # this rank's sequences
+        T = B * L
+        if T % self.world:
+            raise ValueError(f"{B} x {L} token rows do not split over {self.world} ranks")
+        r0, r1 = self.rank * (T // self.world), (self.rank + 1) * (T // self.world)  # this rank's rows
         bs = kw.get("block_size", 128)
         if self._rope is None or self._rope[0].shape[0] != L:
-            inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
+            inv = 1.0 / (self.rope_base ** (torch.arange(0, D, 2, device=self.device, dtype=torch.float64) / D))
             fr = torch.arange(L, device=self.device, dtype=torch.float64)[:, None] * inv[None]
             emb = torch.cat([fr, fr], -1)
             self._rope = (emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16))
         cos, sin = self._rope
 
-        h = self.embed[ids]
+        def stack(ts):
+            return ts[0] if len(ts) == 1 else torch.cat(ts, 0)
+
+        h = self.embed[ids.reshape(-1)]  # [B * L, HID]
         for lw in self.layers:
-            x = self.rmsnorm(h)
+            x = self.rmsnorm(h[b_lo * L:b_hi * L])
             qkv = x @ lw["wqkv"]
             del x
-            q, k, v, qb, kb = F.rope_pool(qkv[:, :Hl * D], qkv[:, Hl * D:(Hl + Hkvl) * D],
-                                          qkv[:, (Hl + Hkvl) * D:], Hl, Hkvl, cos, sin, bs)
+            parts = [F.rope_pool(qkv[i * L:(i + 1) * L, :Hl * D], qkv[i * L:(i + 1) * L, Hl * D:(Hl + Hkvl) * D],
+                                 qkv[i * L:(i + 1) * L, (Hl + Hkvl) * D:], Hl, Hkvl, cos, sin, bs)
+                     for i in range(b_hi - b_lo)]
             del qkv
+            q, k, v, qb, kb = (stack([p[j] for p in parts]) for j in range(5))
+            del parts
             if self.world == 1:
-                attn = F.myattn_prefill(q, k, v, 0, pooled=(qb, kb), **kw).view(L, H * D)
+                attn = F.myattn_prefill(q, k, v, 0, pooled=(qb, kb), **kw).view(T, H * D)
             else:
-                full = sharded_prefill(q, k, v, 0, inputs_are_local=True, gather=self.gather, pooled=(qb, kb),
-                                       **kw)
-                attn = full[0, :, r0:r1].transpose(0, 1).reshape(r1 - r0, H * D)
+                full = sharded_prefill(q, k, v, 0, inputs_are_local=True, global_batch=B, num_heads=H,
+                                       num_kv_heads=self.HKV, gather=self.gather if B == 1 else None,
+                                       pooled=(qb, kb), **kw)
+                rows = []  # token rows [r0, r1) of the head-major output, token-major
+                for b in range(B):
+                    lo, hi = max(r0, b * L), min(r1, (b + 1) * L)
+                    if lo < hi:
+                        rows.append(full[b, :, lo - b * L:hi - b * L].transpose(0, 1).reshape(hi - lo, H * D))
+                attn = stack(rows)
+                del full, rows
             del q, k, v, qb, kb
             hr = h[r0:r1] + attn @ lw["wo"]
             del attn
@@ -339,18 +370,26 @@ class Llama8BShape:
                 h = torch.empty_like(h)
                 dist.all_gather_into_tensor(h, hr)
             del hr
-        return self.rmsnorm(h[-1:]) @ self.lm_head  # logits of the last position only
+        last = h.view(B, L, HID)[:, -1]
+        return self.rmsnorm(last) @ self.lm_head  # logits of each sequence's last position
 
 
 def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
-    """Prefill TTFT of the 8B-shape decoder: token ids already on the device to
-    the last position's logits, device-timed with CUDA events, max over ranks."""
+    """Prefill TTFT of BASELINE config 4 (default) or 5: token ids already on the
+    device to the last positions' logits, device-timed with CUDA events, max over
+    ranks."""
     import torch.distributed as dist
-    L = args.seq_len
-    model = Llama8BShape(args.ttft_layers, dev, world, rank, gather=gather)
+    if args.ttft_config == 5:
+        shape, B, L, bs, name = DecoderShape.QWEN25_7B, 2, args.ttft_seq_len or 65536, 64, "cfg5: Qwen2.5-7B"
+        gather = None  # two sequences: the NCCL gather
+    else:
+        shape, B, L, bs, name = DecoderShape.LLAMA31_8B, 1, args.seq_len, BLOCK, "cfg4: Llama-3.1-8B"
+    layers = args.ttft_layers or shape["layers"]
+    model = DecoderShape(layers, dev, world, rank, gather=gather, dims=shape["dims"], batch=B,
+                         rope_base=shape["rope_base"])
     g = torch.Generator(device=dev).manual_seed(0)
-    ids = torch.randint(0, model.VOCAB, (L,), generator=g, device=dev)
-    kw = mask_kwargs(args.keep_ratio)
+    ids = torch.randint(0, model.VOCAB, (B, L), generator=g, device=dev)
+    kw = dict(mask_kwargs(args.keep_ratio), block_size=bs)
     reps = 2
     with torch.no_grad():
         model.forward(ids, kw)
@@ -369,12 +408,13 @@ def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
     del model
     torch.cuda.empty_cache()
     return {"value": round(float(t.item()) / 1e3, 4), "unit": "s",
-            "workload": f"cfg4: Llama-3.1-8B-shape decoder, {args.ttft_layers} layers, random N(0,0.02) weights "
-                        f"(seed 0), bf16; prefill of {L} uniform random token ids (seed 0) to the last-token "
-                        f"logits; FFTSparse attention (keep ratio {args.keep_ratio}) in every layer, GQA k/v "
-                        f"un-expanded, RoPE + layout + q/k pooling fused (rope_pool); dense parts torch/cuBLAS"
-                        + ("" if world == 1 else f"; QKV columns and attention sharded by KV group over {world} "
-                                                 f"ranks, o_proj/MLP sharded by token rows, hidden states "
+            "workload": f"{name}-shape decoder, {layers} layers, random N(0,0.02) weights "
+                        f"(seed 0), bf16; prefill of {B} x {L} uniform random token ids (seed 0) to the last-token "
+                        f"logits; FFTSparse attention (block {bs}, keep ratio {args.keep_ratio}) in every layer, "
+                        f"GQA k/v un-expanded, RoPE + layout + q/k pooling fused (rope_pool); dense parts "
+                        f"torch/cuBLAS"
+                        + ("" if world == 1 else f"; QKV columns and attention sharded by (sequence, KV group) over "
+                                                 f"{world} ranks, o_proj/MLP sharded by token rows, hidden states "
                                                  f"all-gathered per layer"),
             "logits_finite": finite, "reps": reps}
 

@@ -1,6 +1,8 @@
-"""The TTFT decoder harness (bench.Llama8BShape) split over two gloo CPU ranks:
-attention by KV group, o_proj/MLP by token rows with one all-gather of the
-hidden states per layer.  The fused RoPE + pooling and the two attention entry
+"""The TTFT decoder harness (bench.DecoderShape) split over two gloo CPU ranks:
+attention by (sequence, KV group) unit, o_proj/MLP by token rows with one
+all-gather of the hidden states per layer.  Two shapes: one sequence whose two
+KV groups split over the ranks (config 4's split), and two sequences of one KV
+group with block 64, which split by sequence (config 5's split).  The fused RoPE + pooling and the two attention entry
 points are replaced by the CPU oracle inside each rank, which also checks that
 the pooled blocks handed to the selection are those of the rotated q and k.
 The last-position logits of the two-rank run equal the one-rank run's, bit for
@@ -9,12 +11,15 @@ import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-DIMS = (4, 2, 128, 256, 512, 1000)  # H, HKV, D, HIDDEN, INTER, VOCAB
-L, LAYERS = 2048, 2
+# (dims = H, HKV, D, HIDDEN, INTER, VOCAB; batch; sequence length; block size)
+CASES = {"kv_groups": ((4, 2, 128, 256, 512, 1000), 1, 2048, 128),
+         "sequences": ((2, 1, 128, 256, 512, 1000), 2, 1280, 64)}
+LAYERS = 2
 
 
 def _free_port() -> int:
@@ -59,38 +64,41 @@ def _patch_with_oracle():
     F.rope_pool = fake_rope_pool
 
 
-def _run(world, rank):
+def _run(world, rank, case):
     import bench
     _patch_with_oracle()
-    kw = bench.mask_kwargs(0.2)
-    model = bench.Llama8BShape(LAYERS, torch.device("cpu"), world, rank, dims=DIMS)
-    ids = torch.randint(0, DIMS[-1], (L,), generator=torch.Generator().manual_seed(0))
+    dims, B, L, bs = CASES[case]
+    kw = dict(bench.mask_kwargs(0.2), block_size=bs)
+    model = bench.DecoderShape(LAYERS, torch.device("cpu"), world, rank, dims=dims, batch=B)
+    ids = torch.randint(0, dims[-1], (B, L), generator=torch.Generator().manual_seed(0))
     with torch.no_grad():
         return model.forward(ids, kw).float()
 
 
-def _worker(rank, world, port, result_q):
+def _worker(rank, world, port, result_q, case):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        logits = _run(world, rank)
+        logits = _run(world, rank, case)
         result_q.put((rank, logits.numpy().tobytes()))
     finally:
         dist.destroy_process_group()
 
 
-def test_decoder_two_ranks_equals_one():
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_decoder_two_ranks_equals_one(case):
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q_out, case)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q_out.get(timeout=600) for _ in range(2))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    ref = _run(1, 0)
+    ref = _run(1, 0, case)
+    assert ref.shape == (CASES[case][1], CASES[case][0][-1])
     for r in (0, 1):
         logits = torch.from_numpy(np.frombuffer(got[r], dtype=np.float32).copy()).view_as(ref)
         assert torch.isfinite(logits).all()
