@@ -60,6 +60,23 @@ def test_params_derivation_efficiency_settings():
     assert p.last_topk == 128
 
 
+@pytest.mark.parametrize("L,ratio,want", [
+    # N, keep_sink, keep_recent, local_window, remote_start, FFT cut, columns, column top-k,
+    # stripe samples, last-row top-k (BASELINE configs 1 and 2 with the efficiency-script ratios)
+    (8192, 0.1, (64, 1, 1, 1, 2, 58, 6, 52, 9, 5, 64)),
+    (32768, 0.05, (256, 2, 1, 2, 3, 249, 25, 205, 25, 19, 128)),
+    (131072, 0.05, (1024, 10, 1, 10, 11, 1009, 102, 820, 50, 64, 128)),
+])
+def test_params_derivation_baseline_configs(L, ratio, want):
+    p = derive_mask_params(L, sink_ratio=0.01, recent_ratio=0.0, local_span_ratio=0.02,
+                           correlation_selection_mode="topk", correlation_topk_ratio=ratio,
+                           qk_topk_ratio=ratio, column_topk_ratio=0.2, diag_sample_ratio=0.15,
+                           min_diag_samples=5, max_diag_samples=64)
+    got = (p.n_blocks, p.keep_sink, p.keep_recent, p.local_window, p.remote_start, p.sink_tau_raw,
+           p.col_start, p.col_end, p.col_topk, len(p.diag_taus), p.last_topk)
+    assert got == want
+
+
 def test_unknown_selection_mode_raises_value_error():
     with pytest.raises(ValueError):
         derive_mask_params(8192, correlation_selection_mode="bogus")
