@@ -10,18 +10,21 @@
 //
 // One CTA computes one 128-row query tile of one head, walking the selected
 // key columns in 64-key tiles; two CTAs share an SM (256 TMEM columns and
-// ~106 KB of shared memory each), so their pipelines interleave on the SM's
+// ~113 KB of shared memory each), so their pipelines interleave on the SM's
 // tensor core:
-//   warp 4      TMA producer: Q once, then the K and V tiles of every selected
-//               tile into two-stage rings (no multicast).
+//   warp 4      TMA producer: Q once, then the K tiles into a three-stage ring
+//               and the V tiles into a two-stage ring (no multicast).
 //   warp 5      MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
 //               accumulator (2 x 64 columns), O += P V with P read from TMEM;
 //               completion is signalled with tcgen05.commit on mbarriers.
 //   warps 0-3   softmax: thread r owns query row r (TMEM lane r); reads S(n)
 //               while the tensor core computes S(n+1), applies the causal /
-//               ragged / block masks, keeps the running max (rescaling O in
-//               TMEM only when it grows by more than 2^8) and sum, and writes P
-//               as bf16 pairs over its S buffer; finally normalises O and stores.
+//               ragged / block masks, exponentiates against a running reference
+//               max (rescaling O and l in TMEM only when a score outgrows it by
+//               more than 2^64) and writes P as bf16 pairs over its S buffer;
+//               finally normalises O, stages the bf16 tile in shared memory and
+//               stores it row-contiguously to the output and to any peer GPUs'
+//               buffers (the sharded prefill's all-gather).
 // Unselected key tiles are never loaded.  Every mbarrier wait is bounded: on a
 // time-out the CTA records an error status, stops issuing work, waits (bounded)
 // for its own TMA copies and MMAs in flight, frees TMEM and exits.
@@ -243,7 +246,6 @@ constexpr uint32_t idesc_bf16(bool b_mn_major, int n) {
          | (uint32_t(kBM >> 4) << 24);    // M
 }
 
-// ------------------------------------------------------------------ layout
 // ------------------------------------------------------------------ layout
 constexpr int kKStages = 3;     // K tile ring (a stage is released by the S MMA that read it)
 constexpr int kVStages = 2;     // V tile ring (released by the PV MMA)
