@@ -28,7 +28,9 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _patch_with_oracle():
+def _patch_with_oracle(mp=None):
+    """Replace the CUDA entry points with oracle stand-ins; through ``mp`` (pytest's
+    monkeypatch, undone after the test) in the test process, for good in a worker."""
     from types import SimpleNamespace
 
     import fftsparse_b200 as F
@@ -58,15 +60,16 @@ def _patch_with_oracle():
     def fake_rope_pool(qp, kp, vp, h, hkv, cos, sin, block_size=128):
         return O.rope_pool(qp, kp, vp, h, hkv, cos, sin, block_size)
 
-    P.fft_block_mask = fake_mask
-    P.sparse_attention = fake_attn
-    F.myattn_prefill = fake_prefill
-    F.rope_pool = fake_rope_pool
+    put = mp.setattr if mp is not None else setattr
+    put(P, "fft_block_mask", fake_mask)
+    put(P, "sparse_attention", fake_attn)
+    put(F, "myattn_prefill", fake_prefill)
+    put(F, "rope_pool", fake_rope_pool)
 
 
-def _run(world, rank, case):
+def _run(world, rank, case, mp=None):
     import bench
-    _patch_with_oracle()
+    _patch_with_oracle(mp)
     dims, B, L, bs = CASES[case]
     kw = dict(bench.mask_kwargs(0.2), block_size=bs)
     model = bench.DecoderShape(LAYERS, torch.device("cpu"), world, rank, dims=dims, batch=B)
@@ -86,7 +89,7 @@ def _worker(rank, world, port, result_q, case):
 
 
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_decoder_two_ranks_equals_one(case):
+def test_decoder_two_ranks_equals_one(case, monkeypatch):
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
@@ -97,7 +100,7 @@ def test_decoder_two_ranks_equals_one(case):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    ref = _run(1, 0, case)
+    ref = _run(1, 0, case, monkeypatch)
     assert ref.shape == (CASES[case][1], CASES[case][0][-1])
     for r in (0, 1):
         logits = torch.from_numpy(np.frombuffer(got[r], dtype=np.float32).copy()).view_as(ref)
