@@ -6,14 +6,17 @@
 // the host at :342-357):
 //
 //   select_stage1_kernel  one launch for all independent per-head jobs:
-//      fft_partial_body   per (b, h, 8-channel chunk): zero-padded FFT of
-//                         z = q + i k per channel (warp-shuffle butterflies for
-//                         spans < 32, shared-memory butterflies above), cross
-//                         spectrum Q conj(K) summed over the chunk's channels
-//                         (batch_fft_cross_correlation, :117-131);
-//      diag_stats_body    per (b, h, sampled lag): the normalised variance of
-//                         one block-score diagonal (compute_stripe_variance,
-//                         :301-383);
+//      fft_warp_body /    per (b, h, 8-channel chunk): zero-padded FFT of
+//      fft_partial_body   z = q + i k per channel, cross spectrum Q conj(K)
+//                         summed over the chunk's channels
+//                         (batch_fft_cross_correlation, :117-131); a
+//                         register-resident FFT, one warp per channel, for
+//                         lengths up to 2048, else shared-memory butterflies;
+//                         both compute the same butterflies;
+//      diag_group_body    per (b, h, group of up to 8 sampled lags): the
+//                         normalised variance of each lag's block-score
+//                         diagonal (compute_stripe_variance, :301-383), with the
+//                         q and k rows the group needs staged once;
 //      colrow_body        per (b, h): hot key columns (create_column_block_mask,
 //                         :390-447) and the last query row's top-k
 //                         (create_last_block_query_mask, :54-72).
