@@ -17,6 +17,11 @@ host synchronisation:
 
 ``fft_block_mask`` additionally exposes the selected block mask (the
 reference's ``base_blockmask``) and the intermediate statistics.
+``rope_pool`` (ffts_rope_pool) serves the caller's side: the RoPE its
+attention forward applies before the call, the head-major layout and the
+pooling of q and k in one pass, whose pooled blocks ``fft_block_mask`` and
+``myattn_prefill`` accept (``pooled=``).  ``corr_mask_fraction`` feeds the
+reference's calibration hook.
 """
 from __future__ import annotations
 
