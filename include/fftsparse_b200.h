@@ -4,16 +4,20 @@
  * The reference operator is `myattn_prefill` in attn_src/fft_attn/my_attn_v7.py
  * (lines 454-792): block mean pooling, FFT lag correlation, stripe/diffuse head
  * classification, four auxiliary block masks, and a call into the third-party
- * `block_sparse_attn_func` CUDA kernel (my_attn_v7.py:775-786).  Every entry
- * point below replaces one step of that function; ffts_pool + ffts_block_mask
- * + ffts_sparse_attn_fwd, in that order, replace the whole of it.
+ * `block_sparse_attn_func` CUDA kernel (my_attn_v7.py:775-786).  ffts_pool +
+ * ffts_block_mask + ffts_sparse_attn_fwd, in that order, replace the whole of
+ * it; each cites the reference lines it replaces.  The other entry points serve
+ * the operator's caller (ffts_rope_pool: its RoPE, layout and the pooling in one
+ * pass) and the sharded prefill (query-row ranges, stores into peer GPUs'
+ * buffers, CUDA IPC mapping, copy-engine row pushes, epoch flags).
  *
  * Conventions
  *   - All tensor arguments are DEVICE pointers with explicit element strides.
  *     The caller owns every buffer (inputs, outputs and the workspace); the
  *     library allocates nothing per call.
- *   - Work is enqueued on `stream` (a cudaStream_t passed as void*); no entry
- *     point synchronises the host with the device.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*); no compute
+ *     entry point synchronises the host with the device (the IPC mapping calls
+ *     are one-time setup and may).
  *   - Every entry point returns FFTS_OK (0) or a negative FFTS_E* code; the
  *     message for the last failure on the calling thread is returned by
  *     ffts_last_error_string().  No C++ exception crosses this boundary.
