@@ -93,7 +93,7 @@ def load_peaks():
             p = json.load(f)
         return (float(p["hbm_gbs"]), float(p["bf16_tflops"]),
                 float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured")
-    except Exception:
+    except (OSError, ValueError, KeyError, TypeError):  # absent or malformed: the pool's earlier figures
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
@@ -127,7 +127,7 @@ class ClockSampler:
             deadline = time.time() + 10.0  # nvidia-smi takes a moment to start
             while time.time() < deadline and os.path.getsize(self.path) == 0 and self.proc.poll() is None:
                 time.sleep(0.02)
-        except Exception:
+        except OSError:  # no nvidia-smi: the summary says so
             self.proc = None
         return self
 
@@ -142,7 +142,7 @@ class ClockSampler:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
-            except Exception:
+            except subprocess.TimeoutExpired:
                 self.proc.kill()
             self.f.close()
 
@@ -551,8 +551,9 @@ def run_ours(args):
     tpath = os.path.join(HERE, "profiles", "attn_traffic.json")
     if os.path.exists(tpath):
         try:
-            traffic = json.load(open(tpath)).get("bytes_per_launch")
-        except Exception:
+            with open(tpath) as f:
+                traffic = json.load(f).get("bytes_per_launch")
+        except (OSError, ValueError, AttributeError):
             traffic = None
     roofline = {"kernel": "sparse_attn_kernel", "bound": "tensor", "achieved": round(achieved, 1),
                 "peak": bf16_peak, "unit": "TFLOP/s", "frac": round(achieved / bf16_peak, 4),
