@@ -9,6 +9,7 @@ Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
   rope_pool(q_proj, k_proj, v_proj, ...)    the caller's RoPE + head-major layout + pooling, one pass
   derive_mask_params(L, ...)                host-side parameter derivation
   calibrate.calibrate_from_qk(layers, t)    target-sparsity calibration on the device
+  decode_attention(q, k_cache, v_cache)     one-token decode over the un-expanded KV cache
   dist.sharded_prefill(...)                 KV-group sharded prefill (peer-memory all-gather)
 """
 from .params import derive_mask_params, MaskParams  # noqa: F401
@@ -22,6 +23,7 @@ from .prefill import (  # noqa: F401
     rope_pool,
     sparse_attention,
 )
+from .decode import decode_attention  # noqa: F401
 from ._lib import load as load_library, LIB_PATH  # noqa: F401
 
 __version__ = "0.1.0"

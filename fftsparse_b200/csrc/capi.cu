@@ -51,6 +51,10 @@ int launch_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t
                      int64_t v_ld, int64_t L, int64_t Hq, int64_t Hkv, int64_t D, const void *cos, const void *sin,
                      int64_t cs_ld, int bs, void *q_out, void *k_out, void *v_out, void *q_pooled, void *k_pooled,
                      cudaStream_t stream);
+int64_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits);
+int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const int64_t *ks, const void *v,
+                const int64_t *vs, int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
+                void *ws, int64_t ws_bytes, void *out, int64_t os_b, int64_t os_h, cudaStream_t stream);
 int64_t mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
                const ffts_mask_params *params, uint32_t *bits, int32_t *row_count, float *corr,
@@ -117,6 +121,22 @@ int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64
   if (rc) return rc;
   return launch_rope_pool(q_src, q_ld, k_src, k_ld, v_src, v_ld, L, Hq, Hkv, D, cos, sin, cs_ld, block_size,
                           q_out, k_out, v_out, q_pooled, k_pooled, static_cast<cudaStream_t>(stream));
+}
+
+int64_t ffts_decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits) {
+  return decode_workspace_bytes(B, H, Hkv, splits);
+}
+
+int32_t ffts_decode_attn(const void *q, int64_t q_stride_b, int64_t q_stride_h, const void *k_cache,
+                         const int64_t *k_strides, const void *v_cache, const int64_t *v_strides, int64_t B,
+                         int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits, void *workspace,
+                         int64_t workspace_bytes, void *out, int64_t out_stride_b, int64_t out_stride_h,
+                         void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return decode_attn(q, q_stride_b, q_stride_h, k_cache, k_strides, v_cache, v_strides, B, H, Hkv, Lk, D, splits,
+                     workspace, workspace_bytes, out, out_stride_b, out_stride_h, static_cast<cudaStream_t>(stream));
 }
 
 int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D) {

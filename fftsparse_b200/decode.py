@@ -1,0 +1,55 @@
+"""Decode attention after the FFTSparse prefill (ffts_decode_attn).
+
+The reference's callers switch to an eager decode branch once the prompt is
+prefilled (eval/LongBench/pred.py:306-322): softmax(q k^T / sqrt(D)) v over
+the repeat_kv-expanded cache, softmax in fp32.  ``decode_attention`` computes
+the same for one new token per sequence, reading the cache un-expanded in the
+head-major [B, Hkv, Lk, D] layout that ``rope_pool`` writes and an HF cache
+stores (the KV-cache handoff needs no copy), with fp32 scores, softmax and
+accumulation and a bf16 result.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_SMS = 148  # B200 streaming multiprocessors: the split count aims at ~4 CTAs per SM
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     splits: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [B, H, 1, D] or [B, H, D]; k_cache / v_cache [B, Hkv, Lk, D] (bf16, unit
+    stride over D, H % Hkv == 0, H / Hkv <= 16, D = 128).  Returns [B, H, D] bf16
+    (or fills ``out``)."""
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise ValueError("decode_attention takes one new token per sequence (q_len 1)")
+        q = q[:, :, 0]
+    if q.dim() != 3 or k_cache.dim() != 4 or v_cache.dim() != 4:
+        raise ValueError("q must be [B, H, D] (or [B, H, 1, D]) and the caches [B, Hkv, Lk, D]")
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"decode attention supports bfloat16 only (got {name} {t.dtype})")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} must be contiguous in the head dimension")
+    B, H, D = q.shape
+    _, Hkv, Lk, _ = k_cache.shape
+    if k_cache.shape[0] != B or v_cache.shape != k_cache.shape or k_cache.shape[3] != D:
+        raise ValueError(f"caches {tuple(k_cache.shape)} / {tuple(v_cache.shape)} do not match q {tuple(q.shape)}")
+    if splits is None:
+        splits = max(1, min((Lk + 127) // 128, (4 * _SMS + B * Hkv - 1) // (B * Hkv)))
+    if out is None:
+        out = torch.empty(B, H, D, dtype=torch.bfloat16, device=q.device)
+    lib = _lib.load()
+    nbytes = int(lib.ffts_decode_workspace_bytes(B, H, Hkv, splits))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    ks = _lib.i64_array([k_cache.stride(0), k_cache.stride(1), k_cache.stride(2)])
+    vs = _lib.i64_array([v_cache.stride(0), v_cache.stride(1), v_cache.stride(2)])
+    _lib.check(lib.ffts_decode_attn(q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), ks,
+                                    v_cache.data_ptr(), vs, B, H, Hkv, Lk, D, splits, ws.data_ptr(), nbytes,
+                                    out.data_ptr(), out.stride(0), out.stride(1),
+                                    torch.cuda.current_stream(q.device).cuda_stream))
+    return out

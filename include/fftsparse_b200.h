@@ -133,6 +133,27 @@ FFTS_API int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_s
                   void *q_out, void *k_out, void *v_out, void *q_pooled, void *k_pooled,
                   void *stream);
 
+/*
+ * Decode attention for one new token per sequence over the KV cache.  Replaces
+ * the caller's eager decode branch (eval/LongBench/pred.py:306-322:
+ * softmax(q k^T / sqrt(D)) v over the repeat_kv-expanded cache) after the
+ * prefill, reading the cache un-expanded.
+ *   q [B, H, D] bf16 (strides q_stride_b, q_stride_h; unit over D);
+ *   k_cache, v_cache [B, Hkv, Lk, D] bf16 with strides (b, h, l), H % Hkv == 0,
+ *     H / Hkv <= 16 (the layout ffts_rope_pool writes and an HF cache stores);
+ *   out [B, H, D] bf16 (strides out_stride_b, out_stride_h).
+ * The keys are split over `splits` CTAs per KV head (fewer when Lk is short);
+ * the workspace holds their partial results (ffts_decode_workspace_bytes).
+ * fp32 scores, softmax and accumulation; D must be 128.
+ */
+FFTS_API int64_t ffts_decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits);
+FFTS_API int32_t ffts_decode_attn(const void *q, int64_t q_stride_b, int64_t q_stride_h,
+                  const void *k_cache, const int64_t *k_strides /* b,h,l */,
+                  const void *v_cache, const int64_t *v_strides /* b,h,l */,
+                  int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
+                  void *workspace, int64_t workspace_bytes, void *out,
+                  int64_t out_stride_b, int64_t out_stride_h, void *stream);
+
 /* Bytes of device workspace ffts_block_mask / ffts_prefill need. */
 FFTS_API int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 

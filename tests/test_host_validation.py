@@ -59,3 +59,16 @@ def test_sparse_attention_rejects_non_bf16():
     bits = torch.zeros(1, 4, 16, 1, dtype=torch.int32)
     with pytest.raises(TypeError):
         F.sparse_attention(q, k, v, bits, 128)
+
+
+def test_decode_rejects_bad_arguments():
+    q = torch.zeros(1, 8, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(1, 2, 64, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):  # more than one new token
+        F.decode_attention(torch.zeros(1, 8, 2, 128, dtype=torch.bfloat16), kc, kc)
+    with pytest.raises(TypeError):  # fp32 cache
+        F.decode_attention(q, kc.float(), kc.float())
+    with pytest.raises(ValueError):  # caches of different shapes
+        F.decode_attention(q, kc, kc[:, :, :32])
+    with pytest.raises(ValueError):  # batch mismatch
+        F.decode_attention(torch.zeros(2, 8, 128, dtype=torch.bfloat16), kc, kc)
