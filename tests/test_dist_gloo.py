@@ -217,3 +217,18 @@ def test_dead_rank_raises_on_peer():
         if p.is_alive():
             p.kill()
     assert res != "no error"
+
+
+def test_row_chunks_cover_rows_with_equal_causal_work():
+    from fftsparse_b200.dist import row_chunks
+    L = 131072
+    for parts in (2, 4, 8):
+        ch = row_chunks(L, parts)
+        assert ch[0][0] == 0 and ch[-1][1] == L and len(ch) == parts
+        assert all(a[1] == b[0] for a, b in zip(ch, ch[1:]))          # contiguous
+        assert all(lo % 128 == 0 for lo, _ in ch)                      # on tile-row boundaries
+        work = [(hi * hi - lo * lo) / (L * L) for lo, hi in ch]      # causal work ~ rows squared
+        assert max(work) - min(work) < 0.01
+    assert row_chunks(L, 4) == [(0, 65536), (65536, 92672), (92672, 113536), (113536, 131072)]
+    assert row_chunks(1000, 4) == [(0, 1000)]                          # short: one chunk
+    assert row_chunks(L, 1) == [(0, L)]
