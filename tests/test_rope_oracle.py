@@ -31,8 +31,9 @@ def test_rope_equals_hf_apply_rotary_pos_emb(L, Hq, Hkv, scale):
     assert torch.equal(O.rope(k_src, Hkv, cos, sin), ke)
 
 
-def test_rope_pool_pools_the_rotated_tensors():
-    D, L, Hq, Hkv, bs = 128, 1000, 2, 1, 128
+@pytest.mark.parametrize("bs", [128, 64, 32])
+def test_rope_pool_pools_the_rotated_tensors(bs):
+    D, L, Hq, Hkv = 128, 1000, 2, 1
     g = torch.Generator().manual_seed(5)
     qkv = torch.randn(L, (Hq + 2 * Hkv) * D, generator=g).bfloat16()
     cos, sin = rope_tables(L)
