@@ -16,7 +16,14 @@ import torch
 
 from . import _lib
 
-_SMS = 148  # B200 streaming multiprocessors: the split count aims at ~4 CTAs per SM
+_SM_COUNT = {}  # device index -> streaming multiprocessors (the split count aims at ~4 CTAs per SM)
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SM_COUNT[idx]
 
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -40,7 +47,8 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if k_cache.shape[0] != B or v_cache.shape != k_cache.shape or k_cache.shape[3] != D:
         raise ValueError(f"caches {tuple(k_cache.shape)} / {tuple(v_cache.shape)} do not match q {tuple(q.shape)}")
     if splits is None:
-        splits = max(1, min((Lk + 127) // 128, (4 * _SMS + B * Hkv - 1) // (B * Hkv)))
+        sms = _sm_count(q.device)
+        splits = max(1, min((Lk + 127) // 128, (4 * sms + B * Hkv - 1) // (B * Hkv)))
     if out is None:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=q.device)
     lib = _lib.load()

@@ -269,8 +269,15 @@ class PeerGather:
                                        cur.cuda_stream))
         return buf
 
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
     def close(self):
-        """Unmap the peers' buffers (after every rank's last call has completed)."""
+        """Unmap the peers' buffers (after every rank's last call has completed;
+        ``with PeerGather(...) as pg:`` calls it on leaving the block)."""
         torch.cuda.synchronize(self.device)
         for ptr, off in self._opened:
             self.lib.ffts_ipc_close(ptr, off)
