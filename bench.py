@@ -80,6 +80,8 @@ def parse():
                     help="BASELINE config of the TTFT decoder (4: Llama-3.1-8B shape, 1 x seq-len tokens; "
                          "5: Qwen2.5-7B shape, 2 x 65536 tokens, block 64)")
     ap.add_argument("--ttft-seq-len", type=int, default=0, help="config 5 sequence length (0: 65536)")
+    ap.add_argument("--clock-log", default="",
+                    help="directory for the raw nvidia-smi clock samples (default: a temporary directory)")
     return ap.parse_args()
 
 
@@ -111,10 +113,11 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, log_dir: str = ""):
+        import tempfile
         self.index = index
         self.proc = None
-        self.path = os.path.join(HERE, "gpurun_out", f"clocks_gpu{index}.csv")
+        self.path = os.path.join(log_dir or tempfile.mkdtemp(prefix="ffts_clocks_"), f"clocks_gpu{index}.csv")
         self.t0 = self.t1 = None
 
     def __enter__(self):
@@ -472,7 +475,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # clocks are sampled from before the first warm-up step to the last measurement
-    clocks = ClockSampler(local_rank).__enter__()
+    clocks = ClockSampler(local_rank, args.clock_log).__enter__()
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize(dev)

@@ -11,6 +11,7 @@ Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
   calibrate.calibrate_from_qk(layers, t)    target-sparsity calibration on the device
   decode_attention(q, k_cache, v_cache)     one-token decode over the un-expanded KV cache
   dist.sharded_prefill(...)                 KV-group sharded prefill (peer-memory all-gather)
+  check_status(device=None)                 raise WaitTimeout if a kernel's bounded wait ran out
 """
 from .params import derive_mask_params, MaskParams  # noqa: F401
 from .prefill import (  # noqa: F401
@@ -24,6 +25,7 @@ from .prefill import (  # noqa: F401
     sparse_attention,
 )
 from .decode import decode_attention  # noqa: F401
+from .status import WaitTimeout, check_status  # noqa: F401
 from ._lib import load as load_library, LIB_PATH  # noqa: F401
 
 __version__ = "0.1.0"

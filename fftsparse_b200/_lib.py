@@ -40,7 +40,7 @@ EXPORTS = {
                               _P, _P, _P, _P, _P, _P]),
     "ffts_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64]),
     "ffts_decode_attn": (_I32, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P,
-                                _I64, _I64, _P]),
+                                _I64, _I64, _P, _I32, _I64, _P]),
     "ffts_sparse_attn_fwd": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I32,
                                     _I32, _P, _P, _P, _P]),
     "ffts_sparse_attn_fwd_rows": (_I32, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I32,

@@ -47,8 +47,8 @@ constexpr int kKVBytes = kBN * kD * 2;       // 16 KB: two [64 rows][64 cols] sw
 constexpr int kKVHalf = kKVBytes / 2;
 constexpr int kMaxTiles = 4096;              // 64-key tiles per query tile (L <= 262144)
 constexpr int kTileWords = kMaxTiles / 32;   // tile bitmask words
-constexpr long long kWaitCycles = 4000000000ll;   // ~2 s at 1.965 GHz: bound on one wait
-constexpr long long kDrainCycles = 8000000000ll;  // ~4 s: bound on draining own copies / MMAs
+constexpr double kWaitSeconds = 2.0;   // bound on one wait (SM cycles at the device's clock, from the host)
+constexpr double kDrainSeconds = 4.0;  // bound on draining own copies / MMAs
 
 // status codes written to the caller's status word
 constexpr int kErrTimeoutProducer = 1;
@@ -105,7 +105,7 @@ __device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
 // Bounded wait: false on time-out (SM clock cycles) or when another role has
 // aborted the CTA.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          long long limit = kWaitCycles) {
+                                          long long limit) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
@@ -301,6 +301,8 @@ struct Params {
   int out_row0;              // query row written at output row 0
   float scale_log2;
   int *status;
+  long long wait_cycles;   // bound on one wait, SM cycles
+  long long drain_cycles;  // bound on draining own copies / MMAs
   // Peer GPUs' output buffers (CUDA IPC mappings, same strides as out): every
   // output tile is also stored into each of them, so a sharded prefill's
   // all-gather rides on the epilogue over NVLink.
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // stage once PV(n-2) has (the PV barrier of that buffer): the phase the
         // V wait names is the latest one, since PV(n) needs the copy issued here
         const int full = (is_k ? BKF : BVF) + s, empty = (is_k ? BKE : BPV) + s;
-        if (!mbar_wait(bar(empty), ((n / ns) & 1) ^ 1, abort_flag)) return false;
+        if (!mbar_wait(bar(empty), ((n / ns) & 1) ^ 1, abort_flag, prm.wait_cycles)) return false;
         mbar_arrive_tx(bar(full), kKVBytes);
         const uint32_t dst = sbase + (is_k ? SmemLayout::k : SmemLayout::v) + s * kKVBytes;
         const CUtensorMap *map = is_k ? &tm_k : &tm_v;
@@ -481,11 +483,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         atomicCAS(prm.status, 0, kErrTimeoutProducer);
         // wait (bounded, ignoring the abort flag) for the copies this thread issued
         volatile int never = 0;
-        mbar_wait(bar(BQ), 0, &never, kDrainCycles);
+        mbar_wait(bar(BQ), 0, &never, prm.drain_cycles);
         for (int n = max(0, issued_k - kKStages); n < issued_k; ++n)
-          mbar_wait(bar(BKF + n % kKStages), (n / kKStages) & 1, &never, kDrainCycles);
+          mbar_wait(bar(BKF + n % kKStages), (n / kKStages) & 1, &never, prm.drain_cycles);
         for (int n = max(0, issued_v - 2); n < issued_v; ++n)
-          mbar_wait(bar(BVF + n % 2), (n >> 1) & 1, &never, kDrainCycles);
+          mbar_wait(bar(BVF + n % 2), (n >> 1) & 1, &never, prm.drain_cycles);
       }
     }
   } else if (warp == 5) {
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // execute in issue order, so PV(n) has read P(n) by then.
     if (lane == 0 && ntiles > 0) {
       const uint32_t idS = idesc_bf16(false, kBN), idPV = idesc_bf16(true, kD);
-      bool ok = mbar_wait(bar(BQ), 0, abort_flag);
+      bool ok = mbar_wait(bar(BQ), 0, abort_flag, prm.wait_cycles);
       fence_after();
       // Shared-memory descriptors of the tile bases; a 16-byte multiple offset
       // within shared memory adds (offset >> 4) to the address field, which
@@ -505,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t dv0 = smem_desc(sbase + SmemLayout::v, kKVHalf, 1024);
       auto issue_s = [&](int n) -> bool {
         const int s = n % 2, ks = n % kKStages;
-        if (!mbar_wait(bar(BKF + ks), (n / kKStages) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(BKF + ks), (n / kKStages) & 1, abort_flag, prm.wait_cycles)) return false;
         fence_after();
         const uint64_t dk = dk0 + uint64_t((ks * kKVBytes) >> 4);
         const uint32_t td = tmem + s * kBN;
@@ -521,8 +523,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       };
       auto issue_pv = [&](int m) -> bool {
         const int s = m % 2;
-        if (!mbar_wait(bar(BVF + s), (m >> 1) & 1, abort_flag)) return false;
-        if (!mbar_wait(bar(BPF + s), (m >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(bar(BVF + s), (m >> 1) & 1, abort_flag, prm.wait_cycles)) return false;
+        if (!mbar_wait(bar(BPF + s), (m >> 1) & 1, abort_flag, prm.wait_cycles)) return false;
         fence_after();
         const uint64_t dv = dv0 + uint64_t((s * kKVBytes) >> 4);
         const uint32_t pt = tmem + s * kBN;  // P(m): bf16 pairs in the first 32 columns of S buffer m % 2
@@ -545,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // drain: wait (bounded) until every MMA this thread issued has completed
       umma_commit(bar(BDRAIN));
       volatile int never = 0;
-      mbar_wait(bar(BDRAIN), 0, &never, kDrainCycles);
+      mbar_wait(bar(BDRAIN), 0, &never, prm.drain_cycles);
     }
   } else {
     // ================================================================ softmax (warps 0-3)
@@ -562,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int n = 0; n < ntiles; ++n) {
       const int sb = n % 2;
       const int j = cur.next();
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag))) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag, prm.wait_cycles))) { ok = false; break; }
       fence_after();
       const uint32_t s_addr = tmem + sb * kBN + lane_off;
       // masks: causal diagonal, ragged end, and (block_size < 128) this row's own
@@ -579,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint32_t m = rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : ((1u << rem) - 1u));
           if (prm.bs < kBM) {
             const int blk = (col0 + 32 * w) >> prm.bs_shift;
-            if (!((rowbits[blk >> 5] >> (blk & 31)) & 1u)) m = 0u;
+            if (blk >= prm.nblk || !((rowbits[blk >> 5] >> (blk & 31)) & 1u)) m = 0u;
           }
           kw[w] = m;
         }
@@ -663,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // barrier of S buffer (n-1) % 2; that barrier's previous phase (PV(n-3))
         // is complete and its next (PV(n+1)) needs P(n+1), so the parity is exact.
         if (!__all_sync(0xffffffffu,
-                        mbar_wait(bar(BPV + (n - 1) % 2), ((n - 1) >> 1) & 1, abort_flag))) {
+                        mbar_wait(bar(BPV + (n - 1) % 2), ((n - 1) >> 1) & 1, abort_flag, prm.wait_cycles))) {
           ok = false;
           break;
         }
@@ -691,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // later phase, so the parity is exact.
     if (ok && ntiles > 0) {
       const int m = ntiles - 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV + m % 2), (m >> 1) & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(BPV + m % 2), (m >> 1) & 1, abort_flag, prm.wait_cycles));
     }
     if (!ok) {
       *abort_flag = 1;
@@ -860,6 +862,9 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
   p.qt_cnt = int(ceil_div(row_hi, kBM) - row_lo / kBM);
   p.out_row0 = int(row_lo);
   p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
+  rc = device_wait_cycles(kWaitSeconds, &p.wait_cycles);
+  if (!rc) rc = device_wait_cycles(kDrainSeconds, &p.drain_cycles);
+  if (rc) return rc;
   p.n_peers = n_peers;
   for (int i = 0; i < n_peers; ++i) p.peer_out[i] = static_cast<__nv_bfloat16 *>(peer_out[i]);
   if (status) {

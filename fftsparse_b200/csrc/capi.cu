@@ -45,6 +45,46 @@ int ensure_func_smem(const void *func, int bytes, int carveout) {
   return FFTS_OK;
 }
 
+namespace {
+struct DeviceProps {
+  int sms = 0;
+  int clock_khz = 0;
+};
+
+int device_props(DeviceProps *out) {
+  static std::mutex mu;
+  static std::map<int, DeviceProps> cache;
+  int dev = 0;
+  FFTS_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it == cache.end()) {
+    DeviceProps p;
+    FFTS_CUDA(cudaDeviceGetAttribute(&p.sms, cudaDevAttrMultiProcessorCount, dev));
+    FFTS_CUDA(cudaDeviceGetAttribute(&p.clock_khz, cudaDevAttrClockRate, dev));
+    if (p.sms <= 0) p.sms = 1;
+    if (p.clock_khz <= 0) p.clock_khz = 2000000;  // an unreported clock: assume 2 GHz
+    it = cache.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return FFTS_OK;
+}
+}  // namespace
+
+int device_sm_count(int *out) {
+  DeviceProps p;
+  const int rc = device_props(&p);
+  if (rc == FFTS_OK) *out = p.sms;
+  return rc;
+}
+
+int device_wait_cycles(double seconds, long long *out) {
+  DeviceProps p;
+  const int rc = device_props(&p);
+  if (rc == FFTS_OK) *out = static_cast<long long>(seconds * 1e3 * double(p.clock_khz));
+  return rc;
+}
+
 int launch_pool(const void *x, int dtype, int64_t B, int64_t H, int64_t L, int64_t D, int64_t sb,
                 int64_t sh, int64_t sl, int bs, void *out, cudaStream_t stream);
 int launch_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t k_ld, const void *v_src,
@@ -54,7 +94,8 @@ int launch_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t
 int64_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits);
 int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const int64_t *ks, const void *v,
                 const int64_t *vs, int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
-                void *ws, int64_t ws_bytes, void *out, int64_t os_b, int64_t os_h, cudaStream_t stream);
+                void *ws, int64_t ws_bytes, void *out, int64_t os_b, int64_t os_h, const void *bias,
+                int bias_dtype, int64_t bias_sb, cudaStream_t stream);
 int64_t mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);
 int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, int64_t Hkv, int64_t D,
                const ffts_mask_params *params, uint32_t *bits, int32_t *row_count, float *corr,
@@ -131,12 +172,13 @@ int32_t ffts_decode_attn(const void *q, int64_t q_stride_b, int64_t q_stride_h, 
                          const int64_t *k_strides, const void *v_cache, const int64_t *v_strides, int64_t B,
                          int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits, void *workspace,
                          int64_t workspace_bytes, void *out, int64_t out_stride_b, int64_t out_stride_h,
-                         void *stream) {
+                         const void *mask, int32_t mask_dtype, int64_t mask_stride_b, void *stream) {
   g_last_error.clear();
   int rc = check_device();
   if (rc) return rc;
   return decode_attn(q, q_stride_b, q_stride_h, k_cache, k_strides, v_cache, v_strides, B, H, Hkv, Lk, D, splits,
-                     workspace, workspace_bytes, out, out_stride_b, out_stride_h, static_cast<cudaStream_t>(stream));
+                     workspace, workspace_bytes, out, out_stride_b, out_stride_h, mask, mask_dtype, mask_stride_b,
+                     static_cast<cudaStream_t>(stream));
 }
 
 int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D) {

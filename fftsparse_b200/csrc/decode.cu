@@ -14,6 +14,10 @@
 //            sum l, the chunk's exponentials in place;
 //   P V      thread = output dimension; V rows read coalesced; G accumulators,
 //            rescaled when the running max moves.
+// An optional additive bias per (sequence, key) -- the caller's attention mask,
+// added to the scaled scores before the softmax as at pred.py:311-313 -- is
+// read once per key with the key's scores.  Fully masked chunks contribute
+// nothing (their maxima stay -inf and their exponentials are 0).
 // The split's (o[D], m, l) per head go to a workspace.
 // decode_merge_kernel: CTA = (b, q head): o = sum_s 2^(m_s - M) o_s /
 // sum_s 2^(m_s - M) l_s, rounded to bf16.
@@ -39,7 +43,18 @@ struct Params {
   int B, H, Hkv, Lk, splits, per_split;
   float scale_log2;
   float *ws;  // [B * Hkv, splits, G, D + 2]: o, m, l
+  const void *bias;    // additive mask [B, Lk] (row stride bias_sb), fp32 or bf16; nullptr = none
+  int bias_bf16;
+  int64_t bias_sb;
 };
+
+__device__ __forceinline__ float bias_log2(const Params &p, int b, int key) {
+  if (p.bias == nullptr) return 0.0f;
+  const int64_t i = int64_t(b) * p.bias_sb + key;
+  const float x = p.bias_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(p.bias)[i])
+                              : static_cast<const float *>(p.bias)[i];
+  return x * 1.4426950408889634f;  // scores are kept in log2 units
+}
 
 __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_constant__ Params p) {
   __shared__ float q_s[kMaxG][kD];
@@ -92,9 +107,10 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
           }
         }
       }
+      const float bl = bias_log2(p, b, c0 + t);
 #pragma unroll
       for (int g = 0; g < kMaxG; ++g)
-        if (g < G) s_s[g][t] = dot[g] * p.scale_log2;
+        if (g < G) s_s[g][t] = fmaf(dot[g], p.scale_log2, bl);
     }
     __syncthreads();
     const int warp = t >> 5, lane = t & 31;
@@ -106,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
       const float m_new = fmaxf(m_old, mx);
       float sum = 0.0f;
       for (int i = lane; i < n; i += 32) {
-        const float e = exp2f(s_s[g][i] - m_new);
+        const float e = m_new == -INFINITY ? 0.0f : exp2f(s_s[g][i] - m_new);
         s_s[g][i] = e;
         sum += e;
       }
@@ -171,7 +187,8 @@ int64_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits
 
 int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const int64_t *ks, const void *v,
                 const int64_t *vs, int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
-                void *ws, int64_t ws_bytes, void *out, int64_t os_b, int64_t os_h, cudaStream_t stream) {
+                void *ws, int64_t ws_bytes, void *out, int64_t os_b, int64_t os_h, const void *bias,
+                int bias_dtype, int64_t bias_sb, cudaStream_t stream) {
   using namespace decode;
   FFTS_REQUIRE(q && k && v && ks && vs && ws && out, "decode: NULL argument");
   FFTS_REQUIRE(D == kD, "decode: head_dim must be 128 (got %lld)", (long long)D);
@@ -208,6 +225,13 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   p.splits = int(nsplit);
   p.scale_log2 = float(1.4426950408889634 / sqrt(double(D)));
   p.ws = static_cast<float *>(ws);
+  FFTS_REQUIRE(bias == nullptr || bias_dtype == FFTS_DTYPE_F32 || bias_dtype == FFTS_DTYPE_BF16,
+               "decode: the additive mask must be fp32 or bf16");
+  FFTS_REQUIRE(bias == nullptr || B == 1 || bias_sb >= Lk, "decode: mask row stride %lld shorter than Lk %lld",
+               (long long)bias_sb, (long long)Lk);
+  p.bias = bias;
+  p.bias_bf16 = bias_dtype == FFTS_DTYPE_BF16 ? 1 : 0;
+  p.bias_sb = bias_sb;
   decode_split_kernel<<<dim3(unsigned(B * Hkv), unsigned(nsplit)), kThreads, 0, stream>>>(p);
   FFTS_CUDA(cudaGetLastError());
   decode_merge_kernel<<<unsigned(B * H), kThreads, 0, stream>>>(p, static_cast<__nv_bfloat16 *>(out), os_b, os_h);

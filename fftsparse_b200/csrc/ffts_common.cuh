@@ -18,6 +18,11 @@ int cuda_status(cudaError_t e, const char *what);
 // set its preferred carveout) on the current device; the attribute calls are made
 // only when the value grows, so per-call launches skip them.
 int ensure_func_smem(const void *func, int bytes, int carveout = -1);
+// Properties of the current device, looked up once per device: its SM count and
+// the number of SM clock cycles in `seconds` at its maximum SM clock (the bound
+// of a kernel's spin-waits, which count cycles with clock64).
+int device_sm_count(int *out);
+int device_wait_cycles(double seconds, long long *out);
 
 #define FFTS_REQUIRE(cond, ...)                          \
   do {                                                   \

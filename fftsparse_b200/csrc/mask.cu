@@ -1312,7 +1312,11 @@ int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, 
 int unpack_mask(const uint32_t *bits, int64_t B, int64_t H, int64_t N, uint8_t *out, cudaStream_t stream) {
   FFTS_REQUIRE(bits && out && B > 0 && H > 0 && N > 0, "bad unpack arguments");
   const int64_t total = B * H * N * N;
-  const int blocks = int(std::min<int64_t>(ceil_div(total, 256), 148 * 16));
+  int sms = 1;
+  const int rc = device_sm_count(&sms);
+  if (rc) return rc;
+  // a grid-stride loop: enough CTAs to fill every SM 16 deep, fewer for small masks
+  const int blocks = int(std::min<int64_t>(ceil_div(total, 256), int64_t(sms) * 16));
   unpack_kernel<<<blocks, 256, 0, stream>>>(bits, B * H * N, N, out);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;

@@ -35,7 +35,7 @@
 namespace ffts {
 namespace peer {
 
-constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.965 GHz
+constexpr double kWaitSeconds = 2.0;  // bound on the flag wait (converted to SM cycles per device)
 constexpr int kErrPeerTimeout = 5;
 
 constexpr int kMaxPeers = 32;
@@ -49,7 +49,7 @@ __global__ void signal_kernel(FlagList flags, int n, int32_t value) {
     asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(flags.flag[threadIdx.x]), "r"(value) : "memory");
 }
 
-__global__ void wait_kernel(const int32_t *flags, int n, int32_t epoch, int32_t *status) {
+__global__ void wait_kernel(const int32_t *flags, int n, int32_t epoch, int32_t *status, long long limit) {
   const int i = threadIdx.x;
   if (i >= n) return;
   const long long t0 = clock64();
@@ -57,7 +57,7 @@ __global__ void wait_kernel(const int32_t *flags, int n, int32_t epoch, int32_t 
     int32_t v;
     asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
     if (v >= epoch) break;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicCAS(status, 0, kErrPeerTimeout);
       break;
     }
@@ -153,7 +153,10 @@ FFTS_API int32_t ffts_signal(int32_t *const *flags, void *const *streams, int32_
 
 FFTS_API int32_t ffts_wait_flags(const int32_t *flags, int32_t n, int32_t epoch, int32_t *status, void *stream) {
   FFTS_REQUIRE(flags && status && n >= 1 && n <= 32, "wait_flags: bad argument");
-  peer::wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, n, epoch, status);
+  long long limit = 0;
+  const int rc = device_wait_cycles(peer::kWaitSeconds, &limit);
+  if (rc) return rc;
+  peer::wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, n, epoch, status, limit);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }

@@ -25,6 +25,8 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from .status import StatusWord
+
 
 @dataclass(frozen=True)
 class Shard:
@@ -159,8 +161,11 @@ class PeerGather:
 
     The two buffers alternate between calls, so the tensor a call returns stays
     valid until the call after next; consume it (o_proj) before that.  One
-    sequence (B = 1), KV-group shards, bf16 output.  ``status`` is nonzero after
-    a wait that timed out (a peer never delivered its rows)."""
+    sequence (B = 1), KV-group shards, bf16 output.  ``status`` (int32 [1]) is
+    nonzero after a bounded wait of the attention kernel or of the flag wait
+    timed out (code 5: a peer never delivered its rows); ``run`` raises
+    WaitTimeout for it at the first call after the failing one has completed,
+    and ``check()`` raises at once."""
 
     def __init__(self, num_heads: int, seq_len: int, head_dim: int = 128, group=None, device=None,
                  push: str = "epilogue", chunks: int = 4):
@@ -181,7 +186,8 @@ class PeerGather:
         self.bufs = [torch.empty(1, num_heads, seq_len, head_dim, dtype=torch.bfloat16, device=self.device)
                      for _ in range(2)]
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=self.device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status_word = StatusWord(self.device)
+        self.status = self.status_word.word
         torch.cuda.synchronize(self.device)
 
         def handle(t):
@@ -234,6 +240,7 @@ class PeerGather:
 
         lib, dev, ct = self.lib, self.device, ctypes
         cur = torch.cuda.current_stream(dev)
+        self.status_word.poll()  # a time-out of an earlier call, once its read-back has landed
         self.epoch += 1
         e, slot = self.epoch, self.epoch % 2
         buf = self.bufs[slot]
@@ -244,18 +251,19 @@ class PeerGather:
         bases = self._dst[slot]
         if self.push == "epilogue":
             mine = buf[:, shard.h_lo:shard.h_hi].permute(0, 2, 1, 3)
-            sparse_attention(ql, kl, vl, bits, block_size, causal=causal, out=mine,
+            sparse_attention(ql, kl, vl, bits, block_size, causal=causal, out=mine, status=self.status,
                              peers=[b + shard.h_lo * pitch for b in bases[:self._npeers]])
             n = self._npeers + 1
             _lib.check(lib.ffts_signal(self._all_flags, (ct.c_void_p * n)(*([cur.cuda_stream] * n)), n, e))
             _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
                                            cur.cuda_stream))
+            self.status_word.read_back(cur)
             return buf
         # the buffer used now was last read by this rank's pushes two calls ago
         for st in self.streams:
             cur.wait_stream(st)
         for (lo, hi), done in zip(self.chunks, self.events):
-            sparse_attention(ql, kl, vl, bits, block_size, causal=causal,
+            sparse_attention(ql, kl, vl, bits, block_size, causal=causal, status=self.status,
                              out=buf[:, shard.h_lo:shard.h_hi, lo:hi].permute(0, 2, 1, 3), rows=(lo, hi))
             done.record(cur)
             off = shard.h_lo * pitch + lo * row_bytes
@@ -267,7 +275,12 @@ class PeerGather:
         _lib.check(lib.ffts_signal(self._own_flag, (ct.c_void_p * 1)(cur.cuda_stream), 1, e))
         _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
                                        cur.cuda_stream))
+        self.status_word.read_back(cur)
         return buf
+
+    def check(self) -> None:
+        """Wait for the device and raise WaitTimeout if any call so far timed out."""
+        self.status_word.check()
 
     def __enter__(self):
         return self

@@ -33,6 +33,7 @@ import torch
 
 from . import _lib
 from .params import SEL_TOPK, derive_mask_params, MaskParams
+from .status import device_status
 
 __all__ = ["myattn_prefill", "fft_block_mask", "sparse_attention", "pool_blocks", "BlockMask",
            "AttentionCache", "_attention_cache"]
@@ -299,6 +300,11 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: to
     With ``peers`` (device addresses of other GPUs' buffers laid out like ``out``,
     mapped into this process) every output row is also stored there by the
     kernel's epilogue (ffts_sparse_attn_fwd_push).
+
+    ``status`` (int32 [1] on q's device) receives the code of a bounded wait that
+    timed out; the caller then reads it.  Without it the device's own status word
+    is used (fftsparse_b200.status): a time-out raises WaitTimeout at the first
+    call after the failing kernel has completed, or at ``check_status()``.
     """
     for name, t in (("q", q), ("k", k), ("v", v)):
         _check_4d(name, t)
@@ -314,7 +320,12 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: to
     ks = _lib.i64_array([k.stride(0), k.stride(1), k.stride(2)])
     vs = _lib.i64_array([v.stride(0), v.stride(1), v.stride(2)])
     os_ = _lib.i64_array([out.stride(0), out.stride(2), out.stride(1)])
-    st = status.data_ptr() if status is not None else None
+    own = None
+    if status is None:
+        own = device_status(q.device)
+        own.poll()  # an earlier call's time-out, if its read-back has landed
+        status = own.word
+    st = status.data_ptr()
     if peers:
         arr = (_lib.ctypes.c_void_p * len(peers))(*peers)
         _lib.check(lib.ffts_sparse_attn_fwd_push(
@@ -329,6 +340,8 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bits: to
         _lib.check(lib.ffts_sparse_attn_fwd_rows(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, Hkv, L, D, qs, ks, vs, bits.data_ptr(),
             block_size, int(bool(causal)), lo, hi, out.data_ptr(), os_, st, _stream_ptr(q.device)))
+    if own is not None:
+        own.read_back()
     return out
 
 

@@ -141,7 +141,12 @@ FFTS_API int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_s
  *   q [B, H, D] bf16 (strides q_stride_b, q_stride_h; unit over D);
  *   k_cache, v_cache [B, Hkv, Lk, D] bf16 with strides (b, h, l), H % Hkv == 0,
  *     H / Hkv <= 16 (the layout ffts_rope_pool writes and an HF cache stores);
- *   out [B, H, D] bf16 (strides out_stride_b, out_stride_h).
+ *   out [B, H, D] bf16 (strides out_stride_b, out_stride_h);
+ *   mask: NULL, or the caller's additive attention mask for this step, [B, Lk]
+ *     (row stride mask_stride_b, unit over keys; dtype FFTS_DTYPE_F32 or
+ *     FFTS_DTYPE_BF16), added to q k^T / sqrt(D) before the softmax as
+ *     pred.py:311-313 adds attention_mask[:, :, :, :Lk] (0 keeps a key, a large
+ *     negative value such as the dtype's minimum drops it; padding of a batch).
  * The keys are split over `splits` CTAs per KV head (fewer when Lk is short);
  * the workspace holds their partial results (ffts_decode_workspace_bytes).
  * fp32 scores, softmax and accumulation; D must be 128.
@@ -152,7 +157,8 @@ FFTS_API int32_t ffts_decode_attn(const void *q, int64_t q_stride_b, int64_t q_s
                   const void *v_cache, const int64_t *v_strides /* b,h,l */,
                   int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
                   void *workspace, int64_t workspace_bytes, void *out,
-                  int64_t out_stride_b, int64_t out_stride_h, void *stream);
+                  int64_t out_stride_b, int64_t out_stride_h,
+                  const void *mask, int32_t mask_dtype, int64_t mask_stride_b, void *stream);
 
 /* Bytes of device workspace ffts_block_mask / ffts_prefill need. */
 FFTS_API int64_t ffts_mask_workspace_bytes(int64_t B, int64_t H, int64_t N, int64_t D);

@@ -30,7 +30,8 @@ import types
 
 import torch
 
-REF_ROOT = os.environ.get("FFTS_REFERENCE_ROOT", "/root/reference")
+# The reference checkout is named explicitly by the caller; there is no default path.
+REF_ROOT = os.environ.get("FFTS_REFERENCE_ROOT", "")
 
 _captured: dict = {}
 _module = None
@@ -122,8 +123,10 @@ def load_reference():
     global _module
     if _module is not None:
         return _module
+    if not REF_ROOT:
+        raise RuntimeError("set FFTS_REFERENCE_ROOT to the root of a PureEidolon/FFTSparse checkout")
     if not os.path.isdir(os.path.join(REF_ROOT, "attn_src")):
-        raise RuntimeError(f"reference checkout not found at {REF_ROOT}")
+        raise RuntimeError(f"reference checkout not found at FFTS_REFERENCE_ROOT={REF_ROOT}")
     _stub_matplotlib()
     bsa = types.ModuleType("block_sparse_attn")
     bsa.block_sparse_attn_func = _block_sparse_attn_stub

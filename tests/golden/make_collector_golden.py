@@ -1,7 +1,7 @@
 """Record the reference's calibration-hook values for every golden case.
 
-Run in a container that holds the reference checkout (default
-/root/reference, override with FFTS_REFERENCE_ROOT):
+Run in a container that holds the reference checkout, named by
+FFTS_REFERENCE_ROOT:
 
     python tests/golden/make_collector_golden.py
 

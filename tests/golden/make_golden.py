@@ -1,7 +1,7 @@
 """Generate the golden block-mask fixtures from the reference implementation.
 
-Run in a container that holds the reference checkout (default
-/root/reference, override with FFTS_REFERENCE_ROOT):
+Run in a container that holds the reference checkout, named by
+FFTS_REFERENCE_ROOT:
 
     python tests/golden/make_golden.py
 
@@ -15,6 +15,11 @@ CPU through oracle/ref_import.py with lowest-index tie-breaking, and stores:
   pooled_sha sha256 of the reference's pooled Q_b / K_b bytes
   input_sha  sha256 of the generated q / k bytes (detects generator drift)
   raw_topk_agrees  whether the mask is unchanged with torch.topk's own tie order
+  pooled_diff  per sequence, how many pooled q / k elements of the reference
+             differ from the canonical pooling (fp32 sum of the block's rows in
+             order, divided by block_size, rounded once; oracle.pool).  torch's
+             CPU mean sums a large tensor in a different order, which moves a
+             rare rounding boundary by one ulp.
 
 Batch-2 cases run the reference once per sequence (it supports batch 1 only,
 my_attn_v7.py:521, :528) and stack the results.
@@ -87,6 +92,11 @@ CASES = {
     # batch of two sequences (seeds 0 and 1)
     "batch2": dict(L=4096 + 100, dtype="bf16", batch=2, kw={**EFF, **keep_ratio(0.1),
                                                              "stripe_threshold": 0.012}),
+    # BASELINE config 3 as bench.py runs it: 128K tokens, 32 / 8 heads, bf16, keep ratio 0.05
+    "cfg3_topk005_128k": dict(L=131072, dtype="bf16", kw={**EFF, **keep_ratio(0.05)}),
+    # BASELINE config 5's attention shape: 2 x 65536 tokens, 28 / 4 heads, block 64, RoPE base 1e6
+    "cfg5_qwen_bs64_2x64k": dict(L=65536, dtype="bf16", bs=64, batch=2, hq=28, hkv=4, rope_base=1e6,
+                                 kw={**EFF, **keep_ratio(0.05)}),
 }
 
 DT = {"fp32": torch.float32, "bf16": torch.bfloat16}
@@ -107,13 +117,18 @@ def pack(mask: np.ndarray) -> np.ndarray:
     return np.packbits(m, axis=-1, bitorder="little").view(np.uint32)
 
 
+def input_kwargs(spec):
+    """make_inputs arguments of a case (head counts and RoPE base default to config 1-3's)."""
+    return dict(dtype=DT[spec["dtype"]], batch=spec.get("batch", 1), num_q_heads=spec.get("hq", 32),
+                num_kv_heads=spec.get("hkv", 8), rope_base=spec.get("rope_base", 500000.0))
+
+
 def case_inputs(spec):
-    B = spec.get("batch", 1)
-    q, k, v = make_inputs(spec["L"], dtype=DT[spec["dtype"]], batch=B)
-    return q, k, v
+    return make_inputs(spec["L"], **input_kwargs(spec))
 
 
 def main(names=None):
+    from oracle import oracle as O
     from oracle.ref_import import reference_intermediates, run_reference
 
     manifest = {}
@@ -123,7 +138,7 @@ def main(names=None):
         bs = spec.get("bs", 128)
         kw = dict(spec["kw"], block_size=bs)
         q, k, v = case_inputs(spec)
-        masks, corrs, sums, psha = [], [], [], []
+        masks, corrs, sums, psha, pdiff = [], [], [], [], []
         raw_agree = True
         for b in range(q.shape[0]):
             qb, kb, vb = q[b:b + 1], k[b:b + 1], v[b:b + 1]
@@ -138,12 +153,18 @@ def main(names=None):
             corrs.append(inter["corr"].numpy())
             sums.append(inter["corr_sum"].numpy())
             psha.append(sha(inter["Qb"]) + ":" + sha(inter["Kb"]))
+            diff = 0
+            for x, ref in ((qb, inter["Qb"]), (kb, inter["Kb"])):
+                canon = O.pool(x, bs)[0].permute(1, 0, 2)  # [N, H, D], the reference's layout
+                diff += int((canon.float() != ref.float()).sum())
+            pdiff.append(diff)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), mask=np.stack(masks),
                             corr=np.stack(corrs).astype(np.float32),
                             corr_sum=np.stack(sums).astype(np.float32))
         manifest[name] = dict(L=spec["L"], dtype=spec["dtype"], block_size=bs,
                               batch=q.shape[0], kwargs=spec["kw"], input_sha=sha(q) + ":" + sha(k),
-                              pooled_sha=psha, raw_topk_agrees=raw_agree,
+                              hq=q.shape[1], hkv=spec.get("hkv", 8), rope_base=spec.get("rope_base", 500000.0),
+                              pooled_sha=psha, pooled_diff=pdiff, raw_topk_agrees=raw_agree,
                               density=float(np.mean([np.unpackbits(mm.view(np.uint8)).mean() for mm in masks])))
         print(name, "N=", (spec["L"] + bs - 1) // bs, "raw topk agrees:", raw_agree, flush=True)
     path = os.path.join(HERE, "manifest.json")

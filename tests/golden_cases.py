@@ -31,12 +31,23 @@ def sha(t: torch.Tensor) -> str:
 def load_case(name: str):
     """(spec, q, k, v, params, fixture arrays) for one golden case."""
     spec = manifest()[name]
-    q, k, v = make_inputs(spec["L"], dtype=DT[spec["dtype"]], batch=spec["batch"])
+    q, k, v = make_inputs(spec["L"], dtype=DT[spec["dtype"]], batch=spec["batch"],
+                          num_q_heads=spec.get("hq", 32), num_kv_heads=spec.get("hkv", 8),
+                          rope_base=spec.get("rope_base", 500000.0))
     kw = dict(spec["kwargs"], block_size=spec["block_size"])
     params = derive_mask_params(spec["L"], **kw)
     fx = np.load(os.path.join(GOLDEN, f"{name}.npz"))
     return spec, q, k, v, params, {key: fx[key] for key in fx.files}
 
 
-def case_names():
-    return sorted(manifest().keys())
+def is_large(spec) -> bool:
+    """The BASELINE config 3 / 5 shaped cases (131072 tokens per case): their
+    inputs take tens of seconds to generate on the CPU, so each test module
+    loads them once."""
+    return spec["L"] * spec["batch"] >= 131072
+
+
+def case_names(large=None):
+    """Golden case names; ``large`` True / False selects the large / small ones."""
+    m = manifest()
+    return sorted(n for n in m if large is None or is_large(m[n]) == large)

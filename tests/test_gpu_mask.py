@@ -90,7 +90,10 @@ def test_block_mask_rejects_bad_workspace(lib):
 
 @pytest.mark.slow
 def test_mask_bit_exact_128k(lib):
-    """BASELINE config 3 shape (L = 131072, 32 heads, bf16), keep ratio 0.05."""
+    """BASELINE config 3 shape (L = 131072, 32 heads, bf16), keep ratio 0.05, against the
+    oracle (lag scores bit-exact), and with a stripe threshold that splits the heads into
+    stripe and diffuse.  The same mask is compared with the reference's own
+    (cfg3_topk005_128k fixture) in test_mask_bit_exact."""
     from oracle.synth import make_inputs
     from fftsparse_b200.params import derive_mask_params
     L = 131072

@@ -122,3 +122,42 @@ def test_wait_flags_times_out_with_status():
     assert int(status.item()) == 5
     x = torch.ones(4, device=dev)
     assert float((x + 1).sum().item()) == 8.0
+
+
+def test_peer_gather_raises_when_a_peer_never_delivers():
+    """PeerGather.run on one GPU (a one-rank group) with a second flag that no
+    peer ever stores: the bounded flag wait ends with status 5, and the next run
+    raises WaitTimeout before launching anything; once the flag set is whole
+    again the calls go on."""
+    import torch.distributed as dist
+
+    import bench
+    import fftsparse_b200 as F
+    from fftsparse_b200.dist import PeerGather, kv_group_shard, local_views
+    from fftsparse_b200.status import WaitTimeout
+    from fftsparse_b200.synthetic import make_inputs
+    F.load_library()
+    dev = torch.device("cuda", 0)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{_free_port()}", rank=0, world_size=1)
+    try:
+        L = 2048
+        q, k, v = make_inputs(L, num_q_heads=8, num_kv_heads=2, dtype=torch.bfloat16, device=str(dev), expand=False)
+        shard = kv_group_shard(8, 2, 1, 0)
+        ql, kl, vl = local_views(q, k, v, shard)
+        mask = F.fft_block_mask(ql, kl, **bench.mask_kwargs(0.1))
+        pg = PeerGather(8, L, 128, device=dev)
+        ref = pg.run(ql, kl, vl, mask.bits, 128, True, shard).clone()
+        pg.check()
+        own_flags, pg.flags, pg.world = pg.flags, torch.zeros(2, dtype=torch.int32, device=dev), 2
+        pg.run(ql, kl, vl, mask.bits, 128, True, shard)  # waits ~2 s for flag 1, then gives up
+        torch.cuda.synchronize(dev)
+        with pytest.raises(WaitTimeout) as exc:
+            pg.run(ql, kl, vl, mask.bits, 128, True, shard)
+        assert exc.value.code == 5
+        pg.flags, pg.world = own_flags, 1
+        got = pg.run(ql, kl, vl, mask.bits, 128, True, shard)
+        pg.check()
+        assert torch.equal(got, ref)
+        pg.close()
+    finally:
+        dist.destroy_process_group()

@@ -11,7 +11,8 @@ import torch
 from oracle import oracle as O
 from tests.golden_cases import case_names, load_case, sha
 
-CASES = case_names()
+CASES = case_names(large=False)
+LARGE = case_names(large=True)
 
 
 @pytest.mark.parametrize("name", CASES)
@@ -46,6 +47,26 @@ def test_oracle_corr_within_tolerance(name):
     ref_sum = torch.from_numpy(fx["corr_sum"])
     scale = max(1.0, float(ref_sum.abs().max()))
     assert float((out["corr_sum"] - ref_sum).abs().max()) <= 1e-4 * scale
+
+
+@pytest.mark.parametrize("name", LARGE)
+def test_large_case_against_reference(name):
+    """BASELINE config 3 (128K tokens, 32 / 8 heads, keep ratio 0.05) and config 5's
+    attention shape (2 x 65536, 28 / 4 heads, block 64): the oracle's mask equals
+    the reference's bit for bit and its lag scores are within 1e-4.  The pooled
+    bytes are not compared here: at this size torch's CPU mean sums in another
+    order, which the generator measured as a one-ulp change in a handful of the
+    millions of pooled elements (manifest ``pooled_diff``); the masks agree anyway."""
+    spec, q, k, v, params, fx = load_case(name)
+    assert sha(q) + ":" + sha(k) == spec["input_sha"], "synthetic generator drifted"
+    assert sum(spec["pooled_diff"]) <= 16
+    out = O.prefill_mask(q, k, params)
+    got = O.as_numpy_bits(out["bits"])
+    assert got.shape == fx["mask"].shape
+    mismatched_rows = int((got != fx["mask"]).any(-1).sum())
+    assert mismatched_rows == 0, f"{mismatched_rows} rows differ from the reference mask"
+    ref = torch.from_numpy(fx["corr"])
+    assert float((out["corr"] - ref).abs().max()) <= 1e-4 * max(1.0, float(ref.abs().max()))
 
 
 @pytest.mark.parametrize("name", [n for n in CASES if n.endswith(("topk", "8k", "16k"))])

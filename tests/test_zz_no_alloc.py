@@ -17,6 +17,7 @@ import ctypes
 import pytest
 import torch
 
+from oracle import oracle as O
 from tests.golden_cases import load_case
 
 pytestmark = pytest.mark.gpu
@@ -82,6 +83,32 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(F):
     _run_both(F, "cfg2_topk")
     # second call, different shape and diffuse heads, over the scratch left by the first
     _run_both(F, "mixed_16k")
+
+
+def test_noalloc_call_allocates_nothing(F):
+    """After a first call (which loads the library's code and scratch onto the
+    device), a call takes no device memory: neither torch's allocator nor the
+    device's free total moves."""
+    from fftsparse_b200 import _lib
+    lib = _lib.load()
+    spec, q, k, v, params, fx = load_case("mixed_16k")
+    dev = torch.device("cuda")
+    qb = F.pool_blocks(q.to(dev), params.block_size)
+    kb = F.pool_blocks(k.to(dev), params.block_size)
+    B, H, N, D = qb.shape
+    cp = params.to_c()
+    stream = torch.cuda.current_stream().cuda_stream
+    out = _outputs(B, H, N, dev)
+    args = (qb.data_ptr(), kb.data_ptr(), 1, B, H, kb.shape[1], D, ctypes.addressof(cp), *_ptrs(out), stream)
+    assert lib.ffts_block_mask_noalloc(*args) == 0, lib.ffts_last_error_string()
+    torch.cuda.synchronize()
+    torch_bytes = torch.cuda.memory_allocated(dev)
+    free_before = torch.cuda.mem_get_info(dev)[0]
+    assert lib.ffts_block_mask_noalloc(*args) == 0, lib.ffts_last_error_string()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated(dev) == torch_bytes
+    assert torch.cuda.mem_get_info(dev)[0] == free_before, "ffts_block_mask_noalloc allocated device memory"
+    assert (O.as_numpy_bits(out["bits"].cpu()) == fx["mask"]).all()
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(F):

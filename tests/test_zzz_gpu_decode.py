@@ -45,3 +45,32 @@ def test_decode_over_a_cache_slice_and_q_len_one():
     got = F.decode_attention(q, kc[:, :, :Lk], vc[:, :, :Lk])
     ref = reference(q[:, :, 0], kc[:, :, :Lk], vc[:, :, :Lk])
     assert float((got.float() - ref).abs().max()) <= 2e-2
+
+
+@pytest.mark.parametrize("mask_dtype", [torch.bfloat16, torch.float32])
+def test_decode_with_padding_mask(mask_dtype):
+    """A left-padded batch of two: HF's 4-D additive mask [B, 1, 1, kv_len] (0 for
+    real keys, the dtype's minimum for padding, one spare column past Lk) is added
+    to the scaled scores before the softmax, as the caller's decode branch adds
+    attention_mask (eval/LongBench/pred.py:311-313)."""
+    import fftsparse_b200 as F
+    g = torch.Generator().manual_seed(11)
+    B, H, Hkv, Lk = 2, 8, 2, 3000
+    q = (torch.randn(B, H, 128, generator=g) * 2).bfloat16().cuda()
+    k = torch.randn(B, Hkv, Lk, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(B, Hkv, Lk, 128, generator=g).bfloat16().cuda()
+    pad = [0, 700]  # sequence 1 has 700 padding tokens on the left
+    mask = torch.zeros(B, 1, 1, Lk + 1, dtype=mask_dtype)
+    for b, p in enumerate(pad):
+        mask[b, 0, 0, :p] = torch.finfo(mask_dtype).min
+    mask = mask.cuda()
+    got = F.decode_attention(q, k, v, attention_mask=mask)
+    D = q.shape[2]
+    qg = q.float().view(B, Hkv, H // Hkv, D)
+    s = torch.einsum("bkgd,bkld->bkgl", qg, k.float()) / D ** 0.5 + mask[:, :, :, :Lk].float()
+    ref = torch.einsum("bkgl,bkld->bkgd", s.softmax(-1), v.float()).reshape(B, H, D)
+    err = (got.float() - ref).abs()
+    assert float(err.max()) <= 2e-2 and float(err.mean()) <= 1e-3, (float(err.max()), float(err.mean()))
+    # the padded keys really are excluded: the same as attending the unpadded keys only
+    alone = F.decode_attention(q[1:], k[1:, :, pad[1]:].contiguous(), v[1:, :, pad[1]:].contiguous())
+    assert float((got[1:].float() - alone.float()).abs().max()) <= 2e-2
