@@ -36,6 +36,8 @@ EXPORTS = {
     "ffts_block_mask_noalloc": (_I32, [_P, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P,
                                        _P]),
     "ffts_unpack_mask": (_I32, [_P, _I64, _I64, _I64, _P, _P]),
+    "ffts_mask_row_ptr": (_I32, [_P, _I64, _P, _P]),
+    "ffts_mask_col_idx": (_I32, [_P, _I64, _I64, _P, _P, _I64, _P, _P]),
     "ffts_rope_pool": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32,
                               _P, _P, _P, _P, _P, _P]),
     "ffts_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64]),

@@ -102,6 +102,9 @@ int block_mask(const void *qb, const void *kb, int dtype, int64_t B, int64_t H, 
                float *csum, uint8_t *is_stripe, float *svar, void *workspace, int64_t ws_bytes,
                cudaStream_t stream);
 int unpack_mask(const uint32_t *bits, int64_t B, int64_t H, int64_t N, uint8_t *out, cudaStream_t stream);
+int mask_row_ptr(const int32_t *row_count, int64_t rows, int64_t *row_ptr, cudaStream_t stream);
+int mask_col_idx(const uint32_t *bits, int64_t rows, int64_t N, const int64_t *row_ptr, int32_t *col_idx,
+                 int64_t capacity, int32_t *status, cudaStream_t stream);
 int ensure_tables();
 int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,
                     int64_t L, int64_t D, const int64_t *qs, const int64_t *ks, const int64_t *vs,
@@ -201,6 +204,21 @@ int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_
                          void *stream) {
   g_last_error.clear();
   return unpack_mask(mask_bits, B, H, N, out, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_mask_row_ptr(const int32_t *row_count, int64_t rows, int64_t *row_ptr, void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return mask_row_ptr(row_count, rows, row_ptr, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_mask_col_idx(const uint32_t *mask_bits, int64_t rows, int64_t N, const int64_t *row_ptr,
+                          int32_t *col_idx, int64_t capacity, int32_t *status, void *stream) {
+  g_last_error.clear();
+  int rc = check_device();
+  if (rc) return rc;
+  return mask_col_idx(mask_bits, rows, N, row_ptr, col_idx, capacity, status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int64_t H, int64_t Hkv,

@@ -163,12 +163,24 @@ class BlockMask:
         return out.view(torch.bool)
 
     def csr(self):
-        """(row_ptr int64 [B*H*N+1], col_idx int32 [nnz]) with ascending columns per row."""
-        dense = self.dense().reshape(-1, self.n_blocks)
-        row_ptr = torch.zeros(dense.shape[0] + 1, dtype=torch.int64, device=dense.device)
-        row_ptr[1:] = torch.cumsum(self.row_count.reshape(-1).to(torch.int64), 0)
-        col_idx = dense.nonzero()[:, 1].to(torch.int32)
-        return row_ptr, col_idx
+        """(row_ptr int64 [B*H*N+1], col_idx int32 [nnz]): the kept key blocks of
+        each query block in ascending order, rows in [B, H, N] order, built on the
+        device from the packed bits (ffts_mask_row_ptr, ffts_mask_col_idx).  Reads
+        the total count back once to size col_idx."""
+        lib = _lib.load()
+        dev = self.bits.device
+        B, H, N, _ = self.bits.shape
+        rows = B * H * N
+        row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+        _lib.check(lib.ffts_mask_row_ptr(self.row_count.data_ptr(), rows, row_ptr.data_ptr(), _stream_ptr(dev)))
+        nnz = int(row_ptr[-1].item())
+        col_idx = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        _lib.check(lib.ffts_mask_col_idx(self.bits.data_ptr(), rows, N, row_ptr.data_ptr(), col_idx.data_ptr(), nnz,
+                                         status.data_ptr(), _stream_ptr(dev)))
+        if int(status.item()) != 0:
+            raise RuntimeError("block mask rows and row counts disagree (row_count does not match the bits)")
+        return row_ptr, col_idx[:nnz]
 
     def density(self) -> float:
         """Kept fraction of the causal block pairs."""

@@ -216,6 +216,24 @@ FFTS_API int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t 
                          uint8_t *out, void *stream);
 
 /*
+ * The selected blocks as a CSR index list, the block index list a block-sparse
+ * kernel that takes indices consumes (the reference passes the bool form,
+ * base_blockmask, my_attn_v7.py:780).  rows = B * H * N, in the [B, H, N]
+ * order of the packed bits.
+ *   ffts_mask_row_ptr: row_ptr[i] = sum of row_count[0..i) (int64, rows + 1
+ *     entries; row_ptr[rows] = number of kept blocks), from the row_count that
+ *     ffts_block_mask writes.
+ *   ffts_mask_col_idx: col_idx[row_ptr[i] .. row_ptr[i+1]) = the kept key
+ *     blocks of row i in ascending order (int32).  capacity = entries col_idx
+ *     holds.  A row whose popcount differs from its row_ptr span, or that would
+ *     end past capacity, is not written and *status (int32, device) is set to 1.
+ */
+FFTS_API int32_t ffts_mask_row_ptr(const int32_t *row_count, int64_t rows, int64_t *row_ptr, void *stream);
+FFTS_API int32_t ffts_mask_col_idx(const uint32_t *mask_bits, int64_t rows, int64_t N,
+                                   const int64_t *row_ptr, int32_t *col_idx, int64_t capacity,
+                                   int32_t *status, void *stream);
+
+/*
  * Block-sparse causal attention forward (bf16 in, fp32 accumulate, bf16 out).
  * Replaces block_sparse_attn_func (my_attn_v7.py:775-786; package
  * block_sparse_attn 0.0.2) with head_mask_type all 1 (:772), p_dropout 0,

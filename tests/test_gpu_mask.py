@@ -135,3 +135,27 @@ def test_mask_bit_exact_n2048(lib):
     m2 = lib.fft_block_mask(q.cuda(), k.cuda(), params=params2)
     assert 0 < int(ref2["is_stripe"].sum()) < 4
     assert torch.equal(m2.bits.cpu(), ref2["bits"])
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_csr_equals_dense_mask(lib, name):
+    """The device-built CSR list (ffts_mask_row_ptr / ffts_mask_col_idx) equals the
+    row-major nonzeros of the reference's bool block mask, ascending per row."""
+    spec, q, k, v, params, fx = load_case(name)
+    m = lib.fft_block_mask(q.cuda(), k.cuda(), params=params)
+    row_ptr, col_idx = m.csr()
+    N = params.n_blocks
+    dense = O.unpack_bits(torch.from_numpy(fx["mask"].view("int32")), N).reshape(-1, N)
+    nz = dense.nonzero()
+    want_ptr = torch.zeros(dense.shape[0] + 1, dtype=torch.int64)
+    want_ptr[1:] = torch.cumsum(dense.sum(1), 0)
+    assert torch.equal(row_ptr.cpu(), want_ptr)
+    assert torch.equal(col_idx.cpu().long(), nz[:, 1])
+
+
+def test_csr_rejects_inconsistent_counts(lib):
+    spec, q, k, v, params, fx = load_case("n10")
+    m = lib.fft_block_mask(q.cuda(), k.cuda(), params=params)
+    m.row_count[0, 0, 3] += 1  # no longer the popcount of its row
+    with pytest.raises(RuntimeError):
+        m.csr()
