@@ -75,6 +75,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-ttft", action="store_true")
+    ap.add_argument("--no-caller-kernels", action="store_true", help="skip the rope_pool / decode bandwidth fields")
     ap.add_argument("--ttft-layers", type=int, default=0, help="0: the config's own layer count")
     ap.add_argument("--ttft-config", type=int, choices=[4, 5], default=4,
                     help="BASELINE config of the TTFT decoder (4: Llama-3.1-8B shape, 1 x seq-len tokens; "
@@ -193,6 +194,81 @@ def causal_pairs(bits: torch.Tensor, L: int, bs: int) -> int:
     return int(full + corr)
 
 
+def kernel_times_us(fn, reps: int = 3) -> dict:
+    """Average device time per call of each kernel ``fn`` launches, in µs, from the
+    CUDA activity trace of ``reps`` calls (torch.profiler / CUPTI); keys are the
+    kernels' short names."""
+    from torch.profiler import ProfilerActivity, profile
+    fn()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    out = {}
+    for ev in prof.key_averages():
+        if ev.device_type is None or str(ev.device_type).endswith("CPU"):
+            continue
+        name = ev.key.split("(")[0].split("<")[0].split("::")[-1]
+        us = getattr(ev, "device_time_total", None)
+        if us is None:
+            us = getattr(ev, "cuda_time_total", 0.0)
+        if us:
+            out[name] = out.get(name, 0.0) + us / reps
+    return {k: round(v, 2) for k, v in out.items()}
+
+
+def caller_side_kernels(dev, L: int, hbm_peak: float, reps: int = 5) -> dict:
+    """Achieved HBM bandwidth of the two caller-side kernels at BASELINE config 4's
+    shape: rope_pool on one layer's QKV projection (32 q / 8 KV heads of 128, L
+    tokens) and one decode step over an L-token cache of 8 KV heads.  Algorithmic
+    bytes: rope_pool reads the projection (L x 6144 bf16) and cos / sin, writes q,
+    k, v head-major and the pooled q / k blocks; decode reads the K and V caches
+    once (2 x L x 8 x 128 x 2 bytes)."""
+    import fftsparse_b200 as F
+    g = torch.Generator(device=dev).manual_seed(0)
+    H, HKV_, D = HQ, HKV, HEAD_DIM
+    qkv = torch.randn(L, (H + 2 * HKV_) * D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, D, 2, device=dev, dtype=torch.float64) / D))
+    fr = torch.arange(L, device=dev, dtype=torch.float64)[:, None] * inv[None]
+    emb = torch.cat([fr, fr], -1)
+    cos, sin = emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+    del fr, emb
+
+    def rp():
+        return F.rope_pool(qkv[:, :H * D], qkv[:, H * D:(H + HKV_) * D], qkv[:, (H + HKV_) * D:], H, HKV_, cos, sin,
+                           BLOCK)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / reps
+
+    t_rp = timed(rp)
+    N = (L + BLOCK - 1) // BLOCK
+    rp_bytes = 2 * L * (H + 2 * HKV_) * D * 2 + 2 * L * D * 2 + N * (H + HKV_) * D * 2
+    del qkv
+    kc = torch.randn(1, HKV_, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    vc = torch.randn(1, HKV_, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    qd = torch.randn(1, H, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    t_dec = timed(lambda: F.decode_attention(qd, kc, vc))
+    dec_bytes = 2 * L * HKV_ * D * 2
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"rope_pool": {"ms": round(t_rp, 4), "bytes": rp_bytes, "gbs": round(rp_bytes / (t_rp * 1e-3) / 1e9, 1),
+                          "frac_hbm": round(rp_bytes / (t_rp * 1e-3) / 1e9 / hbm_peak, 4),
+                          "shape": f"L={L}, projection [L, {(H + 2 * HKV_) * D}] bf16, block {BLOCK}"},
+            "decode": {"ms": round(t_dec, 4), "bytes": dec_bytes, "gbs": round(dec_bytes / (t_dec * 1e-3) / 1e9, 1),
+                       "frac_hbm": round(dec_bytes / (t_dec * 1e-3) / 1e9 / hbm_peak, 4),
+                       "shape": f"one token, {H} q / {HKV_} KV heads, Lk={L}"}}
+
+
 # ----------------------------------------------------------- CPU baseline
 def cpu_baseline_sample(q, k, v, keep_ratio, row_stride=16):
     """Oracle port on the host cores: full-size mask selection for all heads
@@ -223,32 +299,48 @@ def cpu_baseline_sample(q, k, v, keep_ratio, row_stride=16):
 
 
 def run_reference(args):
-    """--impl reference: the CPU path on the host cores (rank 0 only)."""
+    """--impl reference: the CPU path on the host cores (rank 0 only).
+
+    Each step runs a bounded sample of the layer on the host cores and the
+    line's value is the measured time of that sample per step: the full mask
+    selection for all heads (the C oracle, OpenMP) plus fp32 block-sparse
+    attention for head 0 on every 16th query block.  The time the whole layer
+    would take on the CPU, scaled from the sample by kept (query, key) blocks,
+    is reported beside it as ``extrapolated_ms_per_layer``."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from fftsparse_b200.synthetic import make_inputs
     q, k, v = make_inputs(args.seq_len, num_q_heads=HQ, num_kv_heads=HKV, dtype=torch.bfloat16)
-    times, info = [], {}
+    times, extrap, info = [], [], {}
     for i in range(args.warmup + args.steps):
-        ms, info = cpu_baseline_sample(q, k, v, args.keep_ratio)
+        t0 = time.perf_counter()
+        ms_layer, info = cpu_baseline_sample(q, k, v, args.keep_ratio)
+        step_ms = (time.perf_counter() - t0) * 1e3
         if i >= args.warmup:
-            times.append(ms)
+            times.append(step_ms)
+            extrap.append(ms_layer)
     value = sum(times) / len(times)
-    sample = (f"per step: full {args.seq_len}-token mask selection for all {HQ} heads (C oracle, OpenMP) + fp32 "
-              f"attention for head 0 on {info['rows_sampled']} evenly spaced query blocks, scaled by kept blocks "
-              f"(x{info['attn_scale']:.1f})")
+    sample = (f"per step, measured: the full {args.seq_len}-token mask selection for all {HQ} heads (C oracle, "
+              f"{info['threads']} OpenMP threads) plus fp32 block-sparse attention for head 0 on "
+              f"{info['rows_sampled']} evenly spaced query blocks of {args.seq_len // BLOCK}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value, 3),
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": f"cfg3: L={args.seq_len}, Hq={HQ}, Hkv={HKV} (expanded), D={HEAD_DIM}, "
-                               f"block {BLOCK}, keep ratio {args.keep_ratio}", "seq_len": args.seq_len,
+                               f"block {BLOCK}, keep ratio {args.keep_ratio}; CPU sample of the layer (see "
+                               f"cpu_baseline.sample)", "seq_len": args.seq_len,
                    "global_batch": 1, "parallelism": "host cores"},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": info.get("threads"),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "extrapolated_ms_per_layer": round(sum(extrap) / len(extrap), 1),
+        "extrapolation": {"mask_s": round(info["mask_s"], 4), "attn_sample_s": round(info["attn_sample_s"], 4),
+                          "attn_scale": round(info["attn_scale"], 2),
+                          "how": "mask time + attention sample time x (kept blocks of all heads / kept blocks "
+                                 "of the sampled query blocks of head 0)"},
         "detail": info,
     }
     emit(line)
@@ -565,9 +657,14 @@ def run_ours(args):
                 "algorithmic_flops_per_launch": flops, "launch_ms": round(t_attn, 4),
                 "causal_pair_density": pairs / (shard.heads * L * (L + 1) / 2)}
     pool_bytes = (ql.numel() + kl.numel()) * 2 + mask.q_pooled.numel() * 2 + mask.k_pooled.numel() * 2
+    try:
+        sel_kernels = kernel_times_us(lambda: F.fft_block_mask(ql, kl, pooled=(mask.q_pooled, mask.k_pooled), **kw))
+    except Exception as exc:  # noqa: BLE001 - the activity trace is a report, not a requirement
+        sel_kernels = {"error": f"{exc}"[:200]}
     stages = {"pool_ms": round(t_pool, 4), "pool_gbs": round(pool_bytes / (t_pool * 1e-3) / 1e9, 1),
               "pool_frac_hbm": round(pool_bytes / (t_pool * 1e-3) / 1e9 / hbm_peak, 4),
-              "select_ms": round(t_mask - t_pool, 4), "attention_ms": round(t_attn, 4),
+              "select_ms": round(t_mask - t_pool, 4), "select_kernels_us": sel_kernels,
+              "attention_ms": round(t_attn, 4),
               "block_density": round(mask.density(), 5),
               "stripe_heads": int(mask.is_stripe.sum().item())}
 
@@ -601,6 +698,14 @@ def run_ours(args):
                            "block_density": round(F.fft_block_mask(ql, kl, **kwr).density(), 5)}
         except Exception as exc:  # noqa: BLE001
             sweep[name] = {"error": f"{exc}"[:200]}
+
+    # ---- the caller-side kernels (rope_pool, decode) against the HBM copy peak
+    caller = None
+    if not args.no_caller_kernels:
+        try:
+            caller = caller_side_kernels(dev, L, hbm_peak)
+        except Exception as exc:  # noqa: BLE001 - reported in the field instead of ending the run
+            caller = {"error": f"{exc}"[:200]}
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -691,6 +796,7 @@ def run_ours(args):
                                                 "captured Llama-3.1-8B Q/K; here synthetic inputs, so block "
                                                 "densities differ)"),
             "ttft": ttft,
+            "caller_kernels": caller,
         }
         emit(line)
     if world > 1:
