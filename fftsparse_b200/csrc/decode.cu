@@ -6,14 +6,17 @@
 // layout ffts_rope_pool writes and an HF cache stores), once per KV head for
 // all G q-heads of its group: HBM-bound at 2 * B * Hkv * Lk * D * 2 bytes.
 //
-// decode_split_kernel: CTA = (b, kv head, split of the keys); 128 threads.  The
-// split's keys are walked in chunks of 128:
-//   scores   thread = key; 16-byte loads of the key's row; q of the G heads in
-//            shared memory (broadcast reads); fp32 dot products, in log2 units;
-//   softmax  warp w handles heads w, w + 4, ...: chunk max, running max m and
-//            sum l, the chunk's exponentials in place;
-//   P V      thread = output dimension; V rows read coalesced; G accumulators,
-//            rescaled when the running max moves.
+// decode_split_kernel: CTA = (b, kv head, split of the keys, up to 8 q-heads
+// of the group); 256 threads.  The split's keys are walked in chunks of 64:
+//   scores   a half-warp per key row, 16-byte loads (lane = 8 channels), so each
+//            warp instruction reads two whole rows; q of the heads in
+//            registers; fp32 dot products reduced over the 16 lanes, in log2
+//            units;
+//   softmax  warp w handles head w: chunk max, running max m and sum l, the
+//            chunk's exponentials in place;
+//   P V      the same row split over V; each lane accumulates its 8 channels for
+//            every head, rescaled when the running max moves; the row slots
+//            are summed once at the end of the split.
 // An optional additive bias per (sequence, key) -- the caller's attention mask,
 // added to the scaled scores before the softmax as at pred.py:311-313 -- is
 // read once per key with the key's scores.  Fully masked chunks contribute
@@ -22,7 +25,9 @@
 // decode_merge_kernel: CTA = (b, q head): o = sum_s 2^(m_s - M) o_s /
 // sum_s 2^(m_s - M) l_s, rounded to bf16.
 // No waits; every __syncthreads is reached by the whole CTA; every index is
-// bounded by Lk, G <= 16 and D = 128.
+// bounded by Lk, G <= 16 (in blocks of 8 heads per CTA) and D = 128.
+
+#include <algorithm>
 
 #include "ffts_common.cuh"
 
@@ -31,7 +36,6 @@ namespace decode {
 
 constexpr int kD = 128;
 constexpr int kThreads = 128;
-constexpr int kChunk = 128;  // one key per thread in the score phase
 constexpr int kMaxG = 16;
 
 struct Params {
@@ -56,76 +60,113 @@ __device__ __forceinline__ float bias_log2(const Params &p, int b, int key) {
   return x * 1.4426950408889634f;  // scores are kept in log2 units
 }
 
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_constant__ Params p) {
-  __shared__ float q_s[kMaxG][kD];
-  __shared__ float s_s[kMaxG][kChunk];
-  __shared__ float m_s[kMaxG], l_s[kMaxG], a_s[kMaxG];
+constexpr int kSplitThreads = 256;  // 8 warps
+constexpr int kRows = 64;           // keys per chunk: 8 per warp, two per warp instruction
+constexpr int kHeadsPerCta = 8;     // q-heads of one group per CTA (groups of up to 16 take two CTAs)
+
+__device__ __forceinline__ void widen8(const uint4 &raw, float *f) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+// CTA = (b, kv head, split of the keys, block of up to 8 q-heads of the group);
+// 256 threads.  Each half-warp reads one key row with 16-byte loads (lane =
+// 8-channel segment), so a warp instruction moves two whole 256-byte rows and a
+// chunk of 64 rows is in flight per CTA; the G dot products of a row are
+// reduced over the 16 lanes by shuffles.  Softmax per chunk as before (warp w
+// handles head w); P V: each lane accumulates its 8 channels over its rows for
+// every head, and the 16 row slots are summed once at the end of the split.
+template <int GM>
+__global__ void __launch_bounds__(kSplitThreads) decode_split_kernel(const __grid_constant__ Params p) {
+  __shared__ float s_s[GM][kRows];
+  __shared__ float m_s[GM], l_s[GM], a_s[GM];
+  __shared__ float red[kSplitThreads / 32][GM][kD];
   const int G = p.H / p.Hkv;
   const int bh = blockIdx.x;  // b * Hkv + kv head
   const int b = bh / p.Hkv, kvh = bh % p.Hkv;
   const int split = blockIdx.y;
-  const int t = threadIdx.x;
+  const int g0 = blockIdx.z * kHeadsPerCta;
+  const int ng = min(GM, G - g0);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int half = lane >> 4, seg = lane & 15;
   const int k0 = split * p.per_split;
   const int k1 = min(p.Lk, k0 + p.per_split);
-  for (int i = t; i < G * kD; i += kThreads) {
-    const int g = i / kD, d = i % kD;
-    q_s[g][d] = __bfloat162float(p.q[int64_t(b) * p.qs_b + int64_t(kvh * G + g) * p.qs_h + d]);
-  }
-  if (t < G) {
-    m_s[t] = -INFINITY;
-    l_s[t] = 0.0f;
-  }
-  float acc[kMaxG];
+  // q of this CTA's heads for the lane's 8 channels, pre-multiplied by scale * log2(e)
+  float qr[GM][8];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) acc[g] = 0.0f;
-  const __nv_bfloat16 *kb = p.k + int64_t(b) * p.ks_b + int64_t(kvh) * p.ks_h;
-  const __nv_bfloat16 *vb = p.v + int64_t(b) * p.vs_b + int64_t(kvh) * p.vs_h;
+  for (int g = 0; g < GM; ++g) {
+    if (g < ng) {
+      const uint4 raw = *reinterpret_cast<const uint4 *>(p.q + int64_t(b) * p.qs_b +
+                                                         int64_t(kvh * G + g0 + g) * p.qs_h + seg * 8);
+      widen8(raw, qr[g]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[g][e] *= p.scale_log2;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[g][e] = 0.0f;
+    }
+  }
+  if (tid < GM) {
+    m_s[tid] = -INFINITY;
+    l_s[tid] = 0.0f;
+  }
+  float acc[GM][8];
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+  const __nv_bfloat16 *kb = p.k + int64_t(b) * p.ks_b + int64_t(kvh) * p.ks_h + seg * 8;
+  const __nv_bfloat16 *vb = p.v + int64_t(b) * p.vs_b + int64_t(kvh) * p.vs_h + seg * 8;
   __syncthreads();
-  for (int c0 = k0; c0 < k1; c0 += kChunk) {
-    const int n = min(kChunk, k1 - c0);
-    if (t < n) {
-      const __nv_bfloat16 *row = kb + int64_t(c0 + t) * p.ks_l;
-      float dot[kMaxG];
+  for (int c0 = k0; c0 < k1; c0 += kRows) {
+    const int n = min(kRows, k1 - c0);
+    // rows warp * 8 + 2 * it + half of the chunk: K and V loads issued together
+    uint4 kv[4], vv[4];
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) dot[g] = 0.0f;
-#pragma unroll 4
-      for (int d0 = 0; d0 < kD; d0 += 8) {
-        const uint4 raw = *reinterpret_cast<const uint4 *>(row + d0);
-        const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
-        float kf[8];
+    for (int it = 0; it < 4; ++it) {
+      const int row = warp * 8 + 2 * it + half;
+      kv[it] = row < n ? *reinterpret_cast<const uint4 *>(kb + int64_t(c0 + row) * p.ks_l) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(h2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
+    for (int it = 0; it < 4; ++it) {
+      const int row = warp * 8 + 2 * it + half;
+      vv[it] = row < n ? *reinterpret_cast<const uint4 *>(vb + int64_t(c0 + row) * p.vs_l) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-          if (g < G) {
+    for (int it = 0; it < 4; ++it) {
+      const int row = warp * 8 + 2 * it + half;
+      float kf[8];
+      widen8(kv[it], kf);
+      const float bl = (seg == 0 && row < n) ? bias_log2(p, b, c0 + row) : 0.0f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) dot[g] = fmaf(q_s[g][d0 + e], kf[e], dot[g]);
-          }
-        }
+      for (int g = 0; g < GM; ++g) {
+        float part = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part = fmaf(qr[g][e], kf[e], part);
+#pragma unroll
+        for (int o = 8; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (seg == 0 && row < n) s_s[g][row] = part + bl;
       }
-      const float bl = bias_log2(p, b, c0 + t);
-#pragma unroll
-      for (int g = 0; g < kMaxG; ++g)
-        if (g < G) s_s[g][t] = fmaf(dot[g], p.scale_log2, bl);
     }
     __syncthreads();
-    const int warp = t >> 5, lane = t & 31;
-    for (int g = warp; g < G; g += kThreads / 32) {
-      float mx = -INFINITY;
-      for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s_s[g][i]);
+    // softmax of the chunk: warp w handles head w
+    if (warp < ng) {
+      const int g = warp;
+      const float x = lane < n ? s_s[g][lane] : -INFINITY;
+      const float y = lane + 32 < n ? s_s[g][lane + 32] : -INFINITY;
+      float mx = fmaxf(x, y);
       for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_old = m_s[g];
       const float m_new = fmaxf(m_old, mx);
-      float sum = 0.0f;
-      for (int i = lane; i < n; i += 32) {
-        const float e = m_new == -INFINITY ? 0.0f : exp2f(s_s[g][i] - m_new);
-        s_s[g][i] = e;
-        sum += e;
-      }
+      const float ex = m_new == -INFINITY ? 0.0f : exp2f(x - m_new);
+      const float ey = m_new == -INFINITY ? 0.0f : exp2f(y - m_new);
+      s_s[g][lane] = ex;
+      s_s[g][lane + 32] = ey;
+      float sum = ex + ey;
       for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       if (lane == 0) {
         const float alpha = m_old == -INFINITY ? 0.0f : exp2f(m_old - m_new);
@@ -135,24 +176,50 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
       }
     }
     __syncthreads();
+    // P V over the same rows
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g)
-      if (g < G) acc[g] *= a_s[g];
-    for (int i = 0; i < n; ++i) {
-      const float vv = __bfloat162float(vb[int64_t(c0 + i) * p.vs_l + t]);
+    for (int g = 0; g < GM; ++g) {
+      const float alpha = g < ng ? a_s[g] : 1.0f;
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g)
-        if (g < G) acc[g] = fmaf(s_s[g][i], vv, acc[g]);
+      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
     }
-    __syncthreads();
-  }
-  float *w = p.ws + (int64_t(bh) * p.splits + split) * G * (kD + 2);
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g)
-    if (g < G) w[g * (kD + 2) + t] = acc[g];
-  if (t < G) {
-    w[t * (kD + 2) + kD] = m_s[t];
-    w[t * (kD + 2) + kD + 1] = l_s[t];
+    for (int it = 0; it < 4; ++it) {
+      const int row = warp * 8 + 2 * it + half;
+      float vf[8];
+      widen8(vv[it], vf);
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        const float pr = (g < ng && row < n) ? s_s[g][row] : 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr, vf[e], acc[g][e]);
+      }
+    }
+    __syncthreads();  // s_s is rewritten by the next chunk
+  }
+  // sum the 16 row slots: the two halves of each warp, then the 8 warps
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], 16);
+  if (half == 0) {
+#pragma unroll
+    for (int g = 0; g < GM; ++g)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) red[warp][g][seg * 8 + e] = acc[g][e];
+  }
+  __syncthreads();
+  float *w = p.ws + (int64_t(bh) * p.splits + split) * G * (kD + 2);
+  for (int idx = tid; idx < ng * kD; idx += kSplitThreads) {
+    const int g = idx / kD, d = idx % kD;
+    float o = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < kSplitThreads / 32; ++ww) o += red[ww][g][d];
+    w[(g0 + g) * (kD + 2) + d] = o;
+  }
+  if (tid < ng) {
+    w[(g0 + tid) * (kD + 2) + kD] = m_s[tid];
+    w[(g0 + tid) * (kD + 2) + kD + 1] = l_s[tid];
   }
 }
 
@@ -196,11 +263,12 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
                "decode: bad shape (B %lld, H %lld, Hkv %lld, Lk %lld, splits %lld; at most %d q-heads per KV head)",
                (long long)B, (long long)H, (long long)Hkv, (long long)Lk, (long long)splits, kMaxG);
   FFTS_REQUIRE(Lk < (int64_t(1) << 31) && B * Hkv <= 0x7fffffff && B * H <= 0x7fffffff, "decode: shape too large");
-  FFTS_REQUIRE(ks[2] % 8 == 0 && ks[2] >= D && vs[2] >= D,
-               "decode: cache row strides must be at least D (the key cache's a multiple of 8 elements)");
+  FFTS_REQUIRE(ks[2] >= D && vs[2] >= D && ks[0] % 8 == 0 && ks[1] % 8 == 0 && ks[2] % 8 == 0 &&
+                   vs[0] % 8 == 0 && vs[1] % 8 == 0 && vs[2] % 8 == 0 && qs_b % 8 == 0 && qs_h % 8 == 0,
+               "decode: q and cache strides must be multiples of 8 elements (16 bytes), cache rows at least D");
   FFTS_REQUIRE((reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
-                   ks[0] % 8 == 0 && ks[1] % 8 == 0,
-               "decode: the key cache must be 16-byte aligned");
+                   (reinterpret_cast<uintptr_t>(q) & 15) == 0,
+               "decode: q and the caches must be 16-byte aligned");
   const int64_t per = ceil_div(Lk, splits);
   const int64_t nsplit = ceil_div(Lk, per);  // every split non-empty
   FFTS_REQUIRE(nsplit <= 65535, "decode: too many splits");
@@ -232,7 +300,17 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   p.bias = bias;
   p.bias_bf16 = bias_dtype == FFTS_DTYPE_BF16 ? 1 : 0;
   p.bias_sb = bias_sb;
-  decode_split_kernel<<<dim3(unsigned(B * Hkv), unsigned(nsplit)), kThreads, 0, stream>>>(p);
+  const int G = int(H / Hkv);
+  const dim3 grid(unsigned(B * Hkv), unsigned(nsplit), unsigned(ceil_div(int64_t(G), int64_t(kHeadsPerCta))));
+  const int gm = std::min(G, kHeadsPerCta);
+  if (gm <= 1)
+    decode_split_kernel<1><<<grid, kSplitThreads, 0, stream>>>(p);
+  else if (gm <= 2)
+    decode_split_kernel<2><<<grid, kSplitThreads, 0, stream>>>(p);
+  else if (gm <= 4)
+    decode_split_kernel<4><<<grid, kSplitThreads, 0, stream>>>(p);
+  else
+    decode_split_kernel<8><<<grid, kSplitThreads, 0, stream>>>(p);
   FFTS_CUDA(cudaGetLastError());
   decode_merge_kernel<<<unsigned(B * H), kThreads, 0, stream>>>(p, static_cast<__nv_bfloat16 *>(out), os_b, os_h);
   FFTS_CUDA(cudaGetLastError());
