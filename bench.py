@@ -81,6 +81,9 @@ def parse():
                     help="BASELINE config of the TTFT decoder (4: Llama-3.1-8B shape, 1 x seq-len tokens; "
                          "5: Qwen2.5-7B shape, 2 x 65536 tokens, block 64)")
     ap.add_argument("--ttft-seq-len", type=int, default=0, help="config 5 sequence length (0: 65536)")
+    ap.add_argument("--ttft-qkv", choices=["fused", "rope_pool"], default="fused",
+                    help="QKV path of the TTFT decoder: qkv_rope_pool (projection GEMM with RoPE and pooling in "
+                         "its epilogue) or a cuBLAS projection followed by rope_pool")
     ap.add_argument("--clock-log", default="",
                     help="directory for the raw nvidia-smi clock samples (default: a temporary directory)")
     return ap.parse_args()
@@ -218,13 +221,17 @@ def kernel_times_us(fn, reps: int = 3) -> dict:
     return {k: round(v, 2) for k, v in out.items()}
 
 
-def caller_side_kernels(dev, L: int, hbm_peak: float, reps: int = 5) -> dict:
-    """Achieved HBM bandwidth of the two caller-side kernels at BASELINE config 4's
-    shape: rope_pool on one layer's QKV projection (32 q / 8 KV heads of 128, L
-    tokens) and one decode step over an L-token cache of 8 KV heads.  Algorithmic
-    bytes: rope_pool reads the projection (L x 6144 bf16) and cos / sin, writes q,
-    k, v head-major and the pooled q / k blocks; decode reads the K and V caches
-    once (2 x L x 8 x 128 x 2 bytes)."""
+def caller_side_kernels(dev, L: int, hbm_peak: float, bf16_peak: float, reps: int = 5) -> dict:
+    """The caller-side kernels at BASELINE config 4's shape (Llama-3.1-8B: hidden
+    4096, 32 q / 8 KV heads of 128, L tokens):
+    - qkv_rope_pool, the QKV projection GEMM with RoPE, layout and pooling in its
+      epilogue: 2 x L x 4096 x 6144 FLOP against the measured bf16 peak, beside
+      the unfused path it replaces (cuBLAS bf16 matmul, then rope_pool);
+    - rope_pool on one layer's QKV projection, against HBM: it reads the
+      projection (L x 6144 bf16) and cos / sin, writes q, k, v head-major and the
+      pooled q / k blocks;
+    - one decode step over an L-token cache of 8 KV heads, against HBM: it reads
+      the K and V caches once (2 x L x 8 x 128 x 2 bytes)."""
     import fftsparse_b200 as F
     g = torch.Generator(device=dev).manual_seed(0)
     H, HKV_, D = HQ, HKV, HEAD_DIM
@@ -254,6 +261,23 @@ def caller_side_kernels(dev, L: int, hbm_peak: float, reps: int = 5) -> dict:
     N = (L + BLOCK - 1) // BLOCK
     rp_bytes = 2 * L * (H + 2 * HKV_) * D * 2 + 2 * L * D * 2 + N * (H + HKV_) * D * 2
     del qkv
+    hid = 4096
+    x = (torch.randn(L, hid, generator=g, device=dev, dtype=torch.float32)).to(torch.bfloat16)
+    w = (torch.randn((H + 2 * HKV_) * D, hid, generator=g, device=dev, dtype=torch.float32) * hid ** -0.5).to(
+        torch.bfloat16)
+    t_fused = timed(lambda: F.qkv_rope_pool(x, w, None, H, HKV_, cos, sin, BLOCK))
+
+    def unfused():
+        qkv_ = torch.matmul(x, w.T)
+        return F.rope_pool(qkv_[:, :H * D], qkv_[:, H * D:(H + HKV_) * D], qkv_[:, (H + HKV_) * D:], H, HKV_, cos,
+                           sin, BLOCK)
+
+    t_unfused = timed(unfused)
+    t_gemm = timed(lambda: torch.matmul(x, w.T))
+    F.check_status(dev)
+    qkv_flops = 2.0 * L * hid * (H + 2 * HKV_) * D
+    del x, w
+    torch.cuda.empty_cache()
     kc = torch.randn(1, HKV_, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     vc = torch.randn(1, HKV_, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     qd = torch.randn(1, H, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
@@ -261,7 +285,13 @@ def caller_side_kernels(dev, L: int, hbm_peak: float, reps: int = 5) -> dict:
     dec_bytes = 2 * L * HKV_ * D * 2
     del kc, vc
     torch.cuda.empty_cache()
-    return {"rope_pool": {"ms": round(t_rp, 4), "bytes": rp_bytes, "gbs": round(rp_bytes / (t_rp * 1e-3) / 1e9, 1),
+    return {"qkv_rope_pool": {"ms": round(t_fused, 4), "flops": qkv_flops,
+                              "tflops": round(qkv_flops / (t_fused * 1e-3) / 1e12, 1),
+                              "frac_bf16": round(qkv_flops / (t_fused * 1e-3) / 1e12 / bf16_peak, 4),
+                              "unfused_ms": round(t_unfused, 4), "cublas_gemm_ms": round(t_gemm, 4),
+                              "unfused": "torch.matmul (cuBLAS bf16) then rope_pool",
+                              "shape": f"x [L={L}, {hid}] @ W^T [{hid}, {(H + 2 * HKV_) * D}], block {BLOCK}"},
+            "rope_pool": {"ms": round(t_rp, 4), "bytes": rp_bytes, "gbs": round(rp_bytes / (t_rp * 1e-3) / 1e9, 1),
                           "frac_hbm": round(rp_bytes / (t_rp * 1e-3) / 1e9 / hbm_peak, 4),
                           "shape": f"L={L}, projection [L, {(H + 2 * HKV_) * D}] bf16, block {BLOCK}"},
             "decode": {"ms": round(t_dec, 4), "bytes": dec_bytes, "gbs": round(dec_bytes / (t_dec * 1e-3) / 1e9, 1),
@@ -355,10 +385,11 @@ class DecoderShape:
     (config 5): hidden 3584, 28 q / 4 kv heads of 128, SwiGLU 18944, RoPE base
     1e6, vocab 152064, 28 layers (shape only: no QKV bias).  Weights ~ N(0, 0.02)
     drawn with one seed (identical on every rank), norm weights 1.  The dense
-    parts are torch/cuBLAS.  Per layer: RMSNorm and the QKV projection;
-    fftsparse_b200's rope_pool per sequence (the caller's RoPE, head-major layout
-    and the pooling of q and k in one pass); its attention on un-expanded GQA k/v,
-    given the pooled blocks.
+    parts are torch/cuBLAS.  Per layer: RMSNorm; fftsparse_b200's qkv_rope_pool
+    (the QKV projection GEMM with the caller's RoPE, the head-major layout and the
+    pooling of q and k in its epilogue), or with ``qkv="rope_pool"`` a cuBLAS
+    projection followed by rope_pool per sequence; its attention on un-expanded
+    GQA k/v, given the pooled blocks.
 
     With world > 1 the layer is split two ways:
     - attention by (sequence, KV group) unit (unit_shard): each rank computes
@@ -375,10 +406,13 @@ class DecoderShape:
     QWEN25_7B = dict(dims=(28, 4, 128, 3584, 18944, 152064), rope_base=1e6, layers=28)
 
     def __init__(self, layers, device, world=1, rank=0, seed=0, gather=None, dims=None, batch=1,
-                 rope_base=500000.0):
+                 rope_base=500000.0, qkv="fused"):
         from fftsparse_b200.dist import unit_shard
         self.H, self.HKV, self.D, self.HIDDEN, self.INTER, self.VOCAB = dims or self.LLAMA31_8B["dims"]
         self.B, self.rope_base = batch, rope_base
+        if qkv not in ("fused", "rope_pool"):
+            raise ValueError(f"qkv must be 'fused' or 'rope_pool', got {qkv!r}")
+        self.qkv = qkv
         g = torch.Generator(device=device).manual_seed(seed)
         self.shard = unit_shard(batch, self.H, self.HKV, world, rank)
         self.world, self.rank = world, rank
@@ -395,9 +429,9 @@ class DecoderShape:
         self.embed = w(self.VOCAB, self.HIDDEN)
         self.layers = []
         for _ in range(layers):
-            wqkv = w(self.HIDDEN, (self.H + 2 * self.HKV) * D)
+            wqkv = w(self.HIDDEN, (self.H + 2 * self.HKV) * D).T  # Linear layout [out, in]
             self.layers.append(dict(
-                wqkv=wqkv if world == 1 else wqkv[:, cols].contiguous(),
+                wqkv=wqkv.contiguous() if world == 1 else wqkv[cols].contiguous(),
                 wo=w(self.H * D, self.HIDDEN),
                 wgu=w(self.HIDDEN, 2 * self.INTER),
                 wd=w(self.INTER, self.HIDDEN)))
@@ -442,14 +476,20 @@ class DecoderShape:
         h = self.embed[ids.reshape(-1)]  # [B * L, HID]
         for lw in self.layers:
             x = self.rmsnorm(h[b_lo * L:b_hi * L])
-            qkv = x @ lw["wqkv"]
-            del x
-            parts = [F.rope_pool(qkv[i * L:(i + 1) * L, :Hl * D], qkv[i * L:(i + 1) * L, Hl * D:(Hl + Hkvl) * D],
-                                 qkv[i * L:(i + 1) * L, (Hl + Hkvl) * D:], Hl, Hkvl, cos, sin, bs)
-                     for i in range(b_hi - b_lo)]
-            del qkv
-            q, k, v, qb, kb = (stack([p[j] for p in parts]) for j in range(5))
-            del parts
+            if self.qkv == "fused":
+                q, k, v, qb, kb = F.qkv_rope_pool(x.view(b_hi - b_lo, L, HID), lw["wqkv"], None, Hl, Hkvl, cos, sin,
+                                                  bs)
+                del x
+            else:
+                qkv = x @ lw["wqkv"].T
+                del x
+                parts = [F.rope_pool(qkv[i * L:(i + 1) * L, :Hl * D],
+                                     qkv[i * L:(i + 1) * L, Hl * D:(Hl + Hkvl) * D],
+                                     qkv[i * L:(i + 1) * L, (Hl + Hkvl) * D:], Hl, Hkvl, cos, sin, bs)
+                         for i in range(b_hi - b_lo)]
+                del qkv
+                q, k, v, qb, kb = (stack([p[j] for p in parts]) for j in range(5))
+                del parts
             if self.world == 1:
                 attn = F.myattn_prefill(q, k, v, 0, pooled=(qb, kb), **kw).view(T, H * D)
             else:
@@ -493,7 +533,7 @@ def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
         shape, B, L, bs, name = DecoderShape.LLAMA31_8B, 1, args.seq_len, BLOCK, "cfg4: Llama-3.1-8B"
     layers = args.ttft_layers or shape["layers"]
     model = DecoderShape(layers, dev, world, rank, gather=gather, dims=shape["dims"], batch=B,
-                         rope_base=shape["rope_base"])
+                         rope_base=shape["rope_base"], qkv=args.ttft_qkv)
     g = torch.Generator(device=dev).manual_seed(0)
     ids = torch.randint(0, model.VOCAB, (B, L), generator=g, device=dev)
     kw = dict(mask_kwargs(args.keep_ratio), block_size=bs)
@@ -518,8 +558,11 @@ def run_ttft(args, dev, world, rank, stream, barrier, gather=None):
             "workload": f"{name}-shape decoder, {layers} layers, random N(0,0.02) weights "
                         f"(seed 0), bf16; prefill of {B} x {L} uniform random token ids (seed 0) to the last-token "
                         f"logits; FFTSparse attention (block {bs}, keep ratio {args.keep_ratio}) in every layer, "
-                        f"GQA k/v un-expanded, RoPE + layout + q/k pooling fused (rope_pool); dense parts "
-                        f"torch/cuBLAS"
+                        f"GQA k/v un-expanded, "
+                        + ("QKV projection GEMM with RoPE + layout + q/k pooling in its epilogue (qkv_rope_pool)"
+                           if args.ttft_qkv == "fused" else
+                           "cuBLAS QKV projection, then RoPE + layout + q/k pooling in one pass (rope_pool)")
+                        + "; other dense parts torch/cuBLAS"
                         + ("" if world == 1 else f"; QKV columns and attention sharded by (sequence, KV group) over "
                                                  f"{world} ranks, o_proj/MLP sharded by token rows, hidden states "
                                                  f"all-gathered per layer"),
@@ -703,7 +746,7 @@ def run_ours(args):
     caller = None
     if not args.no_caller_kernels:
         try:
-            caller = caller_side_kernels(dev, L, hbm_peak)
+            caller = caller_side_kernels(dev, L, hbm_peak, bf16_peak)
         except Exception as exc:  # noqa: BLE001 - reported in the field instead of ending the run
             caller = {"error": f"{exc}"[:200]}
 

@@ -7,6 +7,7 @@ Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
   sparse_attention(q, k, v, bits, bs)       block-sparse attention on packed bits
   pool_blocks(x, bs)                        block mean pooling
   rope_pool(q_proj, k_proj, v_proj, ...)    the caller's RoPE + head-major layout + pooling, one pass
+  qkv_rope_pool(hidden, weight, bias, ...)  the QKV projection GEMM with all of rope_pool in its epilogue
   derive_mask_params(L, ...)                host-side parameter derivation
   calibrate.calibrate_from_qk(layers, t)    target-sparsity calibration on the device
   decode_attention(q, k_cache, v_cache)     one-token decode over the un-expanded KV cache
@@ -21,6 +22,7 @@ from .prefill import (  # noqa: F401
     fft_block_mask,
     myattn_prefill,
     pool_blocks,
+    qkv_rope_pool,
     rope_pool,
     sparse_attention,
 )

@@ -20,7 +20,8 @@ reference's ``base_blockmask``) and the intermediate statistics.
 ``rope_pool`` (ffts_rope_pool) serves the caller's side: the RoPE its
 attention forward applies before the call, the head-major layout and the
 pooling of q and k in one pass, whose pooled blocks ``fft_block_mask`` and
-``myattn_prefill`` accept (``pooled=``).  ``corr_mask_fraction`` feeds the
+``myattn_prefill`` accept (``pooled=``); ``qkv_rope_pool`` (ffts_qkv_rope_pool)
+also folds the QKV projection GEMM in front of them.  ``corr_mask_fraction`` feeds the
 reference's calibration hook.
 """
 from __future__ import annotations
@@ -132,6 +133,66 @@ def rope_pool(q_proj: torch.Tensor, k_proj: torch.Tensor, v_proj: Optional[torch
         L, num_heads, num_kv_heads, D, cos.data_ptr(), sin.data_ptr(), cos.stride(0), block_size,
         q.data_ptr(), k.data_ptr(), None if v is None else v.data_ptr(), qb.data_ptr(), kb.data_ptr(),
         _stream_ptr(dev)))
+    return q, k, v, qb, kb
+
+
+def qkv_rope_pool(hidden: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], num_heads: int,
+                  num_kv_heads: int, cos: torch.Tensor, sin: torch.Tensor, block_size: int = 128,
+                  return_projection: bool = False, status: Optional[torch.Tensor] = None):
+    """The caller's QKV projection with RoPE, the head-major layout and the q/k
+    block pooling in the GEMM's epilogue (ffts_qkv_rope_pool).
+
+    hidden [B, L, hidden_size] or [L, hidden_size] bf16 (unit column stride);
+    weight [(num_heads + 2 num_kv_heads) * 128, hidden_size] bf16: the q_proj,
+    k_proj and v_proj weights stacked row-wise (``torch.cat([q_proj.weight,
+    k_proj.weight, v_proj.weight])``); bias: the stacked biases or None; cos /
+    sin: bf16 [L, 128].  Returns (q, k, v, q_pooled, k_pooled) with q
+    [B, num_heads, L, 128], k and v [B, num_kv_heads, L, 128], the pooled blocks
+    [B, H, N, 128]; with ``return_projection`` also the bf16 projection
+    [B, L, (num_heads + 2 num_kv_heads) * 128] before RoPE (what the three
+    Linear calls return, up to the GEMM's summation order), of which the other
+    outputs are exactly ``rope_pool``'s.  ``status`` as for ``sparse_attention``.
+    """
+    if hidden.dim() == 2:
+        hidden = hidden.unsqueeze(0)
+    for name, t in (("hidden", hidden), ("weight", weight), ("cos", cos), ("sin", sin)):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be bf16 with unit column stride")
+    if hidden.dim() != 3 or weight.dim() != 2:
+        raise ValueError("hidden must be [B, L, hidden_size] (or [L, hidden_size]) and weight 2-D")
+    B, L, K = hidden.shape
+    D = 128
+    heads = num_heads + 2 * num_kv_heads
+    if weight.shape != (heads * D, K):
+        raise ValueError(f"weight must be [{heads * D}, {K}] (q, k, v projections stacked), got {tuple(weight.shape)}")
+    if bias is not None and (bias.shape != (heads * D,) or bias.dtype != torch.bfloat16 or not bias.is_contiguous()):
+        raise ValueError(f"bias must be a contiguous bf16 [{heads * D}]")
+    if cos.shape != (L, D) or sin.shape != cos.shape or sin.stride() != cos.stride():
+        raise ValueError(f"cos and sin must both be [{L}, {D}] with the same strides")
+    dev = hidden.device
+    N = (L + block_size - 1) // block_size
+    q = torch.empty(B, num_heads, L, D, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(B, num_kv_heads, L, D, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(B, num_kv_heads, L, D, dtype=torch.bfloat16, device=dev)
+    qb = torch.empty(B, num_heads, N, D, dtype=torch.bfloat16, device=dev)
+    kb = torch.empty(B, num_kv_heads, N, D, dtype=torch.bfloat16, device=dev)
+    proj = torch.empty(B, L, heads * D, dtype=torch.bfloat16, device=dev) if return_projection else None
+    own = None
+    if status is None:
+        own = device_status(dev)
+        own.poll()
+        status = own.word
+    lib = _lib.load()
+    _lib.check(lib.ffts_qkv_rope_pool(
+        hidden.data_ptr(), B, L, K, hidden.stride(1), hidden.stride(0), weight.data_ptr(), weight.stride(0),
+        None if bias is None else bias.data_ptr(), num_heads, num_kv_heads, D, cos.data_ptr(), sin.data_ptr(),
+        cos.stride(0), block_size, q.data_ptr(), k.data_ptr(), v.data_ptr(), qb.data_ptr(), kb.data_ptr(),
+        None if proj is None else proj.data_ptr(), 0 if proj is None else proj.stride(1), status.data_ptr(),
+        _stream_ptr(dev)))
+    if own is not None:
+        own.read_back()
+    if return_projection:
+        return q, k, v, qb, kb, proj
     return q, k, v, qb, kb
 
 

@@ -1,6 +1,7 @@
 """Status words of the kernels' bounded waits, read back without stalling the stream.
 
-Every wait inside the attention kernel and the peer all-gather is bounded; when
+Every wait inside the attention and QKV projection kernels and the peer all-gather is
+bounded; when
 one runs out the kernel stores a nonzero code into a status word in device
 memory and returns instead of hanging (the output it leaves is then wrong).
 The reference has no such failure mode (its kernels come from a library whose
@@ -11,6 +12,10 @@ waits are unbounded), so the codes are this library's own:
   3  attention: a softmax warp's wait timed out
   4  attention: dynamic shared memory was not 1024-byte aligned (nothing ran)
   5  peer all-gather: a peer's epoch flag never arrived
+  6  QKV projection: the TMA producer's wait timed out
+  7  QKV projection: the MMA issuer's wait timed out
+  8  QKV projection: an epilogue warp's wait timed out
+  9  QKV projection: dynamic shared memory was not 1024-byte aligned (nothing ran)
 
 A ``StatusWord`` owns one such word.  After each launch that may write it,
 ``read_back`` enqueues an asynchronous copy of the word into pinned host memory
@@ -37,6 +42,10 @@ MESSAGES = {
     3: "attention kernel: a softmax warp's bounded wait timed out",
     4: "attention kernel: dynamic shared memory was not 1024-byte aligned (nothing ran)",
     5: "peer all-gather: a peer's epoch flag never arrived (its rows are missing)",
+    6: "QKV projection kernel: the TMA producer's bounded wait timed out",
+    7: "QKV projection kernel: the MMA issuer's bounded wait timed out",
+    8: "QKV projection kernel: an epilogue warp's bounded wait timed out",
+    9: "QKV projection kernel: dynamic shared memory was not 1024-byte aligned (nothing ran)",
 }
 
 

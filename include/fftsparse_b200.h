@@ -134,6 +134,35 @@ FFTS_API int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_s
                   void *stream);
 
 /*
+ * The caller's QKV projection GEMM with the rotary embedding, head-major layout
+ * and block pooling in its epilogue (tcgen05 tensor cores; the projection
+ * itself never reaches memory unless proj_out is given).  Replaces, ahead of
+ * myattn_prefill, the q_proj / k_proj / v_proj Linear calls of the HF attention
+ * forward the caller runs (eval/LongBench/pred.py:177-194) and then everything
+ * ffts_rope_pool replaces.
+ *   x [B, L, hidden] bf16, row stride x_stride_l, sequence stride x_stride_b
+ *     (ignored for B = 1); hidden, the strides, w_ld and cs_ld multiples of 8.
+ *   w [(Hq + 2 Hkv) * D, hidden] bf16 (row stride w_ld): the q_proj, k_proj and
+ *     v_proj weights stacked row-wise, torch Linear layout.
+ *   bias [(Hq + 2 Hkv) * D] bf16 or NULL, added in fp32 before rounding.
+ *   cos, sin: bf16 [L, D] (row stride cs_ld), the same positions for every sequence.
+ *   q_out [B, Hq, L, D], k_out / v_out [B, Hkv, L, D]; q_pooled [B, Hq, N, D],
+ *     k_pooled [B, Hkv, N, D], N = ceil(L / block_size), block_size 16..128.
+ *   proj_out: NULL, or [B, L, proj_ld] receiving the bf16 projection before RoPE.
+ *   status: NULL or an int32 device word; a bounded wait that times out stores
+ *     6 (copy producer), 7 (MMA issuer) or 8 (epilogue) and the outputs are
+ *     invalid; 9 means the shared memory was misaligned and nothing ran.
+ * proj = bf16(fp32 sum over hidden of x * w (+ bias)); q, k, v and the pooled
+ * blocks are bit-identical to ffts_rope_pool applied to proj.  D must be 128.
+ */
+FFTS_API int32_t ffts_qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t hidden,
+                  int64_t x_stride_l, int64_t x_stride_b, const void *w, int64_t w_ld,
+                  const void *bias, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
+                  const void *sin, int64_t cs_ld, int32_t block_size, void *q_out, void *k_out,
+                  void *v_out, void *q_pooled, void *k_pooled, void *proj_out, int64_t proj_ld,
+                  int32_t *status, void *stream);
+
+/*
  * Decode attention for one new token per sequence over the KV cache.  Replaces
  * the caller's eager decode branch (eval/LongBench/pred.py:306-322:
  * softmax(q k^T / sqrt(D)) v over the repeat_kv-expanded cache) after the

@@ -60,11 +60,23 @@ def _patch_with_oracle(mp=None):
     def fake_rope_pool(qp, kp, vp, h, hkv, cos, sin, block_size=128):
         return O.rope_pool(qp, kp, vp, h, hkv, cos, sin, block_size)
 
+    def fake_qkv_rope_pool(x, w, bias, h, hkv, cos, sin, block_size=128, return_projection=False, status=None):
+        # the projection per sequence, then the oracle's RoPE + layout + pooling
+        assert bias is None and not return_projection
+        D = cos.shape[1]
+        outs = []
+        for s in range(x.shape[0]):
+            p = x[s] @ w.T
+            outs.append(O.rope_pool(p[:, :h * D], p[:, h * D:(h + hkv) * D], p[:, (h + hkv) * D:], h, hkv, cos, sin,
+                                    block_size))
+        return tuple(torch.cat([o[j] for o in outs], 0) for j in range(5))
+
     put = mp.setattr if mp is not None else setattr
     put(P, "fft_block_mask", fake_mask)
     put(P, "sparse_attention", fake_attn)
     put(F, "myattn_prefill", fake_prefill)
     put(F, "rope_pool", fake_rope_pool)
+    put(F, "qkv_rope_pool", fake_qkv_rope_pool)
 
 
 def _run(world, rank, case, mp=None):
