@@ -28,9 +28,11 @@
 //   warps 2-9   epilogue, four warps per row half (thread = TMEM lane = row): read
 //               the accumulator, round it to bf16 in registers (bias added in fp32
 //               first) and release TMEM at once, so the next tile's MMAs overlap
-//               the rest: RoPE against the cos/sin rows, head-major stores, and
-//               the pooling, which transposes the rotated rows through shared
-//               memory so one thread sums one channel of a block in row order.
+//               the rest.  Per head and 64-channel box: RoPE against the cos/sin
+//               rows into a shared-memory box in the TMA SWIZZLE_128B layout, one
+//               TMA tensor store of the box into the head-major output (rows past
+//               L dropped by the map), and the pooling, one thread per channel
+//               summing the box's rows of a block in order.
 // A 256 x 256 tile loads 64 KB per 2 x 128 MMA cycles of each K step, 64 B per
 // SM clock from L2; a 128-row tile would need 96.  Every mbarrier wait is
 // bounded: on a time-out the CTA records a status code, stops, waits (bounded)
@@ -57,7 +59,7 @@ constexpr int kBBytes = kBN * kBK * 2;       // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 320;
 constexpr int kEpiThreads = 256;
-constexpr int kPoolRow = 136;      // bytes per staged row: 64 bf16 + 8 bytes that spread the banks
+constexpr int kBoxBytes = 128 * 128;  // one staged output box: 128 rows x 64 bf16 (TMA SWIZZLE_128B)
 constexpr int kTmemCols = 512;
 constexpr double kWaitSeconds = 2.0;
 constexpr double kDrainSeconds = 4.0;
@@ -70,8 +72,8 @@ constexpr int kErrSmemAlign = 9;
 
 struct Smem {
   static constexpr int stages = 0;
-  static constexpr int pool = kStages * kStageBytes;         // two [128 rows][kPoolRow] transposes
-  static constexpr int bars = pool + 2 * 128 * kPoolRow;
+  static constexpr int stage = kStages * kStageBytes;        // one output box per row half
+  static constexpr int bars = stage + 2 * kBoxBytes;
   static constexpr int nbars = 2 * kStages + 3;
   static constexpr int tmem_slot = bars + nbars * 8;
   static constexpr int abort = tmem_slot + 4;
@@ -87,7 +89,6 @@ constexpr int BDR = BAE + 1;       // drain
 
 struct Params {
   const __nv_bfloat16 *bias;  // [heads * 128] or NULL
-  __nv_bfloat16 *out[3];      // q [B, Hq, L, D], k and v [B, Hkv, L, D]
   __nv_bfloat16 *pooled[2];   // [B, Hq, N, D], [B, Hkv, N, D]
   __nv_bfloat16 *raw;         // optional [B, L, raw_ld] projection before RoPE
   int64_t raw_ld;
@@ -144,7 +145,8 @@ __device__ __forceinline__ TileCoord tile_coord(const Params &p, int t) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     qkv_rope_pool_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
-                         const __grid_constant__ Params p) {
+                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) atomicCAS(p.status, 0, kErrSmemAlign);
@@ -175,6 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_map(&tm_x);
     prefetch_map(&tm_w);
+    prefetch_map(&tm_q);
+    prefetch_map(&tm_k);
+    prefetch_map(&tm_v);
   }
   fence_before();
   __syncthreads();
@@ -257,7 +262,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;          // TMEM lanes this warp may access: 32 * (warp % 4) + [0, 32)
     const int r = quarter * 32 + lane;     // row within the half == TMEM lane
     const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(half * 256);
-    uint8_t *pool = smem + Smem::pool + half * 128 * kPoolRow;
+    uint8_t *stage = smem + Smem::stage + half * kBoxBytes;  // this half's staged output box
+    const uint32_t stage_s = sbase + uint32_t(Smem::stage + half * kBoxBytes);
     const float fbs = float(p.bs);
     bool ok = true;
     int i = 0;
@@ -295,7 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_before();
       mbar_arrive(bar(BAE));
 
-      const int tl = c.mt * kBM + half * 128 + r;  // token within the sequence
+      const int t_half = c.mt * kBM + half * 128;  // first token of this row half
+      const int tl = t_half + r;                     // this thread's token within the sequence
       const bool valid = tl < p.L;
       if (p.raw != nullptr && valid) {
         __nv_bfloat16 *dst = p.raw + (int64_t(c.b) * p.L + tl) * p.raw_ld + col0;
@@ -305,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4 *>(dst + q * 8) =
                 make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
       }
+      if (t_half >= p.L) continue;  // a row half wholly past the sequence (uniform over the half)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int g = c.nt * 2 + hh;  // head of the stacked projection (uniform over the CTA)
@@ -312,82 +320,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int role = g < p.Hq ? 0 : (g < p.Hq + p.Hkv ? 1 : 2);
         const int hr = role == 0 ? g : (role == 1 ? g - p.Hq : g - p.Hq - p.Hkv);
         const int hcount = role == 0 ? p.Hq : p.Hkv;
-        __nv_bfloat16 *orow = p.out[role] + ((int64_t(c.b) * hcount + hr) * p.L + tl) * kD;
-        if (role == 2) {
-          if (valid) {
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-              *reinterpret_cast<uint4 *>(orow + q * 8) = make_uint4(pk[64 * hh + 4 * q], pk[64 * hh + 4 * q + 1],
-                                                                    pk[64 * hh + 4 * q + 2], pk[64 * hh + 4 * q + 3]);
-          }
-          continue;
-        }
+        const CUtensorMap *omap = role == 0 ? &tm_q : (role == 1 ? &tm_k : &tm_v);
         const __nv_bfloat16 *crow = p.cos + int64_t(valid ? tl : 0) * p.cs_ld;
         const __nv_bfloat16 *srow = p.sin + int64_t(valid ? tl : 0) * p.cs_ld;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          // channels [32j, 32j + 32) and their RoPE partners [64 + 32j, 64 + 32j + 32)
+        for (int box = 0; box < 2; ++box) {
+          // ---- this row's 64 channels [64 box, 64 box + 64), rotated for q / k, into
+          // the staged box: 16-byte chunk c8 of row r at r * 128 + ((c8 ^ (r % 8)) * 16),
+          // the TMA SWIZZLE_128B layout (row-per-thread writes and the pooling's
+          // column reads are both free of bank conflicts)
 #pragma unroll
-          for (int e8 = 0; e8 < 4; ++e8) {
-            const int c1 = 32 * j + 8 * e8;
-            uint32_t o1w[4], o2w[4];
-            if (valid) {
-              const uint4 cl = *reinterpret_cast<const uint4 *>(crow + c1);
-              const uint4 ch = *reinterpret_cast<const uint4 *>(crow + 64 + c1);
-              const uint4 sl = *reinterpret_cast<const uint4 *>(srow + c1);
-              const uint4 sh = *reinterpret_cast<const uint4 *>(srow + 64 + c1);
-              const uint32_t cw1[4] = {cl.x, cl.y, cl.z, cl.w}, cw2[4] = {ch.x, ch.y, ch.z, ch.w};
-              const uint32_t sw1[4] = {sl.x, sl.y, sl.z, sl.w}, sw2[4] = {sh.x, sh.y, sh.z, sh.w};
+          for (int c8 = 0; c8 < 8; ++c8) {
+            uint32_t ow[4];
+            const int wo = 64 * hh + 32 * box + 4 * c8;        // own words (channels 64 box + 8 c8 ..)
+            const int wp = 64 * hh + 32 * (1 - box) + 4 * c8;  // RoPE partners (channels -+ 64)
+            if (!valid) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) ow[e] = 0u;  // rows past L pool as +0 and are not stored
+            } else if (role == 2) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) ow[e] = pk[wo + e];
+            } else {
+              const int cc = 64 * box + 8 * c8;
+              const uint4 cv = *reinterpret_cast<const uint4 *>(crow + cc);
+              const uint4 sv = *reinterpret_cast<const uint4 *>(srow + cc);
+              const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const uint32_t xw1 = pk[64 * hh + (c1 >> 1) + e], xw2 = pk[64 * hh + 32 + (c1 >> 1) + e];
-                float o1[2], o2[2];
+                float o[2];
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
-                  const float x1 = u ? hi_f(xw1) : lo_f(xw1), x2 = u ? hi_f(xw2) : lo_f(xw2);
-                  const float ca = u ? hi_f(cw1[e]) : lo_f(cw1[e]), cb = u ? hi_f(cw2[e]) : lo_f(cw2[e]);
-                  const float sa = u ? hi_f(sw1[e]) : lo_f(sw1[e]), sb = u ? hi_f(sw2[e]) : lo_f(sw2[e]);
-                  o1[u] = __fadd_rn(bf(__fmul_rn(x1, ca)), bf(__fmul_rn(-x2, sa)));
-                  o2[u] = __fadd_rn(bf(__fmul_rn(x2, cb)), bf(__fmul_rn(x1, sb)));
+                  const float x = u ? hi_f(pk[wo + e]) : lo_f(pk[wo + e]);
+                  const float xp = u ? hi_f(pk[wp + e]) : lo_f(pk[wp + e]);
+                  const float cf = u ? hi_f(cw[e]) : lo_f(cw[e]), sf = u ? hi_f(sw[e]) : lo_f(sw[e]);
+                  // rotate_half: -x[d + 64] for d < 64, x[d - 64] for d >= 64
+                  o[u] = __fadd_rn(bf(__fmul_rn(x, cf)), bf(__fmul_rn(box ? xp : -xp, sf)));
                 }
-                o1w[e] = pack2(o1[0], o1[1]);
-                o2w[e] = pack2(o2[0], o2[1]);
+                ow[e] = pack2(o[0], o[1]);
               }
-              *reinterpret_cast<uint4 *>(orow + c1) = make_uint4(o1w[0], o1w[1], o1w[2], o1w[3]);
-              *reinterpret_cast<uint4 *>(orow + 64 + c1) = make_uint4(o2w[0], o2w[1], o2w[2], o2w[3]);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) o1w[e] = o2w[e] = 0u;  // rows past L pool as +0
             }
-            // staged row r: channels c1.. at bytes 2 * (8 e8), partners at 64 + 2 * (8 e8)
-            uint2 *st = reinterpret_cast<uint2 *>(pool + r * kPoolRow + 16 * e8);
-            st[0] = make_uint2(o1w[0], o1w[1]);
-            st[1] = make_uint2(o1w[2], o1w[3]);
-            st[8] = make_uint2(o2w[0], o2w[1]);
-            st[9] = make_uint2(o2w[2], o2w[3]);
+            *reinterpret_cast<uint4 *>(stage + r * 128 + ((c8 ^ (r & 7)) << 4)) =
+                make_uint4(ow[0], ow[1], ow[2], ow[3]);
           }
+          fence_proxy_async();
           half_sync(half);
-          // ---- pooling: thread r sums staged channel r % 64 of blocks r / 64, r / 64 + 2, ...
-          {
+          if (r == 0) {  // one thread stores the box: rows past L fall outside the map and are dropped
+            tma_store_3d(omap, stage_s, 64 * box, t_half, c.b * hcount + hr);
+            bulk_commit();
+          }
+          if (role != 2) {
+            // ---- pooling: thread r sums staged channel r % 64 of blocks r / 64, r / 64 + 2, ...
             const int ch = r & 63;
-            const int col = ch < 32 ? 32 * j + ch : 64 + 32 * j + (ch - 32);
-            const __nv_bfloat16 *src = reinterpret_cast<const __nv_bfloat16 *>(pool) + ch;
+            const uint8_t *col = stage + (ch & 7) * 2;
             for (int pb = r >> 6; pb * p.bs < 128; pb += 2) {
-              const int n = (c.mt * kBM + half * 128 + pb * p.bs) / p.bs;
+              const int n = (t_half + pb * p.bs) / p.bs;
               if (n >= p.N) break;
               float s = 0.0f;
               const int r0 = pb * p.bs;
 #pragma unroll 8
-              for (int rr = 0; rr < p.bs; ++rr)
-                s = __fadd_rn(s, __bfloat162float(src[(r0 + rr) * (kPoolRow / 2)]));
-              p.pooled[role][((int64_t(c.b) * hcount + hr) * p.N + n) * kD + col] =
+              for (int rr = r0; rr < r0 + p.bs; ++rr)
+                s = __fadd_rn(s, __bfloat162float(
+                                     *reinterpret_cast<const __nv_bfloat16 *>(col + rr * 128 + (((ch >> 3) ^ (rr & 7)) << 4))));
+              p.pooled[role][((int64_t(c.b) * hcount + hr) * p.N + n) * kD + 64 * box + ch] =
                   __float2bfloat16_rn(__fdiv_rn(s, fbs));
             }
           }
-          half_sync(half);  // the next chunk overwrites the staged rows
+          if (r == 0) bulk_wait_read();  // the store has read the box
+          half_sync(half);               // before the next box overwrites it
         }
       }
     }
+    if (r == 0) bulk_wait();  // this half's stores are complete before the CTA exits
     if (!ok) {
       *abort_flag = 1;
       atomicCAS(p.status, 0, kErrTimeoutEpilogue);
@@ -414,10 +417,11 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// bf16 rows of `inner` elements: dims {inner, rows, batch, 1}, row / batch strides in elements,
-// box {64, 256, 1, 1}, SWIZZLE_128B; out-of-range rows and columns read as zero.
-static int make_map(CUtensorMap *map, const void *base, int64_t inner, int64_t rows, int64_t batch, int64_t ld,
-                    int64_t sb) {
+// bf16 rows of `inner` elements: dims {inner, rows, batch} (and a unit fourth dim
+// when rank = 4), row / batch strides in elements, box {64, box_rows, 1(, 1)},
+// SWIZZLE_128B; loads read out-of-range rows and columns as zero, stores drop them.
+static int make_map(CUtensorMap *map, int rank, const void *base, int64_t inner, int64_t rows, int64_t batch,
+                    int64_t ld, int64_t sb, int box_rows) {
   auto enc = get_encode();
   if (!enc) {
     set_error(FFTS_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -425,11 +429,11 @@ static int make_map(CUtensorMap *map, const void *base, int64_t inner, int64_t r
   }
   cuuint64_t dims[4] = {cuuint64_t(inner), cuuint64_t(rows), cuuint64_t(batch), 1};
   cuuint64_t strides[3] = {cuuint64_t(ld) * 2, cuuint64_t(sb) * 2, cuuint64_t(sb) * 2 * cuuint64_t(batch)};
-  cuuint32_t box[4] = {cuuint32_t(kBK), 256, 1, 1};
+  cuuint32_t box[4] = {cuuint32_t(kBK), cuuint32_t(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult res = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult res = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void *>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (res != CUDA_SUCCESS) {
     set_error(FFTS_E_INVALID, "cuTensorMapEncodeTiled failed (%d): check 16-byte aligned base and strides", int(res));
     return FFTS_E_INVALID;
@@ -462,15 +466,16 @@ int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, 
   for (const void *ptr : {x, w, bias, cos, sin, (const void *)q_out, (const void *)k_out, (const void *)v_out,
                           (const void *)q_pooled, (const void *)k_pooled, (const void *)raw})
     FFTS_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "qkv_rope_pool: pointers must be 16-byte aligned");
-  CUtensorMap mx, mw;
-  int rc = make_map(&mx, x, K, L, B, x_ld, B == 1 ? L * x_ld : x_sb);
-  if (!rc) rc = make_map(&mw, w, K, heads * kD, 1, w_ld, heads * kD * w_ld);
+  CUtensorMap mx, mw, mq, mk, mv;
+  int rc = make_map(&mx, 4, x, K, L, B, x_ld, B == 1 ? L * x_ld : x_sb, kBM);
+  if (!rc) rc = make_map(&mw, 4, w, K, heads * kD, 1, w_ld, heads * kD * w_ld, kBN);
+  // outputs [B * H, L, D]: a store box is 128 rows of one head, clipped at L
+  if (!rc) rc = make_map(&mq, 3, q_out, kD, L, B * Hq, kD, L * kD, 128);
+  if (!rc) rc = make_map(&mk, 3, k_out, kD, L, B * Hkv, kD, L * kD, 128);
+  if (!rc) rc = make_map(&mv, 3, v_out, kD, L, B * Hkv, kD, L * kD, 128);
   if (rc) return rc;
   Params p{};
   p.bias = static_cast<const __nv_bfloat16 *>(bias);
-  p.out[0] = static_cast<__nv_bfloat16 *>(q_out);
-  p.out[1] = static_cast<__nv_bfloat16 *>(k_out);
-  p.out[2] = static_cast<__nv_bfloat16 *>(v_out);
   p.pooled[0] = static_cast<__nv_bfloat16 *>(q_pooled);
   p.pooled[1] = static_cast<__nv_bfloat16 *>(k_pooled);
   p.raw = static_cast<__nv_bfloat16 *>(raw);
@@ -505,7 +510,7 @@ int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, 
   rc = device_sm_count(&sms);
   if (rc) return rc;
   const unsigned grid = unsigned(p.tiles < sms ? p.tiles : sms);
-  qkv_rope_pool_kernel<<<grid, kThreads, Smem::bytes, stream>>>(mx, mw, p);
+  qkv_rope_pool_kernel<<<grid, kThreads, Smem::bytes, stream>>>(mx, mw, mq, mk, mv, p);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }
