@@ -622,6 +622,45 @@ __device__ double lane_tree(double v, double *part) {
   return r;
 }
 
+// ------------------------------------------------------ exact fp32 products
+// safe[head][part] = 1 when every pooled value of the head's part (q heads
+// first, then k heads; contiguous N x D each, kRangeParts CTAs per head) is zero
+// or has a magnitude in [2^-63, 2^64).
+// The product of two such bf16 values is exact in fp32: 8 + 8 significant bits
+// and a normal exponent.  An fp64 sum that adds (double)(a * b) formed in fp32
+// therefore equals the canonical exact-product chain fma((double)a, (double)b,
+// acc) bit for bit, with one conversion per term instead of two.  fp32 inputs
+// never take this path (their products are not exact in fp32).
+constexpr int kRangeParts = 4;  // CTAs per head, each flags its share of the head's values
+
+__global__ void __launch_bounds__(256) exact_range_kernel(const uint4 *__restrict__ qb, const uint4 *__restrict__ kb,
+                                                          int64_t nq_heads, int64_t vec_per_head,
+                                                          int32_t *__restrict__ safe) {
+  const int64_t head = blockIdx.x / kRangeParts;
+  const int part = blockIdx.x % kRangeParts;
+  const uint4 *src = head < nq_heads ? qb + head * vec_per_head : kb + (head - nq_heads) * vec_per_head;
+  int ok = 1;
+  for (int64_t i = threadIdx.x + int64_t(part) * blockDim.x; i < vec_per_head; i += int64_t(blockDim.x) * kRangeParts) {
+    const uint4 v = src[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t mag = (w[e >> 1] >> (16 * (e & 1))) & 0x7fffu;  // bf16 magnitude bits
+      ok &= int(mag == 0u || (mag >= (64u << 7) && mag < (191u << 7)));
+    }
+  }
+  ok = __syncthreads_and(ok);
+  if (threadIdx.x == 0) safe[blockIdx.x] = ok;
+}
+
+// Every part of the head's values allows exact fp32 products.
+__device__ __forceinline__ bool range_ok(const int32_t *__restrict__ safe, int64_t head) {
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < kRangeParts; ++i) ok = ok && safe[head * kRangeParts + i] != 0;
+  return ok;
+}
+
 // ------------------------------------------------------- stripe statistic
 // One CTA per (b, h, group of sampled lags whose lags lie within kDiagSpan
 // blocks of each other): the normalised variance of the adjacent differences
@@ -646,7 +685,8 @@ struct DiagGroups {
 template <typename T>
 __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
                                 const ffts_mask_params &p, double *__restrict__ nv, int first, int G, int bh,
-                                int gmax, unsigned char *smem_raw) {
+                                int gmax, unsigned char *smem_raw, const int32_t *__restrict__ safe_q,
+                                const int32_t *__restrict__ safe_k) {
   const int N = p.n_blocks;
   const int QS = stage_stride<T>(D);
   const int tid = threadIdx.x;
@@ -662,8 +702,9 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   // [gmax][256], 16-byte aligned whatever gmax * N is
   double *part = reinterpret_cast<double *>((reinterpret_cast<uintptr_t>(vals + gmax * N) + 15) & ~uintptr_t(15));
   const int b = bh / H, h = bh % H;
+  const int kh = b * Hkv + h / (H / Hkv);
   const T *q = qb + int64_t(bh) * N * D;
-  const T *k = kb + (int64_t(b) * Hkv + h / (H / Hkv)) * N * D;
+  const T *k = kb + int64_t(kh) * N * D;
   const double sqrtD = sqrt((double)D);
   constexpr int V = Elem<T>::kVec;
   const int vrow = D / V;
@@ -709,9 +750,18 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
       const T *qa = qw + (t1 + tau1 - t0 - lo) * QS, *ka = ks + (t1 - t0) * QS;
       const T *qb2 = qw + ((v2 ? t2 : t1) + tau2 - t0 - lo) * QS, *kb2 = ks + ((v2 ? t2 : t1) - t0) * QS;
       double a1 = 0.0, a2 = 0.0;
-      for (int d = 0; d < D; ++d) {
-        a1 = __fma_rn((double)Elem<T>::to_f32(qa[d]), (double)Elem<T>::to_f32(ka[d]), a1);
-        a2 = __fma_rn((double)Elem<T>::to_f32(qb2[d]), (double)Elem<T>::to_f32(kb2[d]), a2);
+      bool exact32 = false;
+      if constexpr (sizeof(T) == 2) exact32 = safe_q != nullptr && range_ok(safe_q, bh) && range_ok(safe_k, kh);
+      if (exact32) {
+        for (int d = 0; d < D; ++d) {
+          a1 = __dadd_rn(a1, (double)__fmul_rn(Elem<T>::to_f32(qa[d]), Elem<T>::to_f32(ka[d])));
+          a2 = __dadd_rn(a2, (double)__fmul_rn(Elem<T>::to_f32(qb2[d]), Elem<T>::to_f32(kb2[d])));
+        }
+      } else {
+        for (int d = 0; d < D; ++d) {
+          a1 = __fma_rn((double)Elem<T>::to_f32(qa[d]), (double)Elem<T>::to_f32(ka[d]), a1);
+          a2 = __fma_rn((double)Elem<T>::to_f32(qb2[d]), (double)Elem<T>::to_f32(kb2[d]), a2);
+        }
       }
       if (v1) vals[g1 * N + t1] = __double2float_rn(__ddiv_rn(a1, sqrtD));
       if (v2) vals[g2 * N + t2] = __double2float_rn(__ddiv_rn(a2, sqrtD));
@@ -943,7 +993,9 @@ __global__ void __launch_bounds__(256, 1) select_stage1_kernel(const T *__restri
                                                                DiagGroups gr, int gmax,
                                                                float2 *__restrict__ partial, double *__restrict__ nv,
                                                                uint32_t *__restrict__ colsel,
-                                                               uint32_t *__restrict__ lastsel) {
+                                                               uint32_t *__restrict__ lastsel,
+                                                               const int32_t *__restrict__ safe_q,
+                                                               const int32_t *__restrict__ safe_k) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ int hist[256];
   __shared__ int bc[4];
@@ -952,7 +1004,8 @@ __global__ void __launch_bounds__(256, 1) select_stage1_kernel(const T *__restri
     colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid, smem_raw, hist, bc);
   } else if (bid < nBH + nDG) {
     const int e = bid - nBH, g = e % gr.n;
-    diag_group_body<T>(qb, kb, H, Hkv, D, p, nv, gr.first[g], gr.count[g], e / gr.n, gmax, smem_raw);
+    diag_group_body<T>(qb, kb, H, Hkv, D, p, nv, gr.first[g], gr.count[g], e / gr.n, gmax, smem_raw, safe_q,
+                       safe_k);
   } else {
     const int f = bid - nBH - nDG;
     if constexpr (R > 0)
@@ -1154,6 +1207,7 @@ struct MaskWorkspace {
   double *nv;  // [B*H][FFTS_MAX_DIAG_SAMPLES] per-lag stripe statistics
   uint32_t *tausel, *colsel, *lastsel;
   int32_t *stripe;
+  int32_t *safe;  // [B*H q heads, then up to B*H k heads][kRangeParts]: exact fp32 products (exact_range_kernel)
   int64_t bytes;
 };
 
@@ -1179,6 +1233,8 @@ static MaskWorkspace carve(void *ws, int64_t B, int64_t H, int64_t N, int64_t D)
   off += align256(B * H * W * 4);
   m.stripe = reinterpret_cast<int32_t *>(p + off);
   off += align256(B * H * 4);
+  m.safe = reinterpret_cast<int32_t *>(p + off);
+  off += align256(2 * B * H * 4 * kRangeParts);
   m.bytes = off;
   return m;
 }
@@ -1197,6 +1253,17 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   const int nchunk = int(ceil_div(D, kDChunk));
   const int W = int(ceil_div(N, 32));
   const unsigned BH = unsigned(B * H);
+  // which heads' pooled values allow exact fp32 products (bf16 only)
+  const int32_t *safe_q = nullptr, *safe_k = nullptr;
+  if (sizeof(T) == 2 && D % 8 == 0) {
+    const int64_t nq = B * H, nk = B * Hkv;
+    exact_range_kernel<<<unsigned((nq + nk) * kRangeParts), 256, 0, stream>>>(reinterpret_cast<const uint4 *>(qb),
+                                                             reinterpret_cast<const uint4 *>(kb), nq,
+                                                             int64_t(N) * D / 8, ws.safe);
+    FFTS_CUDA(cudaGetLastError());
+    safe_q = ws.safe;
+    safe_k = ws.safe + nq * kRangeParts;
+  }
   // stage 1: FFT partial spectra, per-lag stripe statistics, column and last-row selections
   int nf = kDChunk;
   while (nf > 1 && fft_partial_smem(M, nf) > 64 * 1024) nf >>= 1;
@@ -1221,7 +1288,7 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
     }                                                                                                            \
     select_stage1_kernel<T, RR><<<grid1, 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, \
                                                                int(BH), nDG, gr, gmax, ws.partial, ws.nv,         \
-                                                               ws.colsel, ws.lastsel);                           \
+                                                               ws.colsel, ws.lastsel, safe_q, safe_k);           \
     break;                                                                                                       \
   }
   switch (R) {
