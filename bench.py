@@ -84,6 +84,9 @@ def parse():
     ap.add_argument("--ttft-qkv", choices=["fused", "rope_pool"], default="fused",
                     help="QKV path of the TTFT decoder: qkv_rope_pool (projection GEMM with RoPE and pooling in "
                          "its epilogue) or a cuBLAS projection followed by rope_pool")
+    ap.add_argument("--caller-kernels-only", action="store_true",
+                    help="time only the caller-side kernels (qkv_rope_pool, rope_pool, decode) at --seq-len on one "
+                         "GPU and print their field (the small case the profiles capture)")
     ap.add_argument("--clock-log", default="",
                     help="directory for the raw nvidia-smi clock samples (default: a temporary directory)")
     return ap.parse_args()
@@ -865,7 +868,15 @@ def main():
     _RESULT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
     args = parse()
-    if args.impl == "reference":
+    if args.caller_kernels_only:
+        import fftsparse_b200 as F
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        F.load_library()
+        hbm_peak, bf16_peak, _, peak_kind = load_peaks()
+        emit({"caller_kernels": caller_side_kernels(dev, args.seq_len, hbm_peak, bf16_peak, reps=args.steps),
+              "seq_len": args.seq_len, "peak_kind": peak_kind})
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
