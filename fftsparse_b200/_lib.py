@@ -41,7 +41,8 @@ EXPORTS = {
     "ffts_rope_pool": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I32,
                               _P, _P, _P, _P, _P, _P]),
     "ffts_qkv_rope_pool": (_I32, [_P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _P, _I64,
-                                  _I32, _P, _P, _P, _P, _P, _P, _I64, _P, _P]),
+                                  _I32, _P, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P]),
+    "ffts_qkv_workspace_bytes": (_I64, [_I64]),
     "ffts_decode_workspace_bytes": (_I64, [_I64, _I64, _I64, _I64]),
     "ffts_decode_attn": (_I32, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P,
                                 _I64, _I64, _P, _I32, _I64, _P]),

@@ -94,7 +94,9 @@ int launch_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64_t
 int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, int64_t x_sb, const void *w,
                   int64_t w_ld, const void *bias, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
                   const void *sin, int64_t cs_ld, int bs, void *q_out, void *k_out, void *v_out, void *q_pooled,
-                  void *k_pooled, void *raw, int64_t raw_ld, int32_t *status, cudaStream_t stream);
+                  void *k_pooled, void *raw, int64_t raw_ld, void *workspace, int64_t ws_bytes, int32_t *status,
+                  cudaStream_t stream);
+int64_t qkv_workspace_bytes(int64_t L);
 int64_t decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits);
 int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const int64_t *ks, const void *v,
                 const int64_t *vs, int64_t B, int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits,
@@ -175,14 +177,17 @@ int32_t ffts_qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t hidden, 
                            int64_t x_stride_b, const void *w, int64_t w_ld, const void *bias, int64_t Hq,
                            int64_t Hkv, int64_t D, const void *cos, const void *sin, int64_t cs_ld,
                            int32_t block_size, void *q_out, void *k_out, void *v_out, void *q_pooled,
-                           void *k_pooled, void *proj_out, int64_t proj_ld, int32_t *status, void *stream) {
+                           void *k_pooled, void *proj_out, int64_t proj_ld, void *workspace,
+                           int64_t workspace_bytes, int32_t *status, void *stream) {
   g_last_error.clear();
   int rc = check_device();
   if (rc) return rc;
   return qkv_rope_pool(x, B, L, hidden, x_stride_l, x_stride_b, w, w_ld, bias, Hq, Hkv, D, cos, sin, cs_ld,
-                       block_size, q_out, k_out, v_out, q_pooled, k_pooled, proj_out, proj_ld, status,
-                       static_cast<cudaStream_t>(stream));
+                       block_size, q_out, k_out, v_out, q_pooled, k_pooled, proj_out, proj_ld, workspace,
+                       workspace_bytes, status, static_cast<cudaStream_t>(stream));
 }
+
+int64_t ffts_qkv_workspace_bytes(int64_t L) { return qkv_workspace_bytes(L); }
 
 int64_t ffts_decode_workspace_bytes(int64_t B, int64_t H, int64_t Hkv, int64_t splits) {
   return decode_workspace_bytes(B, H, Hkv, splits);

@@ -7,24 +7,27 @@
 // all G q-heads of its group: HBM-bound at 2 * B * Hkv * Lk * D * 2 bytes.
 //
 // decode_split_kernel: CTA = (b, kv head, split of the keys, up to 8 q-heads
-// of the group); 256 threads.  The split's keys are walked in chunks of 64:
-//   scores   a half-warp per key row, 16-byte loads (lane = 8 channels), so each
-//            warp instruction reads two whole rows; q of the heads in
-//            registers; fp32 dot products reduced over the 16 lanes, in log2
-//            units;
-//   softmax  warp w handles head w: chunk max, running max m and sum l, the
-//            chunk's exponentials in place;
-//   P V      the same row split over V; each lane accumulates its 8 channels for
-//            every head, rescaled when the running max moves; the row slots
-//            are summed once at the end of the split.
+// of the group); 256 threads, one CTA per SM.  The split's keys are cut into
+// chunks of 8 rows (4 when the CTA holds 8 heads); warp w takes chunks w, w + 8,
+// ... and streams their K and V rows through its own 4-stage cp.async ring, so
+// about 96 KB of cache per SM is in flight and no CTA-wide barrier interrupts
+// the stream:
+//   scores   a half-warp per key row (lane = 8 channels, 16 bytes), q of the
+//            heads in registers; fp32 dot products reduced over the 16 lanes,
+//            in log2 units;
+//   softmax  per warp and head: running max m and sum l, updated per chunk;
+//   P V      each lane accumulates its 8 channels for every head, rescaled when
+//            the running max moves.
 // An optional additive bias per (sequence, key) -- the caller's attention mask,
 // added to the scaled scores before the softmax as at pred.py:311-313 -- is
-// read once per key with the key's scores.  Fully masked chunks contribute
-// nothing (their maxima stay -inf and their exponentials are 0).
-// The split's (o[D], m, l) per head go to a workspace.
+// read once per key with the key's scores.  Fully masked keys contribute
+// nothing (their exponentials are 0).  At the end of the split the warps'
+// (o[D], m, l) are rescaled to their common maximum and summed into the
+// workspace.
 // decode_merge_kernel: CTA = (b, q head): o = sum_s 2^(m_s - M) o_s /
 // sum_s 2^(m_s - M) l_s, rounded to bf16.
-// No waits; every __syncthreads is reached by the whole CTA; every index is
+// No spin-waits (cp.async completion is a hardware wait on the warp's own
+// copies); every __syncthreads is reached by the whole CTA; every index is
 // bounded by Lk, G <= 16 (in blocks of 8 heads per CTA) and D = 128.
 
 #include <algorithm>
@@ -60,8 +63,9 @@ __device__ __forceinline__ float bias_log2(const Params &p, int b, int key) {
   return x * 1.4426950408889634f;  // scores are kept in log2 units
 }
 
-constexpr int kSplitThreads = 256;  // 8 warps
-constexpr int kRows = 64;           // keys per chunk: 8 per warp, two per warp instruction
+constexpr int kSplitThreads = 256;  // 8 warps, each walking its own chunks of keys
+constexpr int kWarps = kSplitThreads / 32;
+constexpr int kStages = 4;          // cp.async ring depth per warp
 constexpr int kHeadsPerCta = 8;     // q-heads of one group per CTA (groups of up to 16 take two CTAs)
 
 __device__ __forceinline__ void widen8(const uint4 &raw, float *f) {
@@ -73,18 +77,40 @@ __device__ __forceinline__ void widen8(const uint4 &raw, float *f) {
   }
 }
 
+// 16-byte global -> shared copy; src_bytes 0 writes zeros without reading
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Dynamic shared memory of decode_split_kernel<GM, ITS>: every warp's ring of
+// kStages chunks, K rows then V rows of 2 * ITS keys (256 bytes each).
+template <int ITS>
+constexpr int split_smem_bytes() {
+  return kWarps * kStages * 2 * (2 * ITS) * kD * 2;
+}
+
 // CTA = (b, kv head, split of the keys, block of up to 8 q-heads of the group);
-// 256 threads.  Each half-warp reads one key row with 16-byte loads (lane =
-// 8-channel segment), so a warp instruction moves two whole 256-byte rows and a
-// chunk of 64 rows is in flight per CTA; the G dot products of a row are
-// reduced over the 16 lanes by shuffles.  Softmax per chunk as before (warp w
-// handles head w); P V: each lane accumulates its 8 channels over its rows for
-// every head, and the 16 row slots are summed once at the end of the split.
-template <int GM>
-__global__ void __launch_bounds__(kSplitThreads) decode_split_kernel(const __grid_constant__ Params p) {
-  __shared__ float s_s[GM][kRows];
-  __shared__ float m_s[GM], l_s[GM], a_s[GM];
-  __shared__ float red[kSplitThreads / 32][GM][kD];
+// 256 threads.  The split's keys are cut into chunks of R = 2 * ITS rows, and
+// warp w takes chunks w, w + 8, ...: each warp keeps its own online softmax
+// (running max m and sum l per head, in log2 units) and P V accumulators, so
+// warps never wait for one another until the end of the split.  A warp's K and
+// V rows stream through its own kStages-deep cp.async ring: a half-warp copies
+// one 256-byte row (lane = 16 bytes, 8 channels) and later reads back exactly
+// the bytes it copied, so no cross-lane barrier is needed.  Per chunk: the G
+// dot products of a row are reduced over the half-warp's 16 lanes; the chunk's
+// maximum and exponential sum combine the two halves; each lane accumulates P V
+// for its 8 channels.  At the end the halves, then the warps (rescaled to the
+// CTA's maximum) are summed into the split's (o, m, l) per head.
+template <int GM, int ITS>
+__global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __grid_constant__ Params p) {
+  constexpr int R = 2 * ITS;
+  constexpr int kRowBytes = kD * 2;
+  constexpr int kSlot = 2 * R * kRowBytes;  // K rows, then V rows
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ float wm[kWarps][GM], wl[kWarps][GM];
   const int G = p.H / p.Hkv;
   const int bh = blockIdx.x;  // b * Hkv + kv head
   const int b = bh / p.Hkv, kvh = bh % p.Hkv;
@@ -110,38 +136,54 @@ __global__ void __launch_bounds__(kSplitThreads) decode_split_kernel(const __gri
       for (int e = 0; e < 8; ++e) qr[g][e] = 0.0f;
     }
   }
-  if (tid < GM) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.0f;
-  }
-  float acc[GM][8];
+  float m[GM], l[GM], acc[GM][8];
 #pragma unroll
-  for (int g = 0; g < GM; ++g)
+  for (int g = 0; g < GM; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+  }
   const __nv_bfloat16 *kb = p.k + int64_t(b) * p.ks_b + int64_t(kvh) * p.ks_h + seg * 8;
   const __nv_bfloat16 *vb = p.v + int64_t(b) * p.vs_b + int64_t(kvh) * p.vs_h + seg * 8;
-  __syncthreads();
-  for (int c0 = k0; c0 < k1; c0 += kRows) {
-    const int n = min(kRows, k1 - c0);
-    // rows warp * 8 + 2 * it + half of the chunk: K and V loads issued together
-    uint4 kv[4], vv[4];
+  const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(dsm)) + uint32_t(warp * kStages * kSlot);
+  const uint8_t *ring_p = dsm + warp * kStages * kSlot;
+  // the lane's 16 bytes of row 2 * it + half inside a slot's K (V: + R rows)
+  const uint32_t lane_off = uint32_t(half * kRowBytes + seg * 16);
+  const int nchunks = (k1 - k0 + R - 1) / R;
+  const int mine = nchunks > warp ? (nchunks - warp + kWarps - 1) / kWarps : 0;  // chunks of this warp
+
+  auto issue = [&](int j) {  // this warp's chunk j into slot j % kStages
+    const int base = k0 + (warp + kWarps * j) * R;
+    const uint32_t slot = ring + uint32_t((j % kStages) * kSlot) + lane_off;
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int row = warp * 8 + 2 * it + half;
-      kv[it] = row < n ? *reinterpret_cast<const uint4 *>(kb + int64_t(c0 + row) * p.ks_l) : make_uint4(0, 0, 0, 0);
+    for (int it = 0; it < ITS; ++it) {
+      const int row = base + 2 * it + half;
+      const bool ok = row < k1;
+      const int64_t r = ok ? row : k0;  // a valid address; nothing is read when !ok
+      cp_async16(slot + uint32_t(2 * it * kRowBytes), kb + r * p.ks_l, ok ? 16 : 0);
+      cp_async16(slot + uint32_t((R + 2 * it) * kRowBytes), vb + r * p.vs_l, ok ? 16 : 0);
     }
+  };
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int row = warp * 8 + 2 * it + half;
-      vv[it] = row < n ? *reinterpret_cast<const uint4 *>(vb + int64_t(c0 + row) * p.vs_l) : make_uint4(0, 0, 0, 0);
-    }
+  for (int j = 0; j < kStages - 1; ++j) {
+    if (j < mine) issue(j);
+    cp_async_commit();  // empty groups keep the count uniform
+  }
+  for (int j = 0; j < mine; ++j) {
+    if (j + kStages - 1 < mine) issue(j + kStages - 1);
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();  // chunk j has landed (this lane's own bytes)
+    const uint8_t *slot = ring_p + (j % kStages) * kSlot + lane_off;
+    const int base = k0 + (warp + kWarps * j) * R;
+    // ---- scores of the chunk's rows (this half's rows: 2 * it + half)
+    float sc[GM][ITS];
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int row = warp * 8 + 2 * it + half;
+    for (int it = 0; it < ITS; ++it) {
+      const int row = base + 2 * it + half;
       float kf[8];
-      widen8(kv[it], kf);
-      const float bl = (seg == 0 && row < n) ? bias_log2(p, b, c0 + row) : 0.0f;
+      widen8(*reinterpret_cast<const uint4 *>(slot + 2 * it * kRowBytes), kf);
+      const float bl = row < k1 ? bias_log2(p, b, row) : 0.0f;
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
         float part = 0.0f;
@@ -149,77 +191,85 @@ __global__ void __launch_bounds__(kSplitThreads) decode_split_kernel(const __gri
         for (int e = 0; e < 8; ++e) part = fmaf(qr[g][e], kf[e], part);
 #pragma unroll
         for (int o = 8; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        if (seg == 0 && row < n) s_s[g][row] = part + bl;
+        sc[g][it] = row < k1 ? part + bl : -INFINITY;
       }
     }
-    __syncthreads();
-    // softmax of the chunk: warp w handles head w
-    if (warp < ng) {
-      const int g = warp;
-      const float x = lane < n ? s_s[g][lane] : -INFINITY;
-      const float y = lane + 32 < n ? s_s[g][lane + 32] : -INFINITY;
-      float mx = fmaxf(x, y);
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_old = m_s[g];
-      const float m_new = fmaxf(m_old, mx);
-      const float ex = m_new == -INFINITY ? 0.0f : exp2f(x - m_new);
-      const float ey = m_new == -INFINITY ? 0.0f : exp2f(y - m_new);
-      s_s[g][lane] = ex;
-      s_s[g][lane + 32] = ey;
-      float sum = ex + ey;
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) {
-        const float alpha = m_old == -INFINITY ? 0.0f : exp2f(m_old - m_new);
-        a_s[g] = alpha;
-        l_s[g] = l_s[g] * alpha + sum;
-        m_s[g] = m_new;
-      }
-    }
-    __syncthreads();
-    // P V over the same rows
+    // ---- online softmax over the chunk (both halves agree on m and l)
+    float pr[GM][ITS];
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
-      const float alpha = g < ng ? a_s[g] : 1.0f;
+      float mx = sc[g][0];
+#pragma unroll
+      for (int it = 1; it < ITS; ++it) mx = fmaxf(mx, sc[g][it]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float m_new = fmaxf(m[g], mx);
+      const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m[g] - m_new);
+      float sum = 0.0f;
+#pragma unroll
+      for (int it = 0; it < ITS; ++it) {
+        pr[g][it] = m_new == -INFINITY ? 0.0f : exp2f(sc[g][it] - m_new);
+        sum += pr[g][it];
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+      l[g] = l[g] * alpha + sum;
+      m[g] = m_new;
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
     }
+    // ---- P V for the lane's 8 channels
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int row = warp * 8 + 2 * it + half;
+    for (int it = 0; it < ITS; ++it) {
       float vf[8];
-      widen8(vv[it], vf);
+      widen8(*reinterpret_cast<const uint4 *>(slot + (R + 2 * it) * kRowBytes), vf);
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        const float pr = (g < ng && row < n) ? s_s[g][row] : 0.0f;
+      for (int g = 0; g < GM; ++g)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr, vf[e], acc[g][e]);
-      }
+        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr[g][it], vf[e], acc[g][e]);
     }
-    __syncthreads();  // s_s is rewritten by the next chunk
   }
-  // sum the 16 row slots: the two halves of each warp, then the 8 warps
+  cp_async_wait<0>();
+  // ---- the two halves of the warp hold the same channels of different rows
 #pragma unroll
   for (int g = 0; g < GM; ++g)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], 16);
+  __syncthreads();  // every warp is done with its ring: reuse it for the cross-warp sum
+  float *red = reinterpret_cast<float *>(dsm);  // [kWarps][GM][kD]
   if (half == 0) {
 #pragma unroll
     for (int g = 0; g < GM; ++g)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) red[warp][g][seg * 8 + e] = acc[g][e];
+      for (int e = 0; e < 8; ++e) red[(warp * GM + g) * kD + seg * 8 + e] = acc[g][e];
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
   }
   __syncthreads();
   float *w = p.ws + (int64_t(bh) * p.splits + split) * G * (kD + 2);
   for (int idx = tid; idx < ng * kD; idx += kSplitThreads) {
     const int g = idx / kD, d = idx % kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, wm[ww][g]);
     float o = 0.0f;
 #pragma unroll
-    for (int ww = 0; ww < kSplitThreads / 32; ++ww) o += red[ww][g][d];
+    for (int ww = 0; ww < kWarps; ++ww)
+      if (wm[ww][g] != -INFINITY) o = fmaf(exp2f(wm[ww][g] - M), red[(ww * GM + g) * kD + d], o);
     w[(g0 + g) * (kD + 2) + d] = o;
   }
   if (tid < ng) {
-    w[(g0 + tid) * (kD + 2) + kD] = m_s[tid];
-    w[(g0 + tid) * (kD + 2) + kD + 1] = l_s[tid];
+    float M = -INFINITY, L = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, wm[ww][tid]);
+#pragma unroll
+    for (int ww = 0; ww < kWarps; ++ww)
+      if (wm[ww][tid] != -INFINITY) L = fmaf(exp2f(wm[ww][tid] - M), wl[ww][tid], L);
+    w[(g0 + tid) * (kD + 2) + kD] = M;
+    w[(g0 + tid) * (kD + 2) + kD + 1] = L;
   }
 }
 
@@ -243,6 +293,17 @@ __global__ void __launch_bounds__(kThreads) decode_merge_kernel(const __grid_con
     den = fmaf(f, w[s * step + kD + 1], den);
   }
   out[int64_t(b) * os_b + int64_t(h) * os_h + t] = __float2bfloat16_rn(den > 0.0f ? num / den : 0.0f);
+}
+
+template <int GM, int ITS>
+static int launch_split(dim3 grid, const Params &p, cudaStream_t stream) {
+  constexpr int smem = split_smem_bytes<ITS>();
+  static_assert(smem >= kWarps * GM * kD * 4, "the ring must hold the cross-warp sum");
+  int rc = ensure_func_smem(reinterpret_cast<const void *>(&decode_split_kernel<GM, ITS>), smem);
+  if (rc) return rc;
+  decode_split_kernel<GM, ITS><<<grid, kSplitThreads, smem, stream>>>(p);
+  FFTS_CUDA(cudaGetLastError());
+  return FFTS_OK;
 }
 
 }  // namespace decode
@@ -303,15 +364,17 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   const int G = int(H / Hkv);
   const dim3 grid(unsigned(B * Hkv), unsigned(nsplit), unsigned(ceil_div(int64_t(G), int64_t(kHeadsPerCta))));
   const int gm = std::min(G, kHeadsPerCta);
+  // chunks of 8 keys per warp (4 when a CTA holds 8 q-heads, for registers)
+  int rc = FFTS_OK;
   if (gm <= 1)
-    decode_split_kernel<1><<<grid, kSplitThreads, 0, stream>>>(p);
+    rc = launch_split<1, 4>(grid, p, stream);
   else if (gm <= 2)
-    decode_split_kernel<2><<<grid, kSplitThreads, 0, stream>>>(p);
+    rc = launch_split<2, 4>(grid, p, stream);
   else if (gm <= 4)
-    decode_split_kernel<4><<<grid, kSplitThreads, 0, stream>>>(p);
+    rc = launch_split<4, 4>(grid, p, stream);
   else
-    decode_split_kernel<8><<<grid, kSplitThreads, 0, stream>>>(p);
-  FFTS_CUDA(cudaGetLastError());
+    rc = launch_split<8, 2>(grid, p, stream);
+  if (rc) return rc;
   decode_merge_kernel<<<unsigned(B * H), kThreads, 0, stream>>>(p, static_cast<__nv_bfloat16 *>(out), os_b, os_h);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;

@@ -29,7 +29,8 @@
 //               the accumulator, round it to bf16 in registers (bias added in fp32
 //               first) and release TMEM at once, so the next tile's MMAs overlap
 //               the rest.  Per head and 64-channel box: RoPE against the cos/sin
-//               rows into a shared-memory box in the TMA SWIZZLE_128B layout, one
+//               rows (re-laid first by rope_tile_kernel so that a warp's 32 rows
+//               load a chunk in one coalesced access) into a shared-memory box in the TMA SWIZZLE_128B layout, one
 //               TMA tensor store of the box into the head-major output (rows past
 //               L dropped by the map), and the pooling, one thread per channel
 //               summing the box's rows of a block in order.
@@ -92,8 +93,7 @@ struct Params {
   __nv_bfloat16 *pooled[2];   // [B, Hq, N, D], [B, Hkv, N, D]
   __nv_bfloat16 *raw;         // optional [B, L, raw_ld] projection before RoPE
   int64_t raw_ld;
-  const __nv_bfloat16 *cos, *sin;
-  int64_t cs_ld;
+  const uint4 *rope;          // cos / sin re-laid by rope_tile_kernel (rope_tile_index)
   int L, N, Hq, Hkv, heads, bs;
   int kblocks;                // K steps of kBK
   int m_tiles, n_tiles, tiles;
@@ -141,6 +141,26 @@ __device__ __forceinline__ TileCoord tile_coord(const Params &p, int t) {
   c.mt = m % p.m_tiles;
   c.b = m / p.m_tiles;
   return c;
+}
+
+// The cos / sin tables re-laid so that the 32 rows of a warp read a 16-byte
+// chunk with one coalesced 512-byte access: uint4 [row / 32][16 chunks][cos, sin][row % 32],
+// rows past L zero.  (The caller's [L, 128] tables, read by row-per-thread lanes,
+// put 32 different rows in every load instruction.)
+__host__ __device__ __forceinline__ int64_t rope_tile_index(int64_t row, int chunk, int table) {
+  return (((row >> 5) * 16 + chunk) * 2 + table) * 32 + (row & 31);
+}
+
+__global__ void __launch_bounds__(256) rope_tile_kernel(const __nv_bfloat16 *__restrict__ cos,
+                                                        const __nv_bfloat16 *__restrict__ sin, int64_t cs_ld,
+                                                        int64_t L, int64_t rows, uint4 *__restrict__ out) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // output uint4 index
+  if (i >= rows * 32) return;
+  const int64_t row = (i >> 10) * 32 + (i & 31);
+  const int table = int((i >> 5) & 1), chunk = int((i >> 6) & 15);
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (row < L) v = *reinterpret_cast<const uint4 *>((table ? sin : cos) + row * cs_ld + chunk * 8);
+  out[i] = v;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -321,8 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int hr = role == 0 ? g : (role == 1 ? g - p.Hq : g - p.Hq - p.Hkv);
         const int hcount = role == 0 ? p.Hq : p.Hkv;
         const CUtensorMap *omap = role == 0 ? &tm_q : (role == 1 ? &tm_k : &tm_v);
-        const __nv_bfloat16 *crow = p.cos + int64_t(valid ? tl : 0) * p.cs_ld;
-        const __nv_bfloat16 *srow = p.sin + int64_t(valid ? tl : 0) * p.cs_ld;
+        const uint4 *rope = p.rope + rope_tile_index(tl, 0, 0);  // this row's chunk 0 of cos
 #pragma unroll
         for (int box = 0; box < 2; ++box) {
           // ---- this row's 64 channels [64 box, 64 box + 64), rotated for q / k, into
@@ -341,9 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) ow[e] = pk[wo + e];
             } else {
-              const int cc = 64 * box + 8 * c8;
-              const uint4 cv = *reinterpret_cast<const uint4 *>(crow + cc);
-              const uint4 sv = *reinterpret_cast<const uint4 *>(srow + cc);
+              const uint4 cv = rope[(8 * box + c8) * 64];       // cos, channels 64 box + 8 c8 ..
+              const uint4 sv = rope[(8 * box + c8) * 64 + 32];  // sin
               const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -445,10 +463,15 @@ __device__ int g_qkv_status_sink;
 
 }  // namespace qkv
 
+int64_t qkv_workspace_bytes(int64_t L) {
+  return L >= 1 ? ceil_div(L, 32) * 32 * qkv::kD * 2 * 2 : 0;  // cos and sin, rows padded to 32
+}
+
 int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, int64_t x_sb, const void *w,
                   int64_t w_ld, const void *bias, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
                   const void *sin, int64_t cs_ld, int bs, void *q_out, void *k_out, void *v_out, void *q_pooled,
-                  void *k_pooled, void *raw, int64_t raw_ld, int32_t *status, cudaStream_t stream) {
+                  void *k_pooled, void *raw, int64_t raw_ld, void *workspace, int64_t ws_bytes, int32_t *status,
+                  cudaStream_t stream) {
   using namespace qkv;
   FFTS_REQUIRE(x && w && cos && sin && q_out && k_out && v_out && q_pooled && k_pooled,
                "qkv_rope_pool: NULL argument");
@@ -463,6 +486,11 @@ int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, 
                    cs_ld >= D && (B == 1 || (x_sb % 8 == 0 && x_sb >= L * x_ld)),
                "qkv_rope_pool: K and the row strides must be multiples of 8 elements and cover their rows");
   FFTS_REQUIRE(!raw || (raw_ld % 8 == 0 && raw_ld >= heads * kD), "qkv_rope_pool: raw_ld too small or unaligned");
+  if (workspace == nullptr || ws_bytes < qkv_workspace_bytes(L) || (reinterpret_cast<uintptr_t>(workspace) & 15)) {
+    set_error(FFTS_E_WORKSPACE, "qkv_rope_pool: workspace needs %lld bytes, 16-byte aligned (got %lld)",
+              (long long)qkv_workspace_bytes(L), (long long)ws_bytes);
+    return FFTS_E_WORKSPACE;
+  }
   for (const void *ptr : {x, w, bias, cos, sin, (const void *)q_out, (const void *)k_out, (const void *)v_out,
                           (const void *)q_pooled, (const void *)k_pooled, (const void *)raw})
     FFTS_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "qkv_rope_pool: pointers must be 16-byte aligned");
@@ -480,9 +508,7 @@ int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, 
   p.pooled[1] = static_cast<__nv_bfloat16 *>(k_pooled);
   p.raw = static_cast<__nv_bfloat16 *>(raw);
   p.raw_ld = raw_ld;
-  p.cos = static_cast<const __nv_bfloat16 *>(cos);
-  p.sin = static_cast<const __nv_bfloat16 *>(sin);
-  p.cs_ld = cs_ld;
+  p.rope = static_cast<const uint4 *>(workspace);
   p.L = int(L);
   p.N = int(ceil_div(L, bs));
   p.Hq = int(Hq);
@@ -509,6 +535,11 @@ int qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t K, int64_t x_ld, 
   int sms = 0;
   rc = device_sm_count(&sms);
   if (rc) return rc;
+  const int64_t rope_rows = ceil_div(L, 32) * 32;
+  rope_tile_kernel<<<unsigned(ceil_div(rope_rows * 32, 256)), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(cos), static_cast<const __nv_bfloat16 *>(sin), cs_ld, L, rope_rows,
+      static_cast<uint4 *>(workspace));
+  FFTS_CUDA(cudaGetLastError());
   const unsigned grid = unsigned(p.tiles < sms ? p.tiles : sms);
   qkv_rope_pool_kernel<<<grid, kThreads, Smem::bytes, stream>>>(mx, mw, mq, mk, mv, p);
   FFTS_CUDA(cudaGetLastError());

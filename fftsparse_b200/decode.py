@@ -54,8 +54,10 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if k_cache.shape[0] != B or v_cache.shape != k_cache.shape or k_cache.shape[3] != D:
         raise ValueError(f"caches {tuple(k_cache.shape)} / {tuple(v_cache.shape)} do not match q {tuple(q.shape)}")
     if splits is None:
-        sms = _sm_count(q.device)
-        splits = max(1, min((Lk + 127) // 128, (4 * sms + B * Hkv - 1) // (B * Hkv)))
+        # one CTA per SM (the kernel's shared-memory rings hold one per SM): splits that
+        # fill the SMs once, each at least 64 keys
+        ctas = B * Hkv * ((H // Hkv + 7) // 8)
+        splits = max(1, min((Lk + 63) // 64, _sm_count(q.device) // ctas))
     if out is None:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=q.device)
     mask_ptr, mask_dt, mask_sb = None, 0, 0

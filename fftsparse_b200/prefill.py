@@ -183,12 +183,14 @@ def qkv_rope_pool(hidden: torch.Tensor, weight: torch.Tensor, bias: Optional[tor
         own.poll()
         status = own.word
     lib = _lib.load()
+    ws_bytes = int(lib.ffts_qkv_workspace_bytes(L))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     _lib.check(lib.ffts_qkv_rope_pool(
         hidden.data_ptr(), B, L, K, hidden.stride(1), hidden.stride(0), weight.data_ptr(), weight.stride(0),
         None if bias is None else bias.data_ptr(), num_heads, num_kv_heads, D, cos.data_ptr(), sin.data_ptr(),
         cos.stride(0), block_size, q.data_ptr(), k.data_ptr(), v.data_ptr(), qb.data_ptr(), kb.data_ptr(),
-        None if proj is None else proj.data_ptr(), 0 if proj is None else proj.stride(1), status.data_ptr(),
-        _stream_ptr(dev)))
+        None if proj is None else proj.data_ptr(), 0 if proj is None else proj.stride(1), ws.data_ptr(), ws_bytes,
+        status.data_ptr(), _stream_ptr(dev)))
     if own is not None:
         own.read_back()
     if return_projection:

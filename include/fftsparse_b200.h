@@ -149,6 +149,8 @@ FFTS_API int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_s
  *   q_out [B, Hq, L, D], k_out / v_out [B, Hkv, L, D]; q_pooled [B, Hq, N, D],
  *     k_pooled [B, Hkv, N, D], N = ceil(L / block_size), block_size 16..128.
  *   proj_out: NULL, or [B, L, proj_ld] receiving the bf16 projection before RoPE.
+ *   workspace: device memory of ffts_qkv_workspace_bytes(L) bytes, 16-byte aligned
+ *     (the cos / sin rows re-laid for coalesced loads); contents need not be kept.
  *   status: NULL or an int32 device word; a bounded wait that times out stores
  *     6 (copy producer), 7 (MMA issuer) or 8 (epilogue) and the outputs are
  *     invalid; 9 means the shared memory was misaligned and nothing ran.
@@ -160,7 +162,10 @@ FFTS_API int32_t ffts_qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t
                   const void *bias, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
                   const void *sin, int64_t cs_ld, int32_t block_size, void *q_out, void *k_out,
                   void *v_out, void *q_pooled, void *k_pooled, void *proj_out, int64_t proj_ld,
-                  int32_t *status, void *stream);
+                  void *workspace, int64_t workspace_bytes, int32_t *status, void *stream);
+
+/* Workspace bytes ffts_qkv_rope_pool needs for L tokens per sequence. */
+FFTS_API int64_t ffts_qkv_workspace_bytes(int64_t L);
 
 /*
  * Decode attention for one new token per sequence over the KV cache.  Replaces

@@ -121,3 +121,16 @@ def test_qkv_rope_pool_rejects_bad_arguments(F):
     w = torch.zeros(3 * D, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError):  # block_size 256 is outside what the epilogue pools
         F.qkv_rope_pool(x, w, None, 1, 1, cos, sin, 256)
+    # through the C ABI: a workspace smaller than ffts_qkv_workspace_bytes(L) is refused, nothing runs
+    from fftsparse_b200 import _lib
+    lib = _lib.load()
+    need = int(lib.ffts_qkv_workspace_bytes(256))
+    assert need == 256 * D * 2 * 2
+    outs = [torch.empty(1, 1, 256, D, dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    pooled = [torch.empty(1, 1, 2, D, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.ffts_qkv_rope_pool(x.data_ptr(), 1, 256, 128, 128, 256 * 128, w.data_ptr(), 128, None, 1, 1, D,
+                                cos.data_ptr(), sin.data_ptr(), D, 128, *[t.data_ptr() for t in outs],
+                                *[t.data_ptr() for t in pooled], None, 0, ws.data_ptr(), need - 16, None, stream)
+    assert rc == _lib.FFTS_E_WORKSPACE
