@@ -3,6 +3,7 @@
 Public surface (mirrors attn_src/fft_attn/my_attn_v7.py):
 
   myattn_prefill(q, k, v, layer_idx, ...)   drop-in for the reference operator
+  myattn_prefill_host(q, k, v, layer_idx)   the same on pinned host buffers, copies overlapped per head chunk
   fft_block_mask(q, k, ...)                 the selected block mask + statistics
   sparse_attention(q, k, v, bits, bs)       block-sparse attention on packed bits
   pool_blocks(x, bs)                        block mean pooling
@@ -21,6 +22,7 @@ from .prefill import (  # noqa: F401
     _attention_cache,
     fft_block_mask,
     myattn_prefill,
+    myattn_prefill_host,
     pool_blocks,
     qkv_rope_pool,
     rope_pool,

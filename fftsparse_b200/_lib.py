@@ -56,6 +56,7 @@ EXPORTS = {
     "ffts_ipc_open": (_I32, [_P, _I64, _P]),
     "ffts_ipc_close": (_I32, [_P, _I64]),
     "ffts_copy_rows": (_I32, [_P, _P, _I32, _P, _I64, _I64, _I64, _P]),
+    "ffts_copy_2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "ffts_signal": (_I32, [_P, _P, _I32, _I32]),
     "ffts_wait_flags": (_I32, [_P, _I32, _I32, _P, _P]),
 }

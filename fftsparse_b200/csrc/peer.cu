@@ -17,6 +17,8 @@
 //   ffts_copy_rows   one strided copy (height rows of width bytes, same pitch on
 //       both sides) to each of n destinations, copy i on stream i, each stream
 //       first waiting for an event (the chunk's attention) when one is given;
+//   ffts_copy_2d     one pitched copy in any direction (host <-> device), for
+//       the host-buffer prefill's per-chunk read-back of its head columns;
 //   ffts_signal      a small kernel storing an epoch number into flags with
 //       release semantics at system scope, flag i queued on stream i after the
 //       copies there (one launch per run of flags that share a stream);
@@ -117,6 +119,15 @@ FFTS_API int32_t ffts_ipc_open(const void *handle, int64_t offset, void **ptr) {
 FFTS_API int32_t ffts_ipc_close(void *ptr, int64_t offset) {
   FFTS_REQUIRE(ptr && offset >= 0, "ipc_close: bad argument");
   FFTS_CUDA(cudaIpcCloseMemHandle(static_cast<char *>(ptr) - offset));
+  return FFTS_OK;
+}
+
+FFTS_API int32_t ffts_copy_2d(void *dst, int64_t dst_pitch, const void *src, int64_t src_pitch, int64_t width,
+                              int64_t height, void *stream) {
+  FFTS_REQUIRE(dst && src && width > 0 && height > 0 && dst_pitch >= width && src_pitch >= width,
+               "copy_2d: bad argument");
+  FFTS_CUDA(cudaMemcpy2DAsync(dst, size_t(dst_pitch), src, size_t(src_pitch), size_t(width), size_t(height),
+                              cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
   return FFTS_OK;
 }
 

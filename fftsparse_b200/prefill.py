@@ -36,7 +36,7 @@ from . import _lib
 from .params import SEL_TOPK, derive_mask_params, MaskParams
 from .status import device_status
 
-__all__ = ["myattn_prefill", "fft_block_mask", "sparse_attention", "pool_blocks", "BlockMask",
+__all__ = ["myattn_prefill", "myattn_prefill_host", "fft_block_mask", "sparse_attention", "pool_blocks", "BlockMask",
            "AttentionCache", "_attention_cache"]
 
 
@@ -502,3 +502,82 @@ def myattn_prefill(
 
     out = sparse_attention(q, k, v, mask.bits, block_size, causal=is_causal)
     return out.view(B, L, H * D)
+
+
+_HOST_STREAMS = {}
+
+
+def _host_streams(device: torch.device):
+    """(copy-in stream, copy-out stream) of ``device``, created once."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _HOST_STREAMS:
+        _HOST_STREAMS[idx] = (torch.cuda.Stream(idx), torch.cuda.Stream(idx))
+    return _HOST_STREAMS[idx]
+
+
+def myattn_prefill_host(query_states, key_states, value_states, layer_idx, chunk_heads: int = 4,
+                        out: Optional[torch.Tensor] = None, device=None, **kwargs):
+    """``myattn_prefill`` on host buffers, with the copies overlapped with the work.
+
+    query_states [B, H, L, D] and key_states / value_states [B, H or Hkv, L, D]
+    are CPU tensors (pinned for the copies to overlap); ``kwargs`` are
+    myattn_prefill's.  Returns ``out``, a pinned CPU [B, L, H*D] bf16 tensor
+    (allocated when None), equal bit for bit to myattn_prefill on the same inputs
+    on the device: the selection and the attention of a head read only that head
+    (and its KV head).  Heads go in chunks of ``chunk_heads`` (a multiple of the
+    group size H / Hkv): chunk c+1 is copied in on one stream while chunk c is
+    selected and attended on the current stream and chunk c-1's output columns
+    are copied back on a third, so the layer takes about as long as its input
+    copy.  The call returns once the work is queued; the result is complete when
+    the current stream's work is (``torch.cuda.current_stream().synchronize()``).
+    The calibration collector, when installed, records one entry per chunk.
+    """
+    q_h, k_h, v_h = query_states, key_states, value_states
+    for name, t in (("query_states", q_h), ("key_states", k_h), ("value_states", v_h)):
+        if t.is_cuda or t.dim() != 4:
+            raise ValueError(f"{name} must be a 4-D CPU tensor (use myattn_prefill for device tensors)")
+    B, H, L, D = q_h.shape
+    Hkv = k_h.shape[1]
+    if H % Hkv or v_h.shape != k_h.shape or k_h.shape[0] != B or k_h.shape[2] != L or k_h.shape[3] != D:
+        raise ValueError(f"key/value {tuple(k_h.shape)} / {tuple(v_h.shape)} incompatible with query {tuple(q_h.shape)}")
+    G = H // Hkv
+    hc = max(G, (chunk_heads // G) * G)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if out is None:
+        out = torch.empty(B, L, H * D, dtype=q_h.dtype, pin_memory=True)
+    elif out.shape != (B, L, H * D) or out.is_cuda or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous CPU tensor of shape {(B, L, H * D)}")
+    lib = _lib.load()
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = _host_streams(dev)
+    s_in.wait_stream(comp)  # device buffers allocated below belong to the current stream's order
+    q_d = torch.empty(B, H, L, D, dtype=q_h.dtype, device=dev)
+    k_d = torch.empty(B, Hkv, L, D, dtype=k_h.dtype, device=dev)
+    v_d = torch.empty(B, Hkv, L, D, dtype=v_h.dtype, device=dev)
+    chunks = [(h0, min(H, h0 + hc)) for h0 in range(0, H, hc)]
+    arrived = []
+    with torch.cuda.stream(s_in):
+        for h0, h1 in chunks:
+            for b in range(B):  # each [b, h0:h1] slice is contiguous on both sides
+                q_d[b, h0:h1].copy_(q_h[b, h0:h1], non_blocking=True)
+                k_d[b, h0 // G:h1 // G].copy_(k_h[b, h0 // G:h1 // G], non_blocking=True)
+                v_d[b, h0 // G:h1 // G].copy_(v_h[b, h0 // G:h1 // G], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+            arrived.append(ev)
+    row = H * D * out.element_size()
+    for (h0, h1), ev in zip(chunks, arrived):
+        comp.wait_event(ev)
+        o = myattn_prefill(q_d[:, h0:h1], k_d[:, h0 // G:h1 // G], v_d[:, h0 // G:h1 // G], layer_idx, **kwargs)
+        done = torch.cuda.Event()
+        done.record(comp)
+        s_out.wait_event(done)
+        o.record_stream(s_out)
+        width = (h1 - h0) * D * out.element_size()
+        for b in range(B):
+            _lib.check(lib.ffts_copy_2d(out[b].data_ptr() + h0 * D * out.element_size(), row,
+                                        o[b].data_ptr(), width, width, L, s_out.cuda_stream))
+    for t in (q_d, k_d, v_d):
+        t.record_stream(s_in)
+    comp.wait_stream(s_out)  # the current stream's completion covers the read-back
+    return out

@@ -328,6 +328,17 @@ FFTS_API int32_t ffts_sparse_attn_fwd_push(const void *q, const void *k, const v
                              int32_t *status, void *stream);
 
 /*
+ * One pitched copy (cudaMemcpy2DAsync, any direction): height rows of width
+ * bytes from src (rows src_pitch bytes apart) to dst (rows dst_pitch apart) on
+ * stream.  No counterpart in the reference, whose operator takes device tensors
+ * only: fftsparse_b200.myattn_prefill_host uses it to read each head chunk's
+ * output columns back into the caller's [B, L, H*D] host buffer while later
+ * chunks are copied in and computed.
+ */
+FFTS_API int32_t ffts_copy_2d(void *dst, int64_t dst_pitch, const void *src, int64_t src_pitch, int64_t width,
+                  int64_t height, void *stream);
+
+/*
  * Copy-engine all-gather support for the sharded prefill (fftsparse_b200/dist.py,
  * PeerGather).  No counterpart in the reference, which runs on one GPU: a rank
  * maps its peers' output buffers (CUDA IPC), pushes each finished row chunk of

@@ -204,3 +204,56 @@ def test_push_to_peer_buffers_equals_own_output(lib):
     assert int(status.item()) == 0
     with pytest.raises(ValueError):
         lib.sparse_attention(q, k, v, bits, bs, peers=[0])  # a NULL peer buffer
+
+
+@pytest.mark.parametrize("L,H,Hkv,bs", [(8000, 4, 2, 128), (6000, 4, 4, 64)])
+def test_selected_mask_matches_flash_attn_on_gathered_blocks(lib, L, H, Hkv, bs):
+    """Pins the sparse attention with a selected FFTSparse mask to flash_attn, the
+    library behind the reference's block_sparse_attn_func.  Each (head, query
+    block) becomes one varlen sequence whose keys are its kept key blocks gathered
+    in ascending order: the diagonal block is always kept and comes last, so
+    flash_attn's bottom-right causal alignment masks exactly the causal part of
+    it.  Same bf16 tolerance as the fp32 comparisons."""
+    try:
+        from flash_attn import flash_attn_varlen_func
+    except Exception as exc:  # noqa: BLE001 - any import failure means the wheel is unusable here
+        pytest.skip(f"flash_attn cannot be imported: {exc}")
+    import bench
+    g = torch.Generator().manual_seed(L + bs)
+    q = torch.randn(1, H, L, 128, generator=g).bfloat16().cuda()
+    k = torch.randn(1, Hkv, L, 128, generator=g).bfloat16().cuda()
+    v = torch.randn(1, Hkv, L, 128, generator=g).bfloat16().cuda()
+    mask = lib.fft_block_mask(q, k, **dict(bench.mask_kwargs(0.1), block_size=bs))
+    row_ptr, col_idx = (t.cpu() for t in mask.csr())
+    out = lib.sparse_attention(q, k, v, mask.bits, bs)  # [1, L, H, D]
+    N, G = mask.n_blocks, H // Hkv
+    qi, ki, cu_q, cu_k, heads_q, heads_k = [], [], [0], [0], [], []
+    for h in range(H):
+        for i in range(N):
+            r = h * N + i
+            sel = col_idx[row_ptr[r]:row_ptr[r + 1]].long()
+            sel = sel[sel <= i]  # the kernel cuts blocks above the diagonal
+            assert int(sel[-1]) == i, "the diagonal block is always kept"
+            rows = torch.arange(i * bs, min((i + 1) * bs, L))
+            keys = torch.cat([torch.arange(j * bs, min((j + 1) * bs, L)) for j in sel.tolist()])
+            qi.append(rows)
+            ki.append(keys)
+            heads_q.append(torch.full_like(rows, h))
+            heads_k.append(torch.full_like(keys, h // G))
+            cu_q.append(cu_q[-1] + rows.numel())
+            cu_k.append(cu_k[-1] + keys.numel())
+    qi, ki = torch.cat(qi).cuda(), torch.cat(ki).cuda()
+    hq, hk = torch.cat(heads_q).cuda(), torch.cat(heads_k).cuda()
+    qg = q[0][hq, qi].unsqueeze(1)  # [total_q, 1, D]
+    kg, vg = k[0][hk, ki].unsqueeze(1), v[0][hk, ki].unsqueeze(1)
+    cq = torch.tensor(cu_q, dtype=torch.int32, device="cuda")
+    ck = torch.tensor(cu_k, dtype=torch.int32, device="cuda")
+    try:
+        ref = flash_attn_varlen_func(qg, kg, vg, cq, ck, bs, max(b - a for a, b in zip(cu_k, cu_k[1:])),
+                                     causal=True)
+    except RuntimeError as exc:
+        pytest.skip(f"flash_attn has no kernel for this GPU: {exc}")
+    got = out[0][qi, hq]  # [total_q, D] in the same (head, block, row) order
+    err = (got.float() - ref[:, 0].float()).abs()
+    assert float(err.max()) <= MAX_ABS, float(err.max())
+    assert float(err.mean()) <= MEAN_ABS, float(err.mean())

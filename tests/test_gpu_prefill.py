@@ -116,3 +116,24 @@ def test_config5_shape(lib):
             sl = slice(i * 64, (i + 1) * 64)
             err = (got[:, h, sl] - exp[:, h, sl]).abs()
             assert float(err.max()) <= 2e-2 and float(err.mean()) <= 1e-3, (h, i, float(err.max()))
+
+
+@pytest.mark.parametrize("Hkv,chunk", [(8, 4), (2, 3)])
+def test_host_buffers_equal_device_call(lib, Hkv, chunk):
+    """myattn_prefill_host on pinned host q/k/v (expanded and GQA k/v; a chunk size
+    that is not a multiple of the group rounds down to whole groups) returns the
+    device call's output bit for bit, on two calls in a row."""
+    import bench
+    g = torch.Generator().manual_seed(Hkv)
+    B, H, L, D = 1, 8, 16384, 128
+    q = torch.randn(B, H, L, D, generator=g).bfloat16().pin_memory()
+    k = torch.randn(B, Hkv, L, D, generator=g).bfloat16().pin_memory()
+    v = torch.randn(B, Hkv, L, D, generator=g).bfloat16().pin_memory()
+    kw = bench.mask_kwargs(0.1)
+    ref = lib.myattn_prefill(q.cuda(), k.cuda(), v.cuda(), 0, **kw).cpu()
+    for _ in range(2):
+        got = lib.myattn_prefill_host(q, k, v, 0, chunk_heads=chunk, **kw)
+        torch.cuda.current_stream().synchronize()
+        assert torch.equal(got, ref)
+    with pytest.raises(ValueError):
+        lib.myattn_prefill_host(q.cuda(), k, v, 0)
