@@ -99,10 +99,13 @@ constexpr int split_smem_bytes() {
 // warps never wait for one another until the end of the split.  A warp's K and
 // V rows stream through its own kStages-deep cp.async ring: a half-warp copies
 // one 256-byte row (lane = 16 bytes, 8 channels) and later reads back exactly
-// the bytes it copied, so no cross-lane barrier is needed.  Per chunk: the G
-// dot products of a row are reduced over the half-warp's 16 lanes; the chunk's
-// maximum and exponential sum combine the two halves; each lane accumulates P V
-// for its 8 channels.  At the end the halves, then the warps (rescaled to the
+// the bytes it copied, so no cross-lane barrier is needed.  Per chunk: the GM
+// dot products of a row are reduced over the half-warp's 16 lanes together
+// (log2 GM halving exchanges leave each lane one head's score, 5 shuffles for
+// 4 heads where one reduction per head would take 16); that lane runs the head's
+// online softmax; each lane then accumulates P V for its 8 channels and every
+// head, with the heads' p and rescale factors taken from their lanes, in paired
+// fp32 FMAs.  At the end the halves, then the warps (rescaled to the
 // CTA's maximum) are summed into the split's (o, m, l) per head.
 template <int GM, int ITS>
 __global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __grid_constant__ Params p) {
@@ -121,29 +124,35 @@ __global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __
   const int half = lane >> 4, seg = lane & 15;
   const int k0 = split * p.per_split;
   const int k1 = min(p.Lk, k0 + p.per_split);
-  // q of this CTA's heads for the lane's 8 channels, pre-multiplied by scale * log2(e)
-  float qr[GM][8];
+  // q of this CTA's heads for the lane's 8 channels (as 4 pairs), pre-multiplied by scale * log2(e)
+  float2 q2[GM][4];
 #pragma unroll
   for (int g = 0; g < GM; ++g) {
+    float f[8];
     if (g < ng) {
       const uint4 raw = *reinterpret_cast<const uint4 *>(p.q + int64_t(b) * p.qs_b +
                                                          int64_t(kvh * G + g0 + g) * p.qs_h + seg * 8);
-      widen8(raw, qr[g]);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) qr[g][e] *= p.scale_log2;
+      widen8(raw, f);
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) qr[g][e] = 0.0f;
+      for (int e = 0; e < 8; ++e) f[e] = 0.0f;
     }
-  }
-  float m[GM], l[GM], acc[GM][8];
 #pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+    for (int j = 0; j < 4; ++j) q2[g][j] = make_float2(f[2 * j] * p.scale_log2, f[2 * j + 1] * p.scale_log2);
   }
+  // After the reduction below, lane seg of each half holds the score of head hl
+  // (the sums of the GM heads are split over the 16 lanes, LG = log2(GM) bits of
+  // seg); that lane keeps the running max m and sum l of head hl, the same in
+  // every lane of the head and in both halves.
+  constexpr int LG = GM == 1 ? 0 : (GM == 2 ? 1 : (GM == 4 ? 2 : 3));
+  const int hl = LG ? (seg >> (4 - LG)) : 0;
+  const bool head_ok = hl < ng;
+  float m = -INFINITY, l = 0.0f;
+  float2 acc[GM][4];
+#pragma unroll
+  for (int g = 0; g < GM; ++g)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[g][j] = make_float2(0.0f, 0.0f);
   const __nv_bfloat16 *kb = p.k + int64_t(b) * p.ks_b + int64_t(kvh) * p.ks_h + seg * 8;
   const __nv_bfloat16 *vb = p.v + int64_t(b) * p.vs_b + int64_t(kvh) * p.vs_h + seg * 8;
   const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(dsm)) + uint32_t(warp * kStages * kSlot);
@@ -177,54 +186,79 @@ __global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __
     const uint8_t *slot = ring_p + (j % kStages) * kSlot + lane_off;
     const int base = k0 + (warp + kWarps * j) * R;
     // ---- scores of the chunk's rows (this half's rows: 2 * it + half)
-    float sc[GM][ITS];
+    float sc[ITS];
 #pragma unroll
     for (int it = 0; it < ITS; ++it) {
       const int row = base + 2 * it + half;
       float kf[8];
       widen8(*reinterpret_cast<const uint4 *>(slot + 2 * it * kRowBytes), kf);
-      const float bl = row < k1 ? bias_log2(p, b, row) : 0.0f;
+      float part[GM];
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
-        float part = 0.0f;
+        float2 a = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) part = fmaf(qr[g][e], kf[e], part);
-#pragma unroll
-        for (int o = 8; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        sc[g][it] = row < k1 ? part + bl : -INFINITY;
+        for (int j = 0; j < 4; ++j) a = __ffma2_rn(q2[g][j], make_float2(kf[2 * j], kf[2 * j + 1]), a);
+        part[g] = a.x + a.y;
       }
+      // reduce the GM partial sums over the 16 lanes together: while more than one
+      // value is held, each exchange step keeps the lower or upper half of the heads
+      // (by the lane's bit) and adds the partner's share of them
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        const int mask = 8 >> st;
+        const int n = GM >> st;
+        if (n >= 2) {
+          const bool up = (seg & mask) != 0;
+#pragma unroll
+          for (int jj = 0; jj < GM / 2; ++jj) {
+            if (jj < n / 2) {
+              const float send = up ? part[jj] : part[jj + n / 2];
+              const float keep = up ? part[jj + n / 2] : part[jj];
+              part[jj] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+            }
+          }
+        } else {
+          part[0] += __shfl_xor_sync(0xffffffffu, part[0], mask);
+        }
+      }
+      const float bl = row < k1 ? bias_log2(p, b, row) : 0.0f;
+      sc[it] = (row < k1 && head_ok) ? part[0] + bl : -INFINITY;
     }
-    // ---- online softmax over the chunk (both halves agree on m and l)
-    float pr[GM][ITS];
+    // ---- online softmax of head hl over the chunk (the halves combine)
+    float mx = sc[0];
+#pragma unroll
+    for (int it = 1; it < ITS; ++it) mx = fmaxf(mx, sc[it]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float m_new = fmaxf(m, mx);
+    const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m - m_new);
+    float pr[ITS];
+    float sum = 0.0f;
+#pragma unroll
+    for (int it = 0; it < ITS; ++it) {
+      pr[it] = m_new == -INFINITY ? 0.0f : exp2f(sc[it] - m_new);
+      sum += pr[it];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+    l = l * alpha + sum;
+    m = m_new;
+    // ---- P V for the lane's 8 channels, every head: alpha and p from the head's lanes
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
-      float mx = sc[g][0];
+      const float ag = __shfl_sync(0xffffffffu, alpha, g << (4 - LG));
 #pragma unroll
-      for (int it = 1; it < ITS; ++it) mx = fmaxf(mx, sc[g][it]);
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-      const float m_new = fmaxf(m[g], mx);
-      const float alpha = m_new == -INFINITY ? 1.0f : exp2f(m[g] - m_new);
-      float sum = 0.0f;
-#pragma unroll
-      for (int it = 0; it < ITS; ++it) {
-        pr[g][it] = m_new == -INFINITY ? 0.0f : exp2f(sc[g][it] - m_new);
-        sum += pr[g][it];
-      }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-      l[g] = l[g] * alpha + sum;
-      m[g] = m_new;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
+      for (int j = 0; j < 4; ++j) acc[g][j] = __fmul2_rn(acc[g][j], make_float2(ag, ag));
     }
-    // ---- P V for the lane's 8 channels
 #pragma unroll
     for (int it = 0; it < ITS; ++it) {
       float vf[8];
       widen8(*reinterpret_cast<const uint4 *>(slot + (R + 2 * it) * kRowBytes), vf);
 #pragma unroll
-      for (int g = 0; g < GM; ++g)
+      for (int g = 0; g < GM; ++g) {
+        const float pg = __shfl_sync(0xffffffffu, pr[it], (half << 4) | (g << (4 - LG)));
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(pr[g][it], vf[e], acc[g][e]);
+        for (int j = 0; j < 4; ++j)
+          acc[g][j] = __ffma2_rn(make_float2(pg, pg), make_float2(vf[2 * j], vf[2 * j + 1]), acc[g][j]);
+      }
     }
   }
   cp_async_wait<0>();
@@ -232,20 +266,26 @@ __global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __
 #pragma unroll
   for (int g = 0; g < GM; ++g)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], 16);
+    for (int j = 0; j < 4; ++j) {
+      acc[g][j].x += __shfl_xor_sync(0xffffffffu, acc[g][j].x, 16);
+      acc[g][j].y += __shfl_xor_sync(0xffffffffu, acc[g][j].y, 16);
+    }
   __syncthreads();  // every warp is done with its ring: reuse it for the cross-warp sum
   float *red = reinterpret_cast<float *>(dsm);  // [kWarps][GM][kD]
   if (half == 0) {
 #pragma unroll
     for (int g = 0; g < GM; ++g)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) red[(warp * GM + g) * kD + seg * 8 + e] = acc[g][e];
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float2 *>(red + (warp * GM + g) * kD + seg * 8 + 2 * j) = acc[g][j];
   }
-  if (lane == 0) {
 #pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      wm[warp][g] = m[g];
-      wl[warp][g] = l[g];
+  for (int g = 0; g < GM; ++g) {
+    const float mg = __shfl_sync(0xffffffffu, m, g << (4 - LG));
+    const float lgs = __shfl_sync(0xffffffffu, l, g << (4 - LG));
+    if (lane == 0) {
+      wm[warp][g] = mg;
+      wl[warp][g] = lgs;
     }
   }
   __syncthreads();
