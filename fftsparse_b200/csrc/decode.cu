@@ -8,7 +8,7 @@
 //
 // decode_split_kernel: CTA = (b, kv head, split of the keys, up to 8 q-heads
 // of the group); 256 threads, one CTA per SM.  The split's keys are cut into
-// chunks of 8 rows (4 when the CTA holds 8 heads); warp w takes chunks w, w + 8,
+// chunks of 8 rows; warp w takes chunks w, w + 8,
 // ... and streams their K and V rows through its own 4-stage cp.async ring, so
 // about 96 KB of cache per SM is in flight and no CTA-wide barrier interrupts
 // the stream:
@@ -404,7 +404,7 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   const int G = int(H / Hkv);
   const dim3 grid(unsigned(B * Hkv), unsigned(nsplit), unsigned(ceil_div(int64_t(G), int64_t(kHeadsPerCta))));
   const int gm = std::min(G, kHeadsPerCta);
-  // chunks of 8 keys per warp (4 when a CTA holds 8 q-heads, for registers)
+  // chunks of 8 keys per warp
   int rc = FFTS_OK;
   if (gm <= 1)
     rc = launch_split<1, 4>(grid, p, stream);
@@ -413,7 +413,7 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   else if (gm <= 4)
     rc = launch_split<4, 4>(grid, p, stream);
   else
-    rc = launch_split<8, 2>(grid, p, stream);
+    rc = launch_split<8, 4>(grid, p, stream);
   if (rc) return rc;
   decode_merge_kernel<<<unsigned(B * H), kThreads, 0, stream>>>(p, static_cast<__nv_bfloat16 *>(out), os_b, os_h);
   FFTS_CUDA(cudaGetLastError());
