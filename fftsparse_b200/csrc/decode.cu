@@ -7,11 +7,11 @@
 // all G q-heads of its group: HBM-bound at 2 * B * Hkv * Lk * D * 2 bytes.
 //
 // decode_split_kernel: CTA = (b, kv head, split of the keys, up to 8 q-heads
-// of the group); 256 threads, one CTA per SM.  The split's keys are cut into
-// chunks of 8 rows; warp w takes chunks w, w + 8,
-// ... and streams their K and V rows through its own 4-stage cp.async ring, so
-// about 96 KB of cache per SM is in flight and no CTA-wide barrier interrupts
-// the stream:
+// of the group); 256 threads; two CTAs per SM with 3-stage rings when a CTA
+// holds up to 4 heads, one with 4 stages for 8 heads (registers).  The split's
+// keys are cut into chunks of 8 rows; warp w takes chunks w, w + 8, ... and
+// streams their K and V rows through its own cp.async ring, so about 128 KB of
+// cache per SM is in flight and no CTA-wide barrier interrupts the stream:
 //   scores   a half-warp per key row (lane = 8 channels, 16 bytes), q of the
 //            heads in registers; fp32 dot products reduced over the 16 lanes,
 //            in log2 units;
@@ -65,7 +65,6 @@ __device__ __forceinline__ float bias_log2(const Params &p, int b, int key) {
 
 constexpr int kSplitThreads = 256;  // 8 warps, each walking its own chunks of keys
 constexpr int kWarps = kSplitThreads / 32;
-constexpr int kStages = 4;          // cp.async ring depth per warp
 constexpr int kHeadsPerCta = 8;     // q-heads of one group per CTA (groups of up to 16 take two CTAs)
 
 __device__ __forceinline__ void widen8(const uint4 &raw, float *f) {
@@ -85,11 +84,11 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Dynamic shared memory of decode_split_kernel<GM, ITS>: every warp's ring of
-// kStages chunks, K rows then V rows of 2 * ITS keys (256 bytes each).
-template <int ITS>
+// Dynamic shared memory of decode_split_kernel<GM, ITS, NS, MINB>: every warp's
+// ring of NS chunks, K rows then V rows of 2 * ITS keys (256 bytes each).
+template <int ITS, int NS>
 constexpr int split_smem_bytes() {
-  return kWarps * kStages * 2 * (2 * ITS) * kD * 2;
+  return kWarps * NS * 2 * (2 * ITS) * kD * 2;
 }
 
 // CTA = (b, kv head, split of the keys, block of up to 8 q-heads of the group);
@@ -107,8 +106,8 @@ constexpr int split_smem_bytes() {
 // head, with the heads' p and rescale factors taken from their lanes, in paired
 // fp32 FMAs.  At the end the halves, then the warps (rescaled to the
 // CTA's maximum) are summed into the split's (o, m, l) per head.
-template <int GM, int ITS>
-__global__ void __launch_bounds__(kSplitThreads, 1) decode_split_kernel(const __grid_constant__ Params p) {
+template <int GM, int ITS, int kStages, int MINB>
+__global__ void __launch_bounds__(kSplitThreads, MINB) decode_split_kernel(const __grid_constant__ Params p) {
   constexpr int R = 2 * ITS;
   constexpr int kRowBytes = kD * 2;
   constexpr int kSlot = 2 * R * kRowBytes;  // K rows, then V rows
@@ -335,13 +334,15 @@ __global__ void __launch_bounds__(kThreads) decode_merge_kernel(const __grid_con
   out[int64_t(b) * os_b + int64_t(h) * os_h + t] = __float2bfloat16_rn(den > 0.0f ? num / den : 0.0f);
 }
 
-template <int GM, int ITS>
+template <int GM, int ITS, int NS, int MINB>
 static int launch_split(dim3 grid, const Params &p, cudaStream_t stream) {
-  constexpr int smem = split_smem_bytes<ITS>();
+  constexpr int smem = split_smem_bytes<ITS, NS>();
   static_assert(smem >= kWarps * GM * kD * 4, "the ring must hold the cross-warp sum");
-  int rc = ensure_func_smem(reinterpret_cast<const void *>(&decode_split_kernel<GM, ITS>), smem);
+  static_assert(MINB * (smem + 2048) <= 228 * 1024, "the CTAs of an SM must fit its shared memory");
+  int rc = ensure_func_smem(reinterpret_cast<const void *>(&decode_split_kernel<GM, ITS, NS, MINB>), smem,
+                           int(cudaSharedmemCarveoutMaxShared));
   if (rc) return rc;
-  decode_split_kernel<GM, ITS><<<grid, kSplitThreads, smem, stream>>>(p);
+  decode_split_kernel<GM, ITS, NS, MINB><<<grid, kSplitThreads, smem, stream>>>(p);
   FFTS_CUDA(cudaGetLastError());
   return FFTS_OK;
 }
@@ -406,14 +407,15 @@ int decode_attn(const void *q, int64_t qs_b, int64_t qs_h, const void *k, const 
   const int gm = std::min(G, kHeadsPerCta);
   // chunks of 8 keys per warp
   int rc = FFTS_OK;
+  // up to 4 heads per CTA: two CTAs per SM with 3-stage rings; 8 heads: one, 4 stages
   if (gm <= 1)
-    rc = launch_split<1, 4>(grid, p, stream);
+    rc = launch_split<1, 4, 3, 2>(grid, p, stream);
   else if (gm <= 2)
-    rc = launch_split<2, 4>(grid, p, stream);
+    rc = launch_split<2, 4, 3, 2>(grid, p, stream);
   else if (gm <= 4)
-    rc = launch_split<4, 4>(grid, p, stream);
+    rc = launch_split<4, 4, 3, 2>(grid, p, stream);
   else
-    rc = launch_split<8, 4>(grid, p, stream);
+    rc = launch_split<8, 4, 4, 1>(grid, p, stream);
   if (rc) return rc;
   decode_merge_kernel<<<unsigned(B * H), kThreads, 0, stream>>>(p, static_cast<__nv_bfloat16 *>(out), os_b, os_h);
   FFTS_CUDA(cudaGetLastError());

@@ -54,10 +54,12 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     if k_cache.shape[0] != B or v_cache.shape != k_cache.shape or k_cache.shape[3] != D:
         raise ValueError(f"caches {tuple(k_cache.shape)} / {tuple(v_cache.shape)} do not match q {tuple(q.shape)}")
     if splits is None:
-        # one CTA per SM (the kernel's shared-memory rings hold one per SM): splits that
-        # fill the SMs once, each at least 64 keys
-        ctas = B * Hkv * ((H // Hkv + 7) // 8)
-        splits = max(1, min((Lk + 63) // 64, _sm_count(q.device) // ctas))
+        # splits that fill the SMs once (two CTAs per SM when a CTA holds at most 4
+        # q-heads, else one: the kernel's shared-memory rings), each at least 64 keys
+        G = H // Hkv
+        per_sm = 2 if G <= 4 else 1
+        ctas = B * Hkv * ((G + 7) // 8)
+        splits = max(1, min((Lk + 63) // 64, per_sm * _sm_count(q.device) // ctas))
     if out is None:
         out = torch.empty(B, H, D, dtype=torch.bfloat16, device=q.device)
     mask_ptr, mask_dt, mask_sb = None, 0, 0
