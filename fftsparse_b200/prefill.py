@@ -533,6 +533,8 @@ def myattn_prefill_host(query_states, key_states, value_states, layer_idx, chunk
     The calibration collector, when installed, records one entry per chunk.
     """
     q_h, k_h, v_h = query_states, key_states, value_states
+    if kwargs.get("pooled") is not None:
+        raise ValueError("myattn_prefill_host pools per head chunk itself; it takes no pooled=")
     for name, t in (("query_states", q_h), ("key_states", k_h), ("value_states", v_h)):
         if t.is_cuda or t.dim() != 4:
             raise ValueError(f"{name} must be a 4-D CPU tensor (use myattn_prefill for device tensors)")

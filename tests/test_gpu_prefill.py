@@ -137,3 +137,5 @@ def test_host_buffers_equal_device_call(lib, Hkv, chunk):
         assert torch.equal(got, ref)
     with pytest.raises(ValueError):
         lib.myattn_prefill_host(q.cuda(), k, v, 0)
+    with pytest.raises(ValueError):
+        lib.myattn_prefill_host(q, k, v, 0, pooled=(q, k))
