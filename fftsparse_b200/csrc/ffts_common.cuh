@@ -102,6 +102,21 @@ __device__ inline void widen_vec<__nv_bfloat16>(const uint4 &v, float *out) {
   }
 }
 
+// Packed bf16 pairs in 32-bit registers: multiply and add with one
+// round-to-nearest-even each (PTX mul.rn.bf16x2 / add.rn.bf16x2), and exact
+// negation (sign bits flipped).
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_neg(uint32_t a) { return a ^ 0x80008000u; }
+
 // Monotone 32-bit key of a float: larger value -> larger key; -0 maps to +0.
 __device__ __forceinline__ uint32_t f32_key(float f) {
   if (f == 0.0f) f = 0.0f;

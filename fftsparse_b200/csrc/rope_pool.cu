@@ -12,7 +12,8 @@
 //
 // Arithmetic (bit-identical to the torch expression, then to pool_kernel): per
 // element a = bf16(x * cos), b = bf16(r * sin) with r = -x[d + D/2] (d < D/2) or
-// x[d - D/2], out = bf16(a + b), every operation in fp32 with round-to-nearest;
+// x[d - D/2], out = bf16(a + b), every operation in fp32 with round-to-nearest
+// (evaluated as packed bf16 multiplies and adds, which round the same way);
 // the pooled value of a channel is the fp32 sum of the block's rotated bf16
 // values in row order from +0, divided by block_size and rounded to bf16.
 //
@@ -42,8 +43,6 @@ struct Args {
   int64_t L, N;
   int Hq, Hkv, bs;
 };
-
-__device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __device__ __forceinline__ void unpack8(const uint4 &w, float *f) {
   const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(&w);
@@ -130,23 +129,28 @@ __global__ void __launch_bounds__(256, 2) rope_pool_kernel(const __grid_constant
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       if (r0 + u < rows) {
-        float x1[8], x2[8], c1[8], c2[8], s1[8], s2[8], o1[8], o2[8];
-        unpack8(xl[u], x1);
-        unpack8(xh[u], x2);
-        unpack8(cl[u], c1);
-        unpack8(ch[u], c2);
-        unpack8(sl[u], s1);
-        unpack8(sh[u], s2);
+        // packed bf16 arithmetic: a bf16 x bf16 product is exact in fp32, so
+        // mul.rn.bf16x2 rounds it once exactly as bf(x * c) does; the sum of two
+        // bf16 values rounds in add.rn.bf16x2 as bf(a + b) does (exact in fp32
+        // when their exponents are within 16, else the larger value is the result
+        // both ways)
+        const uint32_t xa[4] = {xl[u].x, xl[u].y, xl[u].z, xl[u].w}, xb[4] = {xh[u].x, xh[u].y, xh[u].z, xh[u].w};
+        const uint32_t ca[4] = {cl[u].x, cl[u].y, cl[u].z, cl[u].w}, cb[4] = {ch[u].x, ch[u].y, ch[u].z, ch[u].w};
+        const uint32_t sa[4] = {sl[u].x, sl[u].y, sl[u].z, sl[u].w}, sb[4] = {sh[u].x, sh[u].y, sh[u].z, sh[u].w};
+        uint32_t o1[4], o2[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          o1[e] = bf(__fadd_rn(bf(__fmul_rn(x1[e], c1[e])), bf(__fmul_rn(-x2[e], s1[e]))));
-          o2[e] = bf(__fadd_rn(bf(__fmul_rn(x2[e], c2[e])), bf(__fmul_rn(x1[e], s2[e]))));
-          acc_lo[e] = __fadd_rn(acc_lo[e], o1[e]);
-          acc_hi[e] = __fadd_rn(acc_hi[e], o2[e]);
+        for (int e = 0; e < 4; ++e) {
+          o1[e] = bf16x2_add(bf16x2_mul(xa[e], ca[e]), bf16x2_mul(bf16x2_neg(xb[e]), sa[e]));
+          o2[e] = bf16x2_add(bf16x2_mul(xb[e], cb[e]), bf16x2_mul(xa[e], sb[e]));
+          acc_lo[2 * e] = __fadd_rn(acc_lo[2 * e], __uint_as_float(o1[e] << 16));
+          acc_lo[2 * e + 1] = __fadd_rn(acc_lo[2 * e + 1], __uint_as_float(o1[e] & 0xffff0000u));
+          acc_hi[2 * e] = __fadd_rn(acc_hi[2 * e], __uint_as_float(o2[e] << 16));
+          acc_hi[2 * e + 1] = __fadd_rn(acc_hi[2 * e + 1], __uint_as_float(o2[e] & 0xffff0000u));
         }
+        const uint4 w1 = make_uint4(o1[0], o1[1], o1[2], o1[3]), w2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
         __nv_bfloat16 *p = dst + (t0 + r0 + u) * kD;
-        *reinterpret_cast<uint4 *>(p) = pack8(o1);
-        *reinterpret_cast<uint4 *>(p + kHalf) = pack8(o2);
+        *reinterpret_cast<uint4 *>(p) = w1;
+        *reinterpret_cast<uint4 *>(p + kHalf) = w2;
       }
     }
   }
