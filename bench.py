@@ -646,8 +646,8 @@ def run_ours(args):
     # N > 1 one flag store and one bounded wait; at N = 1 counted from the activity trace
     launches_per_step = 7 if world == 1 else 9
     if world == 1:
-        try:
-            launches_per_step = own_kernel_launches(step)
+        try:  # an activity trace that saw nothing (no CUPTI, e.g. under ncu) keeps the count
+            launches_per_step = own_kernel_launches(step) or launches_per_step
         except Exception:  # noqa: BLE001 - the trace is a report; keep the count by construction
             pass
     t = torch.tensor([ms], device=dev)
