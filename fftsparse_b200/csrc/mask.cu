@@ -939,9 +939,21 @@ __device__ void colrow_body(const T *__restrict__ qb, const T *__restrict__ kb, 
       }
       __syncthreads();
       if (col && tid < D) {
-        for (int t = 0; t < rows; ++t) {
-          if (jhi - t <= N - 2) P = __dadd_rn(P, (double)Elem<T>::to_f32(qs[t * QS + tid]));
-          pch[t * PS + tid] = P;
+        // eight rows of channel tid read into registers before their part of the
+        // chain: the loads then do not wait behind the previous rows' stores of pch
+        // (same shared memory), and the additions keep their order
+        for (int t0 = 0; t0 < rows; t0 += 8) {
+          double dv[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) dv[u] = t0 + u < rows ? (double)Elem<T>::to_f32(qs[(t0 + u) * QS + tid]) : 0.0;
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int t = t0 + u;
+            if (t < rows) {
+              if (jhi - t <= N - 2) P = __dadd_rn(P, dv[u]);
+              pch[t * PS + tid] = P;
+            }
+          }
         }
       }
       __syncthreads();
