@@ -118,14 +118,14 @@ def test_config5_shape(lib):
             assert float(err.max()) <= 2e-2 and float(err.mean()) <= 1e-3, (h, i, float(err.max()))
 
 
-@pytest.mark.parametrize("Hkv,chunk", [(8, 4), (2, 3)])
-def test_host_buffers_equal_device_call(lib, Hkv, chunk):
+@pytest.mark.parametrize("B,L,Hkv,chunk", [(1, 16384, 8, 4), (1, 16384, 2, 3), (2, 8192, 4, 2)])
+def test_host_buffers_equal_device_call(lib, B, L, Hkv, chunk):
     """myattn_prefill_host on pinned host q/k/v (expanded and GQA k/v; a chunk size
-    that is not a multiple of the group rounds down to whole groups) returns the
-    device call's output bit for bit, on two calls in a row."""
+    that is not a multiple of the group rounds down to whole groups; two sequences)
+    returns the device call's output bit for bit, on two calls in a row."""
     import bench
-    g = torch.Generator().manual_seed(Hkv)
-    B, H, L, D = 1, 8, 16384, 128
+    g = torch.Generator().manual_seed(Hkv + B)
+    H, D = 8, 128
     q = torch.randn(B, H, L, D, generator=g).bfloat16().pin_memory()
     k = torch.randn(B, Hkv, L, D, generator=g).bfloat16().pin_memory()
     v = torch.randn(B, Hkv, L, D, generator=g).bfloat16().pin_memory()
