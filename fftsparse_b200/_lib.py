@@ -9,7 +9,11 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libfftsparse_b200.so")
+LIB_NORMAL = os.path.join(HERE, "libfftsparse_b200.so")
+# The bounds-checked build (every data-dependent kernel index tested, failures
+# recorded and skipped; slower) is loaded instead when FFTS_LIBRARY=checked.
+LIB_CHECKED = os.path.join(HERE, "libfftsparse_b200_checked.so")
+LIB_PATH = LIB_CHECKED if os.environ.get("FFTS_LIBRARY", "") == "checked" else LIB_NORMAL
 
 FFTS_OK = 0
 FFTS_E_INVALID = -1
@@ -59,6 +63,8 @@ EXPORTS = {
     "ffts_copy_2d": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "ffts_signal": (_I32, [_P, _P, _I32, _I32]),
     "ffts_wait_flags": (_I32, [_P, _I32, _I32, _P, _P]),
+    "ffts_bounds_check_enabled": (_I32, []),
+    "ffts_bounds_report": (_I32, [_P, _I32, _I32]),
 }
 
 _lib = None
@@ -77,7 +83,7 @@ def load(path: str = LIB_PATH):
         return _lib
     if not os.path.exists(path):
         raise ImportError(
-            f"libfftsparse_b200.so not found at {path}; build it with "
+            f"{os.path.basename(path)} not found at {path}; build it with "
             "`python -m fftsparse_b200.build` (nvcc, sm_100a). There is no CPU fallback.")
     lib = ctypes.CDLL(path)
     for name, (res, args) in EXPORTS.items():
@@ -86,6 +92,25 @@ def load(path: str = LIB_PATH):
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+class BoundsRecord(ctypes.Structure):
+    """ffts_bounds_record of include/fftsparse_b200.h."""
+    _fields_ = [("file", ctypes.c_char * 48), ("line", ctypes.c_int32), ("count", ctypes.c_uint32),
+                ("block", ctypes.c_int64)]
+
+
+def bounds_report(clear: bool = True, max_records: int = 32):
+    """Failed index checks of the bounds-checked build on the current device, one
+    dict per source file (file, line of the first failure, count, block); always
+    empty with the normal build."""
+    lib = load()
+    recs = (BoundsRecord * max_records)()
+    n = lib.ffts_bounds_report(recs, max_records, int(bool(clear)))
+    if n < 0:
+        check(n)
+    return [{"file": r.file.decode(), "line": r.line, "count": r.count, "block": r.block}
+            for r in recs[:min(n, max_records)]]
 
 
 def check(rc: int) -> None:

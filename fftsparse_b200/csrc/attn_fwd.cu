@@ -148,7 +148,10 @@ struct TileCursor {
   uint32_t cur;
   __device__ explicit TileCursor(const uint32_t *wd) : words(wd), w(0), cur(wd[0]) {}
   __device__ __forceinline__ int next() {
-    while (cur == 0) cur = words[++w];
+    while (cur == 0) {
+      if (!FFTS_IN_RANGE(w + 1, kTileWords)) return 0;  // more calls than set bits
+      cur = words[++w];
+    }
     const int t = __ffs(cur) - 1;
     cur &= cur - 1;
     return w * 32 + t;
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int lim = nkv - tw * 32;  // tiles valid in this word
         if (lim < 32) word &= (lim <= 0) ? 0u : ((1u << lim) - 1u);
       }
-      if (tw < TW) words[tw] = word;
+      if (tw < TW && FFTS_IN_RANGE(tw, kTileWords)) words[tw] = word;
       int cnt = __popc(word);
       for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
       base += cnt;
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_tx(bar(full), kKVBytes);
         const uint32_t dst = sbase + (is_k ? SmemLayout::k : SmemLayout::v) + s * kKVBytes;
         const CUtensorMap *map = is_k ? &tm_k : &tm_v;
-        const int j = is_k ? kcur.next() : vcur.next();
+        const int j = FFTS_INDEX(is_k ? kcur.next() : vcur.next(), nkv);
         tma_load_4d(dst, map, bar(full), 0, j * kBN, kvh, b);
         tma_load_4d(dst + kKVHalf, map, bar(full), 64, j * kBN, kvh, b);
         if (is_k) ++issued_k; else ++issued_v;
@@ -376,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     TileCursor cur(words);
     for (int n = 0; n < ntiles; ++n) {
       const int sb = n % 2;
-      const int j = cur.next();
+      const int j = FFTS_INDEX(cur.next(), nkv);
       if (!__all_sync(0xffffffffu, mbar_wait(bar(BSF + sb), (n >> 1) & 1, abort_flag, prm.wait_cycles))) { ok = false; break; }
       fence_after();
       const uint32_t s_addr = tmem + sb * kBN + lane_off;
@@ -394,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           uint32_t m = rem >= 32 ? 0xffffffffu : (rem <= 0 ? 0u : ((1u << rem) - 1u));
           if (prm.bs < kBM) {
             const int blk = (col0 + 32 * w) >> prm.bs_shift;
-            if (blk >= prm.nblk || !((rowbits[blk >> 5] >> (blk & 31)) & 1u)) m = 0u;
+            if (blk >= prm.nblk || !((rowbits[FFTS_INDEX(blk >> 5, prm.W)] >> (blk & 31)) & 1u)) m = 0u;
           }
           kw[w] = m;
         }
@@ -571,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int k = r; k < tile_rows * 16; k += kBM) {
           const int row = k >> 4, j = k & 15;
           const uint4 val = *reinterpret_cast<const uint4 *>(stage + row * 256 + ((j ^ (row & 15)) << 4));
-          *reinterpret_cast<uint4 *>(base + int64_t(row) * prm.os_l + j * 8) = val;
+          if (FFTS_IN_RANGE(qt * kBM + row, prm.L) && FFTS_IN_RANGE(qt * kBM + row - prm.out_row0, prm.L))
+            *reinterpret_cast<uint4 *>(base + int64_t(row) * prm.os_l + j * 8) = val;
         }
       }
       // the peers learn of these rows from a flag a later kernel on this

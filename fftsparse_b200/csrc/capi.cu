@@ -6,16 +6,34 @@
 
 #include <stdarg.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "ffts_common.cuh"
 
 namespace ffts {
 
 static thread_local std::string g_last_error;
+
+#ifdef FFTS_BOUNDS_CHECK
+namespace oob {
+struct Entry {
+  const char *file;
+  Reader read;
+};
+static std::vector<Entry> &registry() {
+  static std::vector<Entry> r;  // filled by static initialisers, read after load
+  return r;
+}
+void register_reader(const char *file, Reader fn) { registry().push_back({file, fn}); }
+}  // namespace oob
+#endif
 
 void set_error(int code, const char *fmt, ...) {
   char buf[512];
@@ -118,6 +136,18 @@ int sparse_attn_fwd(const void *q, const void *k, const void *v, int64_t B, int6
                     int64_t row_lo, int64_t row_hi, void *const *peer_out, int n_peers, int32_t *status,
                     cudaStream_t stream);
 
+// One NVTX range per compute entry point (visible in nsys / ncu range filters;
+// a call into the NVTX stubs when no tool is attached).
+namespace {
+struct NvtxRange {
+  explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
+}  // namespace
+#define FFTS_ENTRY(name)        \
+  g_last_error.clear();         \
+  NvtxRange ffts_nvtx_range_(name)
+
 static int check_device() {
   int dev = 0;
   FFTS_CUDA(cudaGetDevice(&dev));
@@ -154,7 +184,7 @@ int32_t ffts_init(int32_t device) {
 int32_t ffts_pool(const void *x, int32_t dtype, int64_t B, int64_t H, int64_t L, int64_t D,
                   int64_t stride_b, int64_t stride_h, int64_t stride_l, int32_t block_size, void *out,
                   void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_pool");
   FFTS_REQUIRE(x != nullptr && out != nullptr, "ffts_pool: NULL pointer");
   int rc = check_device();
   if (rc) return rc;
@@ -166,7 +196,7 @@ int32_t ffts_rope_pool(const void *q_src, int64_t q_ld, const void *k_src, int64
                        int64_t v_ld, int64_t L, int64_t Hq, int64_t Hkv, int64_t D, const void *cos,
                        const void *sin, int64_t cs_ld, int32_t block_size, void *q_out, void *k_out, void *v_out,
                        void *q_pooled, void *k_pooled, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_rope_pool");
   int rc = check_device();
   if (rc) return rc;
   return launch_rope_pool(q_src, q_ld, k_src, k_ld, v_src, v_ld, L, Hq, Hkv, D, cos, sin, cs_ld, block_size,
@@ -179,7 +209,7 @@ int32_t ffts_qkv_rope_pool(const void *x, int64_t B, int64_t L, int64_t hidden, 
                            int32_t block_size, void *q_out, void *k_out, void *v_out, void *q_pooled,
                            void *k_pooled, void *proj_out, int64_t proj_ld, void *workspace,
                            int64_t workspace_bytes, int32_t *status, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_qkv_rope_pool");
   int rc = check_device();
   if (rc) return rc;
   return qkv_rope_pool(x, B, L, hidden, x_stride_l, x_stride_b, w, w_ld, bias, Hq, Hkv, D, cos, sin, cs_ld,
@@ -198,7 +228,7 @@ int32_t ffts_decode_attn(const void *q, int64_t q_stride_b, int64_t q_stride_h, 
                          int64_t H, int64_t Hkv, int64_t Lk, int64_t D, int64_t splits, void *workspace,
                          int64_t workspace_bytes, void *out, int64_t out_stride_b, int64_t out_stride_h,
                          const void *mask, int32_t mask_dtype, int64_t mask_stride_b, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_decode_attn");
   int rc = check_device();
   if (rc) return rc;
   return decode_attn(q, q_stride_b, q_stride_h, k_cache, k_strides, v_cache, v_strides, B, H, Hkv, Lk, D, splits,
@@ -215,7 +245,7 @@ int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B
                         int64_t D, const ffts_mask_params *params, uint32_t *mask_bits, int32_t *row_count,
                         float *corr, float *corr_sum, uint8_t *is_stripe, float *stripe_var, void *workspace,
                         int64_t workspace_bytes, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_block_mask");
   int rc = check_device();
   if (rc) return rc;
   return block_mask(qb, kb, dtype, B, H, Hkv, D, params, mask_bits, row_count, corr, corr_sum, is_stripe,
@@ -224,12 +254,12 @@ int32_t ffts_block_mask(const void *qb, const void *kb, int32_t dtype, int64_t B
 
 int32_t ffts_unpack_mask(const uint32_t *mask_bits, int64_t B, int64_t H, int64_t N, uint8_t *out,
                          void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_unpack_mask");
   return unpack_mask(mask_bits, B, H, N, out, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ffts_mask_row_ptr(const int32_t *row_count, int64_t rows, int64_t *row_ptr, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_mask_row_ptr");
   int rc = check_device();
   if (rc) return rc;
   return mask_row_ptr(row_count, rows, row_ptr, static_cast<cudaStream_t>(stream));
@@ -237,7 +267,7 @@ int32_t ffts_mask_row_ptr(const int32_t *row_count, int64_t rows, int64_t *row_p
 
 int32_t ffts_mask_col_idx(const uint32_t *mask_bits, int64_t rows, int64_t N, const int64_t *row_ptr,
                           int32_t *col_idx, int64_t capacity, int32_t *status, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_mask_col_idx");
   int rc = check_device();
   if (rc) return rc;
   return mask_col_idx(mask_bits, rows, N, row_ptr, col_idx, capacity, status, static_cast<cudaStream_t>(stream));
@@ -248,7 +278,7 @@ int32_t ffts_sparse_attn_fwd(const void *q, const void *k, const void *v, int64_
                              const int64_t *v_strides, const uint32_t *mask_bits, int32_t block_size,
                              int32_t causal, void *out, const int64_t *out_strides, int32_t *status,
                              void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_sparse_attn_fwd");
   int rc = check_device();
   if (rc) return rc;
   return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
@@ -260,7 +290,7 @@ int32_t ffts_sparse_attn_fwd_rows(const void *q, const void *k, const void *v, i
                                   const int64_t *v_strides, const uint32_t *mask_bits, int32_t block_size,
                                   int32_t causal, int64_t row_lo, int64_t row_hi, void *out,
                                   const int64_t *out_strides, int32_t *status, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_sparse_attn_fwd_rows");
   int rc = check_device();
   if (rc) return rc;
   return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
@@ -274,12 +304,51 @@ int32_t ffts_sparse_attn_fwd_push(const void *q, const void *k, const void *v, i
                                   int32_t causal, int64_t row_lo, int64_t row_hi, void *out,
                                   const int64_t *out_strides, void *const *peer_out, int32_t n_peers,
                                   int32_t *status, void *stream) {
-  g_last_error.clear();
+  FFTS_ENTRY("ffts_sparse_attn_fwd_push");
   int rc = check_device();
   if (rc) return rc;
   return sparse_attn_fwd(q, k, v, B, H, Hkv, L, D, q_strides, k_strides, v_strides, mask_bits, block_size,
                          causal, out, out_strides, row_lo, row_hi, peer_out, n_peers, status,
                          static_cast<cudaStream_t>(stream));
+}
+
+int32_t ffts_bounds_check_enabled(void) {
+#ifdef FFTS_BOUNDS_CHECK
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+int32_t ffts_bounds_report(ffts_bounds_record *records, int32_t max_records, int32_t clear) {
+  g_last_error.clear();
+  FFTS_REQUIRE(max_records >= 0 && (records != nullptr || max_records == 0),
+               "ffts_bounds_report: NULL records with max_records > 0");
+#ifdef FFTS_BOUNDS_CHECK
+  int found = 0;
+  for (const oob::Entry &e : oob::registry()) {
+    unsigned long long first = 0;
+    unsigned int count = 0;
+    const int rc = e.read(clear, &first, &count);
+    if (rc) return cuda_status(cudaError_t(rc), "ffts_bounds_report: reading the records");
+    if (count == 0 && first == 0) continue;
+    if (found < max_records) {
+      ffts_bounds_record &r = records[found];
+      const char *base = strrchr(e.file, '/');
+      base = base ? base + 1 : e.file;
+      snprintf(r.file, sizeof(r.file), "%s", base);
+      r.line = int32_t((first >> 32) & 0x7fffffff);
+      r.count = count;
+      r.block = int64_t(first & 0xffffffffull);
+    }
+    ++found;
+  }
+  return found;
+#else
+  (void)records;
+  (void)clear;
+  return 0;
+#endif
 }
 
 }  // extern "C"

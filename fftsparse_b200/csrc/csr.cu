@@ -98,7 +98,8 @@ __global__ void __launch_bounds__(256) col_idx_kernel(const uint32_t *__restrict
     while (word) {
       const int t = __ffs(word) - 1;
       word &= word - 1u;
-      col_idx[pos++] = w * 32 + t;
+      if (FFTS_IN_RANGE(pos, capacity)) col_idx[pos] = w * 32 + t;
+      ++pos;
     }
     base += __shfl_sync(0xffffffffu, incl, 31);
   }

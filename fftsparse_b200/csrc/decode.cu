@@ -57,7 +57,7 @@ struct Params {
 
 __device__ __forceinline__ float bias_log2(const Params &p, int b, int key) {
   if (p.bias == nullptr) return 0.0f;
-  const int64_t i = int64_t(b) * p.bias_sb + key;
+  const int64_t i = int64_t(b) * p.bias_sb + FFTS_INDEX(key, p.Lk);
   const float x = p.bias_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(p.bias)[i])
                               : static_cast<const float *>(p.bias)[i];
   return x * 1.4426950408889634f;  // scores are kept in log2 units
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kSplitThreads, MINB) decode_split_kernel(const
     for (int it = 0; it < ITS; ++it) {
       const int row = base + 2 * it + half;
       const bool ok = row < k1;
-      const int64_t r = ok ? row : k0;  // a valid address; nothing is read when !ok
+      const int64_t r = ok ? FFTS_INDEX(row, p.Lk) : k0;  // a valid address; nothing is read when !ok
       cp_async16(slot + uint32_t(2 * it * kRowBytes), kb + r * p.ks_l, ok ? 16 : 0);
       cp_async16(slot + uint32_t((R + 2 * it) * kRowBytes), vb + r * p.vs_l, ok ? 16 : 0);
     }
@@ -298,9 +298,9 @@ __global__ void __launch_bounds__(kSplitThreads, MINB) decode_split_kernel(const
 #pragma unroll
     for (int ww = 0; ww < kWarps; ++ww)
       if (wm[ww][g] != -INFINITY) o = fmaf(exp2f(wm[ww][g] - M), red[(ww * GM + g) * kD + d], o);
-    w[(g0 + g) * (kD + 2) + d] = o;
+    if (FFTS_IN_RANGE(g0 + g, G)) w[(g0 + g) * (kD + 2) + d] = o;
   }
-  if (tid < ng) {
+  if (tid < ng && FFTS_IN_RANGE(g0 + tid, G)) {
     float M = -INFINITY, L = 0.0f;
 #pragma unroll
     for (int ww = 0; ww < kWarps; ++ww) M = fmaxf(M, wm[ww][tid]);

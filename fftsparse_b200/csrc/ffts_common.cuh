@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <type_traits>
 
 #include "../../include/fftsparse_b200.h"
 
@@ -136,6 +137,67 @@ __host__ __device__ __forceinline__ int ilog2_ceil(int64_t m) {
   while ((int64_t(1) << r) < m) ++r;
   return r;
 }
+
+// ----------------------------------------------------- bounds-checked build
+// Compute-sanitizer is not available where this library is tested, so the
+// library has a second build, libfftsparse_b200_checked.so, compiled with
+// -DFFTS_BOUNDS_CHECK.  In it, every FFTS_IN_RANGE(i, n) tests 0 <= i < n for an
+// index whose value comes from data or from a ragged edge; a failed test counts
+// itself in a word of this source file's own, remembers the line and the linear
+// block index of the file's first failure, and evaluates to false so that the
+// caller skips the access; FFTS_INDEX(i, n) records the same failure and yields
+// index 0 instead, for a load the caller cannot skip.  Nothing traps.
+// ffts_bounds_report() reads (and optionally clears) those words for the current
+// device.  In the normal build the macro is the constant true and adds nothing.
+#ifdef FFTS_BOUNDS_CHECK
+namespace oob {
+// per translation unit: first failure (bit 63 set | line << 32 | block index) and count
+static __device__ unsigned long long g_first;
+static __device__ unsigned int g_count;
+
+static __device__ __noinline__ void note(int line) {
+  const unsigned long long blk =
+      blockIdx.x + (unsigned long long)gridDim.x * (blockIdx.y + (unsigned long long)gridDim.y * blockIdx.z);
+  atomicCAS(&g_first, 0ull, (1ull << 63) | ((unsigned long long)(line & 0x7fffffff) << 32) | (blk & 0xffffffffull));
+  atomicAdd(&g_count, 1u);
+}
+
+static __device__ __forceinline__ bool in_range(long long i, long long n, int line) {
+  const bool ok = i >= 0 && i < n;
+  if (!ok) note(line);
+  return ok;
+}
+
+// i when 0 <= i < n, else (after recording the failure) 0, a valid index of any
+// non-empty extent: for loads whose address the caller cannot skip
+static __device__ __forceinline__ long long checked_index(long long i, long long n, int line) {
+  return in_range(i, n, line) ? i : 0;
+}
+
+// host side: this file's words, read (and zeroed if clear) on the current device
+typedef int (*Reader)(int clear, unsigned long long *first, unsigned int *count);
+void register_reader(const char *file, Reader fn);
+static int read_words(int clear, unsigned long long *first, unsigned int *count) {
+  cudaError_t e = cudaMemcpyFromSymbol(first, g_first, sizeof(*first));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(count, g_count, sizeof(*count));
+  if (e == cudaSuccess && clear) {
+    const unsigned long long z64 = 0;
+    const unsigned int z32 = 0;
+    e = cudaMemcpyToSymbol(g_first, &z64, sizeof(z64));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_count, &z32, sizeof(z32));
+  }
+  return e == cudaSuccess ? 0 : int(e);
+}
+static const bool g_registered = (register_reader(__BASE_FILE__, &read_words), true);
+}  // namespace oob
+#define FFTS_IN_RANGE(i, n) (::ffts::oob::in_range((long long)(i), (long long)(n), __LINE__))
+#define FFTS_INDEX(i, n) \
+  (static_cast<std::remove_cv_t<std::remove_reference_t<decltype(i)>>>( \
+      ::ffts::oob::checked_index((long long)(i), (long long)(n), __LINE__)))
+#else
+#define FFTS_IN_RANGE(i, n) (true)
+#define FFTS_INDEX(i, n) (i)
+#endif
 
 constexpr int kMaxBlocks = 4096;        // N limit (FFT size <= 8192)
 constexpr int kMaxFFT = 8192;           // largest FFT length

@@ -163,9 +163,9 @@ __device__ void fft_partial_body(const T *__restrict__ qb, const T *__restrict__
     for (int e = threadIdx.x; e < nb * M; e += blockDim.x) {
       const int fi = e / M, t = e - fi * M;
       float2 z = make_float2(0.0f, 0.0f);
-      if (t < N) z = make_float2(Elem<T>::to_f32(q[int64_t(t) * D + d0 + fi]),
-                                 Elem<T>::to_f32(k[int64_t(t) * D + d0 + fi]));
-      buf[fi * M + bitrev(t, bits)] = z;
+      if (t < N && FFTS_IN_RANGE(d0 + fi, D))
+        z = make_float2(Elem<T>::to_f32(q[int64_t(t) * D + d0 + fi]), Elem<T>::to_f32(k[int64_t(t) * D + d0 + fi]));
+      if (FFTS_IN_RANGE(fi * M + bitrev(t, bits), nf * M)) buf[fi * M + bitrev(t, bits)] = z;
     }
     __syncthreads();
     fft_block(buf, M, nb, tw, false);
@@ -260,7 +260,8 @@ __device__ void fft_warp_body(const T *__restrict__ qb, const T *__restrict__ kb
   constexpr int V = Elem<T>::kVec;
   constexpr int NV = kDChunk / V;  // 16-byte vectors per row and tensor
   constexpr int U = 4;             // rows in flight per thread
-  for (int base = threadIdx.x; base < N; base += U * blockDim.x) {
+  const int nstage = FFTS_IN_RANGE(chunk * kDChunk + kDChunk - 1, D) ? N : 0;  // the chunk's channels exist
+  for (int base = threadIdx.x; base < nstage; base += U * blockDim.x) {
     uint4 qv[U][NV], kv[U][NV];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -365,7 +366,7 @@ __device__ void fft_warp_body(const T *__restrict__ qb, const T *__restrict__ kb
       a.x = __fadd_rn(a.x, c.x);
       a.y = __fadd_rn(a.y, c.y);
     }
-    out[L * R + r] = a;
+    if (FFTS_IN_RANGE(L * R + r, F)) out[L * R + r] = a;
   }
 }
 
@@ -478,7 +479,8 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
     int stripe = 0;
     if (p.corr_on && !p.stripe_all_diffuse) {
       double total = 0.0;
-      for (int s = 0; s < p.n_diag_samples; ++s) total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s]);
+      for (int s = 0; s < p.n_diag_samples; ++s)
+        total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + FFTS_INDEX(s, FFTS_MAX_DIAG_SAMPLES)]);
       svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
       stripe = svar <= p.stripe_threshold;
     }
@@ -521,7 +523,7 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
   __syncthreads();
   if (ex < sraw) {
     float mn = INFINITY;
-    for (int t = ex + threadIdx.x; t < sraw; t += blockDim.x) mn = fminf(mn, corr[t]);
+    for (int t = ex + threadIdx.x; t < sraw; t += blockDim.x) mn = fminf(mn, corr[FFTS_INDEX(t, N)]);
     for (int o = 16; o; o >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mn;
     __syncthreads();
@@ -532,11 +534,11 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
     }
     __syncthreads();
     mn = red[0];
-    const float lden0 = g_log10[N - ex];
+    const float lden0 = g_log10[FFTS_INDEX(N - ex, kMaxBlocks + 1)];
     const float lden = lden0 > 1e-6f ? lden0 : 1e-6f;
     for (int t = ex + threadIdx.x; t < sraw; t += blockDim.x) {
-      const float w = __fdiv_rn(g_log10[N - t], lden);
-      corr[t] = __fmul_rn(__fsub_rn(corr[t], mn), w);
+      const float w = __fdiv_rn(g_log10[FFTS_INDEX(N - t, kMaxBlocks + 1)], lden);
+      if (FFTS_IN_RANGE(t, N)) corr[t] = __fmul_rn(__fsub_rn(corr[t], mn), w);
     }
     __syncthreads();
   }
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
   float mx = 0.0f;
   if (nr > 0) {
     if (p.corr_mode == FFTS_SEL_TOPK) {
-      for (int t = threadIdx.x; t < nr; t += blockDim.x) keys[t] = f32_key(corr[rs + t]);
+      for (int t = threadIdx.x; t < nr; t += blockDim.x) keys[t] = f32_key(corr[FFTS_INDEX(rs + t, N)]);
       __syncthreads();
       const float ranks = __fmul_rn(p.corr_quantile, (float)(nr - 1));
       const int lo = (int)ranks;
@@ -562,7 +564,7 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
       thr = fabsf(w) < 0.5f ? __fmaf_rn(w, diff, a) : __fmaf_rn(-diff, __fsub_rn(1.0f, w), bb);
     } else {
       float m = -INFINITY;
-      for (int t = rs + threadIdx.x; t < N; t += blockDim.x) m = fmaxf(m, corr[t]);
+      for (int t = rs + threadIdx.x; t < N; t += blockDim.x) m = fmaxf(m, corr[FFTS_INDEX(t, N)]);
       for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       __syncthreads();
       if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -690,10 +692,10 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   const int N = p.n_blocks;
   const int QS = stage_stride<T>(D);
   const int tid = threadIdx.x;
-  int lo = p.diag_taus[first], hi = lo;
+  int lo = p.diag_taus[FFTS_INDEX(first, FFTS_MAX_DIAG_SAMPLES)], hi = lo;
   for (int g = 1; g < G; ++g) {
-    lo = min(lo, p.diag_taus[first + g]);
-    hi = max(hi, p.diag_taus[first + g]);
+    lo = min(lo, p.diag_taus[FFTS_INDEX(first + g, FFTS_MAX_DIAG_SAMPLES)]);
+    hi = max(hi, p.diag_taus[FFTS_INDEX(first + g, FFTS_MAX_DIAG_SAMPLES)]);
   }
   const int wrows = kDiagTile + (hi - lo);
   T *ks = reinterpret_cast<T *>(smem_raw);           // [kDiagTile][QS]
@@ -747,8 +749,10 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
       const bool v1 = t1 < N - tau1 - 1;
       const bool v2 = idx2 < G * kDiagTile && t2 < N - p.diag_taus[first + min(g2, G - 1)] - 1;
       const int tau2 = v2 ? p.diag_taus[first + g2] : tau1;
-      const T *qa = qw + (t1 + tau1 - t0 - lo) * QS, *ka = ks + (t1 - t0) * QS;
-      const T *qb2 = qw + ((v2 ? t2 : t1) + tau2 - t0 - lo) * QS, *kb2 = ks + ((v2 ? t2 : t1) - t0) * QS;
+      // the q rows of both pairs lie in the staged window [t0 + lo, t0 + hi + 64)
+      const T *qa = qw + FFTS_INDEX(t1 + tau1 - t0 - lo, wrows) * QS, *ka = ks + (t1 - t0) * QS;
+      const T *qb2 = qw + FFTS_INDEX((v2 ? t2 : t1) + tau2 - t0 - lo, wrows) * QS;
+      const T *kb2 = ks + ((v2 ? t2 : t1) - t0) * QS;
       double a1 = 0.0, a2 = 0.0;
       bool exact32 = false;
       if constexpr (sizeof(T) == 2) exact32 = safe_q != nullptr && range_ok(safe_q, bh) && range_ok(safe_k, kh);
@@ -763,8 +767,8 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
           a2 = __fma_rn((double)Elem<T>::to_f32(qb2[d]), (double)Elem<T>::to_f32(kb2[d]), a2);
         }
       }
-      if (v1) vals[g1 * N + t1] = __double2float_rn(__ddiv_rn(a1, sqrtD));
-      if (v2) vals[g2 * N + t2] = __double2float_rn(__ddiv_rn(a2, sqrtD));
+      if (v1 && FFTS_IN_RANGE(g1, gmax)) vals[g1 * N + t1] = __double2float_rn(__ddiv_rn(a1, sqrtD));
+      if (v2 && FFTS_IN_RANGE(g2, gmax)) vals[g2 * N + t2] = __double2float_rn(__ddiv_rn(a2, sqrtD));
     }
     __syncthreads();
   }
@@ -826,7 +830,8 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
       const int m = N - p.diag_taus[first + g] - 1;
       double mabs = m > 0 ? __ddiv_rn(acc[g], (double)m) : __longlong_as_double(0x7ff8000000000000ll);
       if (mabs < floor6) mabs = floor6;
-      nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + first + g] = __ddiv_rn(var[g], mabs);
+      if (FFTS_IN_RANGE(first + g, FFTS_MAX_DIAG_SAMPLES))
+        nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + first + g] = __ddiv_rn(var[g], mabs);
     }
   }
 }
@@ -980,7 +985,8 @@ __device__ void colrow_body(const T *__restrict__ qb, const T *__restrict__ kb, 
   }
   for (int w = tid; w < W; w += blockDim.x) words[w] = 0;
   __syncthreads();
-  if (col) block_topk_bits(ckeys, p.col_start, p.col_end, p.col_topk, words, hist, bc);
+  if (col && FFTS_IN_RANGE(p.col_start, N) && FFTS_IN_RANGE(p.col_end - 1, N))
+    block_topk_bits(ckeys, p.col_start, p.col_end, p.col_topk, words, hist, bc);
   __syncthreads();
   for (int w = tid; w < W; w += blockDim.x) colsel[int64_t(bh) * W + w] = words[w];
   __syncthreads();
@@ -1188,7 +1194,7 @@ __global__ void __launch_bounds__(256) mask_build_kernel(const T *__restrict__ q
       const int tau = i - j;
       bool on = j < p.keep_sink || j >= N - p.keep_recent || tau <= p.local_window;
       if (p.corr_on && stripe)
-        on |= tau >= p.remote_start && ((ts[tau >> 5] >> (tau & 31)) & 1u) && j >= p.keep_sink;
+        on |= tau >= p.remote_start && ((ts[FFTS_INDEX(tau >> 5, W)] >> (tau & 31)) & 1u) && j >= p.keep_sink;
       on |= (dw >> t) & 1u;
       on |= (cw >> t) & 1u;
       on |= (lw >> t) & 1u;

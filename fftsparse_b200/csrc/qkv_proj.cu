@@ -382,7 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async();
           half_sync(half);
-          if (r == 0) {  // one thread stores the box: rows past L fall outside the map and are dropped
+          // one thread stores the box: rows past L fall outside the map and are dropped;
+          // the row and head coordinates are never negative (a TMA store must not start there)
+          if (r == 0 && FFTS_IN_RANGE(t_half, p.L) && FFTS_IN_RANGE(hr, hcount)) {
             tma_store_3d(omap, stage_s, 64 * box, t_half, c.b * hcount + hr);
             bulk_commit();
           }
@@ -399,8 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int rr = r0; rr < r0 + p.bs; ++rr)
                 s = __fadd_rn(s, __bfloat162float(
                                      *reinterpret_cast<const __nv_bfloat16 *>(col + rr * 128 + (((ch >> 3) ^ (rr & 7)) << 4))));
-              p.pooled[role][((int64_t(c.b) * hcount + hr) * p.N + n) * kD + 64 * box + ch] =
-                  __float2bfloat16_rn(__fdiv_rn(s, fbs));
+              if (FFTS_IN_RANGE(hr, hcount))
+                p.pooled[role][((int64_t(c.b) * hcount + hr) * p.N + n) * kD + 64 * box + ch] =
+                    __float2bfloat16_rn(__fdiv_rn(s, fbs));
             }
           }
           if (r == 0) bulk_wait_read();  // the store has read the box

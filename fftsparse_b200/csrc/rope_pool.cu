@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(256, 2) rope_pool_kernel(const __grid_constant
       uint4 lo[kU], hi[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        if (r0 + u < rows) {
+        if (r0 + u < rows && FFTS_IN_RANGE(t0 + r0 + u, a.L)) {
           const __nv_bfloat16 *p = src + (t0 + r0 + u) * ld;
           lo[u] = *reinterpret_cast<const uint4 *>(p);
           hi[u] = *reinterpret_cast<const uint4 *>(p + kHalf);
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(256, 2) rope_pool_kernel(const __grid_constant
       }
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        if (r0 + u < rows) {
+        if (r0 + u < rows && FFTS_IN_RANGE(t0 + r0 + u, a.L)) {
           __nv_bfloat16 *p = dst + (t0 + r0 + u) * kD;
           *reinterpret_cast<uint4 *>(p) = lo[u];
           *reinterpret_cast<uint4 *>(p + kHalf) = hi[u];
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(256, 2) rope_pool_kernel(const __grid_constant
     uint4 xl[kU], xh[kU], cl[kU], ch[kU], sl[kU], sh[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      if (r0 + u < rows) {
+      if (r0 + u < rows && FFTS_IN_RANGE(t0 + r0 + u, a.L)) {
         const int64_t t = t0 + r0 + u;
         const __nv_bfloat16 *p = src + t * ld;
         xl[u] = *reinterpret_cast<const uint4 *>(p);
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(256, 2) rope_pool_kernel(const __grid_constant
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      if (r0 + u < rows) {
+      if (r0 + u < rows && FFTS_IN_RANGE(t0 + r0 + u, a.L)) {
         // packed bf16 arithmetic: a bf16 x bf16 product is exact in fp32, so
         // mul.rn.bf16x2 rounds it once exactly as bf(x * c) does; the sum of two
         // bf16 values rounds in add.rn.bf16x2 as bf(a + b) does (exact in fp32

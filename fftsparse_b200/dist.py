@@ -25,6 +25,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from . import trace
 from .status import StatusWord
 
 
@@ -342,20 +343,25 @@ def sharded_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, layer_idx
         ql, kl, vl = local_views(q, k, v, shard)
     block_size = kwargs.pop("block_size", 128)
     is_causal = kwargs.pop("is_causal", True)
-    mask = fft_block_mask(ql, kl, block_size=block_size, **kwargs)
-    whole_batch = all(sh.b_lo == 0 and sh.b_hi in (-1, B) for sh in shards)
-    if gather is not None and world > 1 and B == 1 and whole_batch:
-        res = gather.run(ql, kl, vl, mask.bits, block_size, is_causal, shard)
-        if out is not None:
-            out.copy_(res)
+    with trace.layer(layer_idx):
+        mask = fft_block_mask(ql, kl, block_size=block_size, **kwargs)
+        whole_batch = all(sh.b_lo == 0 and sh.b_hi in (-1, B) for sh in shards)
+        if gather is not None and world > 1 and B == 1 and whole_batch:
+            # the peer pushes run inside the attention launch and its copy-engine overlap
+            with trace.stage("10_kernel+gather"):
+                res = gather.run(ql, kl, vl, mask.bits, block_size, is_causal, shard)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
+        if out is None:
+            out = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=q.device)
+        Bl = ql.shape[0]
+        local = out if world == 1 else torch.empty(Bl, shard.heads, L, D, dtype=torch.bfloat16, device=q.device)
+        # [Bl, Hl, L, D] storage, written through the kernel's [B, L, H, D] strides
+        with trace.stage("10_kernel"):
+            sparse_attention(ql, kl, vl, mask.bits, block_size, causal=is_causal, out=local.permute(0, 2, 1, 3))
+        if world == 1:
             return out
-        return res
-    if out is None:
-        out = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=q.device)
-    Bl = ql.shape[0]
-    local = out if world == 1 else torch.empty(Bl, shard.heads, L, D, dtype=torch.bfloat16, device=q.device)
-    # [Bl, Hl, L, D] storage, written through the kernel's [B, L, H, D] strides
-    sparse_attention(ql, kl, vl, mask.bits, block_size, causal=is_causal, out=local.permute(0, 2, 1, 3))
-    if world == 1:
-        return out
-    return gather_heads(local, out, group, shards)
+        with trace.stage("11_gather"):  # no counterpart: the reference runs on one device
+            return gather_heads(local, out, group, shards)

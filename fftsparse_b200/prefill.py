@@ -32,7 +32,7 @@ from typing import Optional
 
 import torch
 
-from . import _lib
+from . import _lib, trace
 from .params import SEL_TOPK, derive_mask_params, MaskParams
 from .status import device_status
 
@@ -279,8 +279,9 @@ def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, bloc
     lib = _lib.load()
     N = params.n_blocks
     if pooled is None:
-        qb = pool_blocks(q, params.block_size)
-        kb = pool_blocks(k, params.block_size)
+        with trace.stage("3_mean_pool"):
+            qb = pool_blocks(q, params.block_size)
+            kb = pool_blocks(k, params.block_size)
     else:
         qb, kb = pooled
         if qb.shape != (B, H, N, D) or kb.shape != (B, Hkv, N, D) or qb.dtype != q.dtype or \
@@ -299,10 +300,11 @@ def fft_block_mask(query_states: torch.Tensor, key_states: torch.Tensor, *, bloc
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     if cp is None:
         cp = params.to_c()
-    _lib.check(lib.ffts_block_mask(qb.data_ptr(), kb.data_ptr(), _DTYPES[q.dtype], B, H, Hkv, D,
-                                   _lib.ctypes.addressof(cp), bits.data_ptr(), row_count.data_ptr(),
-                                   corr.data_ptr(), corr_sum.data_ptr(), is_stripe.data_ptr(),
-                                   stripe_var.data_ptr(), ws.data_ptr(), ws_bytes, _stream_ptr(dev)))
+    with trace.stage("4-9_select"):
+        _lib.check(lib.ffts_block_mask(qb.data_ptr(), kb.data_ptr(), _DTYPES[q.dtype], B, H, Hkv, D,
+                                       _lib.ctypes.addressof(cp), bits.data_ptr(), row_count.data_ptr(),
+                                       corr.data_ptr(), corr_sum.data_ptr(), is_stripe.data_ptr(),
+                                       stripe_var.data_ptr(), ws.data_ptr(), ws_bytes, _stream_ptr(dev)))
     return BlockMask(bits, row_count, corr, corr_sum, is_stripe, stripe_var, params, qb, kb)
 
 
@@ -473,17 +475,9 @@ def myattn_prefill(
     L_k = k.shape[2]
     if L_q != L_k:
         raise ValueError("prefill expects equal query and key lengths")
-    B, H, L, D = q.shape
-    min_blocks_needed = 10
-    if L_k < block_size * min_blocks_needed:
-        N = (L + block_size - 1) // block_size
-        bits = _dense_causal_bits(B, H, N, q.device)
-        out = sparse_attention(q, k, v, bits, block_size, causal=True)
-        return out.view(B, L, H * D)
-
-    mask = fft_block_mask(
-        q, k, block_size=block_size, sink_ratio=sink_ratio, recent_ratio=recent_ratio,
-        local_span_ratio=local_span_ratio, enable_correlation_mask=enable_correlation_mask,
+    mask_kwargs = dict(
+        sink_ratio=sink_ratio, recent_ratio=recent_ratio, local_span_ratio=local_span_ratio,
+        enable_correlation_mask=enable_correlation_mask,
         correlation_selection_mode=correlation_selection_mode,
         correlation_topk_ratio=correlation_topk_ratio, corr_threshold=corr_threshold,
         enable_column_mask=enable_column_mask, column_topk_ratio=column_topk_ratio,
@@ -491,7 +485,23 @@ def myattn_prefill(
         column_end_exclude_ratio=column_end_exclude_ratio,
         enable_last_block_mask=enable_last_block_mask, diag_sample_ratio=diag_sample_ratio,
         min_diag_samples=min_diag_samples, max_diag_samples=max_diag_samples,
-        stripe_threshold=stripe_threshold, qk_topk_ratio=qk_topk_ratio, pooled=pooled)
+        stripe_threshold=stripe_threshold, qk_topk_ratio=qk_topk_ratio)
+    if trace.enabled():
+        with trace.layer(layer_idx):
+            return _prefill(q, k, v, block_size, is_causal, pooled, mask_kwargs)
+    return _prefill(q, k, v, block_size, is_causal, pooled, mask_kwargs)
+
+
+def _prefill(q, k, v, block_size, is_causal, pooled, mask_kwargs):
+    B, H, L, D = q.shape
+    if L < block_size * 10:  # the reference's min_blocks_needed (my_attn_v7.py:506)
+        N = (L + block_size - 1) // block_size
+        bits = _dense_causal_bits(B, H, N, q.device)
+        with trace.stage("10_kernel"):
+            out = sparse_attention(q, k, v, bits, block_size, causal=True)
+        return out.view(B, L, H * D)
+
+    mask = fft_block_mask(q, k, block_size=block_size, pooled=pooled, **mask_kwargs)
 
     collector = getattr(sys.modules[__name__], "_sparsity_collector", None)
     if collector is not None:
@@ -500,7 +510,8 @@ def myattn_prefill(
             collector.setdefault("corr", []).append(corr_mask_fraction(mask.corr, mask.params))
         collector.setdefault("final", []).append(float(mask.row_count.sum()) / (B * H * N * N))
 
-    out = sparse_attention(q, k, v, mask.bits, block_size, causal=is_causal)
+    with trace.stage("10_kernel"):
+        out = sparse_attention(q, k, v, mask.bits, block_size, causal=is_causal)
     return out.view(B, L, H * D)
 
 

@@ -365,6 +365,27 @@ FFTS_API int32_t ffts_signal(int32_t *const *flags, void *const *streams, int32_
 FFTS_API int32_t ffts_wait_flags(const int32_t *flags, int32_t n, int32_t epoch, int32_t *status,
                                  void *stream);
 
+/*
+ * Bounds-checked build.  No counterpart in the reference (its kernels are
+ * library calls).  The library also builds as libfftsparse_b200_checked.so with
+ * every data-dependent or ragged-edge index of its kernels tested against its
+ * extent; a failed test skips the access and is recorded per source file on the
+ * device, nothing traps.  ffts_bounds_check_enabled() is 1 in that build and 0
+ * in the normal one.  ffts_bounds_report() reads the records of the current
+ * device (zeroing them when clear != 0), fills up to max_records entries and
+ * returns the number of source files with a failed check (0 in the normal build),
+ * or a negative FFTS_E* code.
+ */
+typedef struct ffts_bounds_record {
+  char file[48];   /* base name of the kernel's source file */
+  int32_t line;    /* source line of the file's first failed check */
+  uint32_t count;  /* failed checks in that file since the last clear */
+  int64_t block;   /* linear block index of the first failure */
+} ffts_bounds_record;
+
+FFTS_API int32_t ffts_bounds_check_enabled(void);
+FFTS_API int32_t ffts_bounds_report(ffts_bounds_record *records, int32_t max_records, int32_t clear);
+
 #ifdef __cplusplus
 }
 #endif

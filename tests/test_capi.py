@@ -85,3 +85,22 @@ def test_unknown_selection_mode_raises_value_error():
 def test_remote_start_beyond_blocks_raises():
     with pytest.raises(ValueError):
         derive_mask_params(1280, recent_ratio=1.0)
+
+
+def test_checked_library_exports_the_same_symbols():
+    """The bounds-checked build exports every symbol of the header and says so."""
+    import ctypes
+    from fftsparse_b200 import _lib
+    assert os.path.exists(_lib.LIB_CHECKED), "build the checked library: python -m fftsparse_b200.build"
+    checked = ctypes.CDLL(_lib.LIB_CHECKED)
+    for name in _lib.EXPORTS:
+        assert hasattr(checked, name), f"{name} missing from {_lib.LIB_CHECKED}"
+    checked.ffts_bounds_check_enabled.restype = ctypes.c_int32
+    assert checked.ffts_bounds_check_enabled() == 1
+    normal = ctypes.CDLL(_lib.LIB_NORMAL)
+    normal.ffts_bounds_check_enabled.restype = ctypes.c_int32
+    assert normal.ffts_bounds_check_enabled() == 0
+    # the normal build has no records and touches no device to say so
+    normal.ffts_bounds_report.restype = ctypes.c_int32
+    normal.ffts_bounds_report.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32]
+    assert normal.ffts_bounds_report(None, 0, 1) == 0

@@ -139,3 +139,30 @@ def test_host_buffers_equal_device_call(lib, B, L, Hkv, chunk):
         lib.myattn_prefill_host(q.cuda(), k, v, 0)
     with pytest.raises(ValueError):
         lib.myattn_prefill_host(q, k, v, 0, pooled=(q, k))
+
+
+def test_stage_trace_records_each_layer_without_changing_the_output(lib):
+    """fftsparse_b200.trace on: the reference's timed-stage schema per layer
+    (my_attn_v6_timed.py:506-657, fused here into 3_mean_pool / 4-9_select /
+    10_kernel), positive CUDA-event times, and the same output bits as untraced."""
+    from fftsparse_b200 import trace
+    spec, q, k, v, params, fx = load_case("mixed_16k")
+    kw = dict(spec["kwargs"], block_size=spec["block_size"])
+    qc, kc, vc = q.cuda().bfloat16(), k.cuda().bfloat16(), v.cuda().bfloat16()
+    plain = lib.myattn_prefill(qc, kc, vc, 0, **kw)
+    trace.reset()
+    trace.enable()
+    try:
+        outs = [lib.myattn_prefill(qc, kc, vc, layer, **kw) for layer in (0, 1)]
+        tab = trace.times()
+        table = trace.table()
+    finally:
+        trace.disable()
+        trace.reset()
+    for o in outs:
+        assert torch.equal(o, plain)
+    assert sorted(tab) == [0, 1]
+    for layer in (0, 1):
+        assert set(tab[layer]) == {"3_mean_pool", "4-9_select", "10_kernel"}
+        assert all(len(v) == 1 and v[0] > 0.0 for v in tab[layer].values())
+    assert table["mean_excl_layer0"]["10_kernel"] == tab[1]["10_kernel"][0]
