@@ -257,3 +257,84 @@ def test_selected_mask_matches_flash_attn_on_gathered_blocks(lib, L, H, Hkv, bs)
     err = (got.float() - ref[:, 0].float()).abs()
     assert float(err.max()) <= MAX_ABS, float(err.max())
     assert float(err.mean()) <= MEAN_ABS, float(err.mean())
+
+
+def _gathered_pairs(row_ptr, col_idx, H, N, bs, pairs):
+    """(query rows, kept key positions) of each (batch, head, query block) pair:
+    the kept key blocks in ascending order, cut at the diagonal as the kernel does."""
+    out = []
+    for b, h, i in pairs:
+        r = (b * H + h) * N + i
+        sel = col_idx[row_ptr[r]:row_ptr[r + 1]].long()
+        sel = sel[sel <= i]
+        assert int(sel[-1]) == i, "the diagonal block is always kept"
+        rows = torch.arange(i * bs, (i + 1) * bs)
+        keys = torch.cat([torch.arange(j * bs, (j + 1) * bs) for j in sel.tolist()])
+        out.append((rows, keys))
+    return out
+
+
+@pytest.mark.parametrize("B,L,H,Hkv,bs,rope_base", [(1, 131072, 32, 8, 128, 500000.0),
+                                                     (2, 65536, 28, 4, 64, 1000000.0)])
+def test_bench_shape_matches_fp32_and_flash_attn(lib, B, L, H, Hkv, bs, rope_base):
+    """The BASELINE shapes at full size: config 3 as bench.py runs it (131072
+    tokens, 32 query heads over 8 KV heads, block 128) and config 5's Qwen2.5-7B
+    layer (2 x 65536 tokens, 28 over 4 heads, block 64), with the bench's synthetic
+    inputs (K/V repeat_kv-expanded, as the reference's callers pass them), keep ratio
+    0.05 and the FFTSparse-selected mask.  One head of every KV
+    group of the last sequence is checked on 40 query blocks spread over the
+    sequence, first and last included: the kernel's rows against a plain PyTorch
+    fp32 evaluation, and against flash_attn (the library behind the reference's
+    block_sparse_attn_func), on the same gathered key blocks.  The drop-in call
+    returns the same bits as the kernel called on the selected mask."""
+    import bench
+    from fftsparse_b200.synthetic import make_inputs
+    G = H // Hkv
+    q, k, v = make_inputs(L, num_q_heads=H, num_kv_heads=Hkv, dtype=torch.bfloat16, device="cuda", batch=B,
+                          rope_base=rope_base)
+    kw = dict(bench.mask_kwargs(0.05), block_size=bs)
+    mask = lib.fft_block_mask(q, k, **kw)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = lib.sparse_attention(q, k, v, mask.bits, bs, status=status)  # [B, L, H, D]
+    full = lib.myattn_prefill(q, k, v, 0, **kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(full.view(B, L, H, 128), out)
+    N = mask.n_blocks
+    row_ptr, col_idx = (t.cpu() for t in mask.csr())
+    b = B - 1
+    kv_of = (lambda h: h // G) if k.shape[1] == Hkv else (lambda h: h)  # the bench passes expanded K/V
+    heads = [g * G + (g % G) for g in range(Hkv)]  # one head per KV group, varying position in the group
+    blocks = sorted({0, 1, 2, N // 2, N - 2, N - 1} | set(range(5, N, max(1, N // 34))))[:40]
+    pairs = [(b, h, i) for h in heads for i in blocks]
+    spans = _gathered_pairs(row_ptr, col_idx, H, N, bs, pairs)
+    scale = 128 ** -0.5
+    errs = []
+    for (_, h, _), (rows, keys) in zip(pairs, spans):
+        rows, keys = rows.cuda(), keys.cuda()
+        s = (q[b, h, rows].float() @ k[b, kv_of(h), keys].float().T) * scale
+        s = s.masked_fill(keys[None, :] > rows[:, None], float("-inf"))
+        ref = torch.softmax(s, dim=-1) @ v[b, kv_of(h), keys].float()
+        errs.append((out[b, rows, h].float() - ref).abs().flatten())
+    err = torch.cat(errs)
+    assert float(err.max()) <= MAX_ABS, float(err.max())
+    assert float(err.mean()) <= MEAN_ABS, float(err.mean())
+    try:
+        from flash_attn import flash_attn_varlen_func
+    except Exception:  # noqa: BLE001 - the fp32 comparison above stands on its own
+        return
+    qi = torch.cat([r for r, _ in spans]).cuda()
+    ki = torch.cat([kk for _, kk in spans]).cuda()
+    hq = torch.cat([torch.full((r.numel(),), h) for (_, h, _), (r, _) in zip(pairs, spans)]).cuda()
+    hk = torch.cat([torch.full((kk.numel(),), kv_of(h)) for (_, h, _), (_, kk) in zip(pairs, spans)]).cuda()
+    cu_q = torch.tensor([0] + [r.numel() for r, _ in spans]).cumsum(0).int().cuda()
+    lens_k = [kk.numel() for _, kk in spans]
+    cu_k = torch.tensor([0] + lens_k).cumsum(0).int().cuda()
+    try:
+        ref = flash_attn_varlen_func(q[b][hq, qi].unsqueeze(1), k[b][hk, ki].unsqueeze(1),
+                                     v[b][hk, ki].unsqueeze(1), cu_q, cu_k, bs, max(lens_k), causal=True)
+    except RuntimeError:
+        return
+    err = (out[b][qi, hq].float() - ref[:, 0].float()).abs()
+    assert float(err.max()) <= MAX_ABS, float(err.max())
+    assert float(err.mean()) <= MEAN_ABS, float(err.mean())
