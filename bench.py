@@ -726,12 +726,35 @@ def run_ours(args):
         sel_kernels = kernel_times_us(lambda: F.fft_block_mask(ql, kl, pooled=(mask.q_pooled, mask.k_pooled), **kw))
     except Exception as exc:  # noqa: BLE001 - the activity trace is a report, not a requirement
         sel_kernels = {"error": f"{exc}"[:200]}
+    # ---- N > 1: the fused gather's parts on every rank (its own heads' attention
+    # without pushes, the same attention storing every tile to all peers, then the
+    # flag store and the wait for the slowest peer)
+    gather_parts = None
+    if world > 1 and pg is not None:
+        torch.cuda.synchronize(dev)
+        barrier()
+        tim = []
+        for _ in range(reps):
+            pg.run(ql, kl, vl, mask.bits, BLOCK, True, shard, timing=tim)
+        torch.cuda.synchronize(dev)
+        pg.check()
+        t_push = sum(a.elapsed_time(b) for a, b, _ in tim) / reps
+        t_wait = sum(b.elapsed_time(c) for _, b, c in tim) / reps
+        mine = torch.tensor([t_attn, t_push, t_wait], device=dev)
+        every = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        every = torch.stack(every).cpu().tolist()
+        gather_parts = {"attention_ms_per_rank": [round(r[0], 4) for r in every],
+                        "attention_with_push_ms_per_rank": [round(r[1], 4) for r in every],
+                        "flag_wait_ms_per_rank": [round(r[2], 4) for r in every]}
     stages = {"pool_ms": round(t_pool, 4), "pool_gbs": round(pool_bytes / (t_pool * 1e-3) / 1e9, 1),
               "pool_frac_hbm": round(pool_bytes / (t_pool * 1e-3) / 1e9 / hbm_peak, 4),
               "select_ms": round(t_mask - t_pool, 4), "select_kernels_us": sel_kernels,
               "attention_ms": round(t_attn, 4),
               "block_density": round(mask.density(), 5),
               "stripe_heads": int(mask.is_stripe.sum().item())}
+    if gather_parts is not None:
+        stages["gather_parts"] = gather_parts
 
     # ---- selection sweep: BASELINE config 3 sweeps keep ratios {0.02, 0.05, 0.1}, and
     # the reference's only published 128K number is threshold mode at T = 0.9.  The

@@ -235,7 +235,10 @@ class PeerGather:
         self.epoch = 0
         dist.barrier(group)  # every rank has mapped every buffer before the first push
 
-    def run(self, ql, kl, vl, bits, block_size: int, causal: bool, shard: Shard) -> torch.Tensor:
+    def run(self, ql, kl, vl, bits, block_size: int, causal: bool, shard: Shard, timing=None) -> torch.Tensor:
+        """The rank's attention with its output pushed to every peer, then the flag
+        exchange.  With a list ``timing`` (epilogue pushes), three timing events are
+        appended per call: before the attention, after it, after the flag wait."""
         from . import _lib
         from .prefill import sparse_attention
 
@@ -251,13 +254,21 @@ class PeerGather:
         local = buf.data_ptr() + shard.h_lo * pitch
         bases = self._dst[slot]
         if self.push == "epilogue":
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if timing is not None else None
+            if evs:
+                evs[0].record(cur)
             mine = buf[:, shard.h_lo:shard.h_hi].permute(0, 2, 1, 3)
             sparse_attention(ql, kl, vl, bits, block_size, causal=causal, out=mine, status=self.status,
                              peers=[b + shard.h_lo * pitch for b in bases[:self._npeers]])
+            if evs:
+                evs[1].record(cur)
             n = self._npeers + 1
             _lib.check(lib.ffts_signal(self._all_flags, (ct.c_void_p * n)(*([cur.cuda_stream] * n)), n, e))
             _lib.check(lib.ffts_wait_flags(self.flags.data_ptr(), self.world, e, self.status.data_ptr(),
                                            cur.cuda_stream))
+            if evs:
+                evs[2].record(cur)
+                timing.append(evs)
             self.status_word.read_back(cur)
             return buf
         # the buffer used now was last read by this rank's pushes two calls ago
