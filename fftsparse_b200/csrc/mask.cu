@@ -668,10 +668,15 @@ __device__ __forceinline__ bool range_ok(const int32_t *__restrict__ safe, int64
 // blocks of each other): the normalised variance of the adjacent differences
 // along each sampled block-score diagonal (my_attn_v7.py:342-351), written to
 // nv[bh * 64 + s]; corr_select_kernel averages them in sample order.  The k rows
-// of a 64-row tile and the q rows every lag of the group pairs them with are
-// staged in shared memory once per tile; each score is one fp64 FMA chain in d
-// order and the three reductions per lag are the 256-lane canonical ones.
-constexpr int kDiagTile = 64;
+// of a tile (128 rows, or 64 where shared memory is short) and the q rows every
+// lag of the group pairs them with are staged in shared memory once per tile;
+// each score is one fp64 chain in d order, and the three reductions per lag are
+// the 256-lane canonical ones.  A thread forms kDiagChains scores of one k row
+// (lags g, g + 256 / tile, ...) side by side: the chains' fp64 additions are
+// independent, so their latencies overlap, and the k row is read once for all.
+constexpr int kDiagTileMax = 128;
+constexpr int kDiagTileMin = 64;
+constexpr int kDiagChains = 4;
 constexpr int kDiagGroup = 8;
 
 // row stride (elements) of staged rows: an odd number of 32-bit words
@@ -687,7 +692,7 @@ struct DiagGroups {
 template <typename T>
 __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ kb, int H, int Hkv, int D,
                                 const ffts_mask_params &p, double *__restrict__ nv, int first, int G, int bh,
-                                int gmax, unsigned char *smem_raw, const int32_t *__restrict__ safe_q,
+                                int gmax, int dt, unsigned char *smem_raw, const int32_t *__restrict__ safe_q,
                                 const int32_t *__restrict__ safe_k) {
   const int N = p.n_blocks;
   const int QS = stage_stride<T>(D);
@@ -697,10 +702,10 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
     lo = min(lo, p.diag_taus[FFTS_INDEX(first + g, FFTS_MAX_DIAG_SAMPLES)]);
     hi = max(hi, p.diag_taus[FFTS_INDEX(first + g, FFTS_MAX_DIAG_SAMPLES)]);
   }
-  const int wrows = kDiagTile + (hi - lo);
-  T *ks = reinterpret_cast<T *>(smem_raw);           // [kDiagTile][QS]
-  T *qw = ks + kDiagTile * QS;                        // [wrows][QS]
-  float *vals = reinterpret_cast<float *>(smem_raw + ((size_t(kDiagTile + wrows) * QS * sizeof(T) + 15) & ~size_t(15)));
+  const int wrows = dt + (hi - lo);
+  T *ks = reinterpret_cast<T *>(smem_raw);           // [dt][QS]
+  T *qw = ks + dt * QS;                               // [wrows][QS]
+  float *vals = reinterpret_cast<float *>(smem_raw + ((size_t(dt + wrows) * QS * sizeof(T) + 15) & ~size_t(15)));
   // [gmax][256], 16-byte aligned whatever gmax * N is
   double *part = reinterpret_cast<double *>((reinterpret_cast<uintptr_t>(vals + gmax * N) + 15) & ~uintptr_t(15));
   const int b = bh / H, h = bh % H;
@@ -711,28 +716,28 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
   constexpr int V = Elem<T>::kVec;
   const int vrow = D / V;
   const int mmax = N - lo - 1;
-  for (int t0 = 0; t0 < mmax; t0 += kDiagTile) {
-    // k rows [t0, t0 + 64) and q rows [t0 + lo, t0 + hi + 64)
+  for (int t0 = 0; t0 < mmax; t0 += dt) {
+    // k rows [t0, t0 + dt) and q rows [t0 + lo, t0 + hi + dt)
     constexpr int U = 8;  // 16-byte loads in flight per thread before their stores
-    const int total = (kDiagTile + wrows) * vrow;
+    const int total = (dt + wrows) * vrow;
     for (int base = tid; base < total; base += U * blockDim.x) {
       uint4 raw[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int idx = base + u * blockDim.x;
         const int rr = idx / vrow, v = idx - rr * vrow;
-        const bool isk = rr < kDiagTile;
-        const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
+        const bool isk = rr < dt;
+        const int row = isk ? t0 + rr : t0 + lo + (rr - dt);
         if (idx < total && row < N) raw[u] = *reinterpret_cast<const uint4 *>((isk ? k : q) + int64_t(row) * D + v * V);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int idx = base + u * blockDim.x;
         const int rr = idx / vrow, v = idx - rr * vrow;
-        const bool isk = rr < kDiagTile;
-        const int row = isk ? t0 + rr : t0 + lo + (rr - kDiagTile);
+        const bool isk = rr < dt;
+        const int row = isk ? t0 + rr : t0 + lo + (rr - dt);
         if (idx < total && row < N) {
-          T *dst = isk ? ks + rr * QS : qw + (rr - kDiagTile) * QS;
+          T *dst = isk ? ks + rr * QS : qw + (rr - dt) * QS;
           const T *e = reinterpret_cast<const T *>(&raw[u]);
 #pragma unroll
           for (int c = 0; c < V; ++c) dst[v * V + c] = e[c];
@@ -740,35 +745,45 @@ __device__ void diag_group_body(const T *__restrict__ qb, const T *__restrict__ 
       }
     }
     __syncthreads();
-    for (int idx = tid; idx < G * kDiagTile; idx += 2 * blockDim.x) {
-      // two (lag, row) pairs per pass: idx and idx + blockDim.x
-      const int idx2 = idx + blockDim.x;
-      const int g1 = idx / kDiagTile, t1 = t0 + idx % kDiagTile;
-      const int g2 = idx2 / kDiagTile, t2 = t0 + idx2 % kDiagTile;
-      const int tau1 = p.diag_taus[first + g1];
-      const bool v1 = t1 < N - tau1 - 1;
-      const bool v2 = idx2 < G * kDiagTile && t2 < N - p.diag_taus[first + min(g2, G - 1)] - 1;
-      const int tau2 = v2 ? p.diag_taus[first + g2] : tau1;
-      // the q rows of both pairs lie in the staged window [t0 + lo, t0 + hi + 64)
-      const T *qa = qw + FFTS_INDEX(t1 + tau1 - t0 - lo, wrows) * QS, *ka = ks + (t1 - t0) * QS;
-      const T *qb2 = qw + FFTS_INDEX((v2 ? t2 : t1) + tau2 - t0 - lo, wrows) * QS;
-      const T *kb2 = ks + ((v2 ? t2 : t1) - t0) * QS;
-      double a1 = 0.0, a2 = 0.0;
+    // kDiagChains scores per thread: (lag g + c * 256 / dt, row t) for c < kDiagChains,
+    // all on the k row t (blockDim.x = 256 is a multiple of dt)
+    for (int base = tid; base < G * dt; base += kDiagChains * blockDim.x) {
+      const int t = t0 + base % dt;  // the same row for every chain of this thread
+      int gc[kDiagChains];
+      bool vc[kDiagChains];
+      const T *qc[kDiagChains];
+#pragma unroll
+      for (int c = 0; c < kDiagChains; ++c) {
+        const int idx = base + c * blockDim.x;
+        gc[c] = idx / dt;
+        const int tau = p.diag_taus[first + min(gc[c], G - 1)];
+        vc[c] = idx < G * dt && t < N - tau - 1;
+        // the q row t + tau lies in the staged window [t0 + lo, t0 + hi + dt)
+        qc[c] = qw + FFTS_INDEX(t + tau - t0 - lo, wrows) * QS;
+      }
+      const T *ka = ks + (t - t0) * QS;
+      double a[kDiagChains];
+#pragma unroll
+      for (int c = 0; c < kDiagChains; ++c) a[c] = 0.0;
       bool exact32 = false;
       if constexpr (sizeof(T) == 2) exact32 = safe_q != nullptr && range_ok(safe_q, bh) && range_ok(safe_k, kh);
       if (exact32) {
         for (int d = 0; d < D; ++d) {
-          a1 = __dadd_rn(a1, (double)__fmul_rn(Elem<T>::to_f32(qa[d]), Elem<T>::to_f32(ka[d])));
-          a2 = __dadd_rn(a2, (double)__fmul_rn(Elem<T>::to_f32(qb2[d]), Elem<T>::to_f32(kb2[d])));
+          const float kf = Elem<T>::to_f32(ka[d]);
+#pragma unroll
+          for (int c = 0; c < kDiagChains; ++c)
+            a[c] = __dadd_rn(a[c], (double)__fmul_rn(Elem<T>::to_f32(qc[c][d]), kf));
         }
       } else {
         for (int d = 0; d < D; ++d) {
-          a1 = __fma_rn((double)Elem<T>::to_f32(qa[d]), (double)Elem<T>::to_f32(ka[d]), a1);
-          a2 = __fma_rn((double)Elem<T>::to_f32(qb2[d]), (double)Elem<T>::to_f32(kb2[d]), a2);
+          const double kd = (double)Elem<T>::to_f32(ka[d]);
+#pragma unroll
+          for (int c = 0; c < kDiagChains; ++c) a[c] = __fma_rn((double)Elem<T>::to_f32(qc[c][d]), kd, a[c]);
         }
       }
-      if (v1 && FFTS_IN_RANGE(g1, gmax)) vals[g1 * N + t1] = __double2float_rn(__ddiv_rn(a1, sqrtD));
-      if (v2 && FFTS_IN_RANGE(g2, gmax)) vals[g2 * N + t2] = __double2float_rn(__ddiv_rn(a2, sqrtD));
+#pragma unroll
+      for (int c = 0; c < kDiagChains; ++c)
+        if (vc[c] && FFTS_IN_RANGE(gc[c], gmax)) vals[gc[c] * N + t] = __double2float_rn(__ddiv_rn(a[c], sqrtD));
     }
     __syncthreads();
   }
@@ -1008,7 +1023,7 @@ template <typename T, int R>
 __global__ void __launch_bounds__(256, 1) select_stage1_kernel(const T *__restrict__ qb, const T *__restrict__ kb,
                                                                int H, int Hkv, int D, ffts_mask_params p, int M,
                                                                int nf, int nchunk, int nBH, int nDG,
-                                                               DiagGroups gr, int gmax,
+                                                               DiagGroups gr, int gmax, int dtile,
                                                                float2 *__restrict__ partial, double *__restrict__ nv,
                                                                uint32_t *__restrict__ colsel,
                                                                uint32_t *__restrict__ lastsel,
@@ -1022,7 +1037,7 @@ __global__ void __launch_bounds__(256, 1) select_stage1_kernel(const T *__restri
     colrow_body<T>(qb, kb, H, Hkv, D, p, colsel, lastsel, bid, smem_raw, hist, bc);
   } else if (bid < nBH + nDG) {
     const int e = bid - nBH, g = e % gr.n;
-    diag_group_body<T>(qb, kb, H, Hkv, D, p, nv, gr.first[g], gr.count[g], e / gr.n, gmax, smem_raw, safe_q,
+    diag_group_body<T>(qb, kb, H, Hkv, D, p, nv, gr.first[g], gr.count[g], e / gr.n, gmax, dtile, smem_raw, safe_q,
                        safe_k);
   } else {
     const int f = bid - nBH - nDG;
@@ -1291,11 +1306,14 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
   const int gmax = std::max(1, std::min(kDiagGroup, 8192 / N));
   const size_t st = size_t(D + (elem == 2 ? 2 : 1)) * elem;
   const int64_t room = int64_t(200 * 1024) - int64_t(gmax) * N * 4 - int64_t(gmax) * kLanes * 8 - 64;
-  const int span = int(std::max<int64_t>(0, std::min<int64_t>(elem == 2 ? 192 : 64, room / int64_t(st) - 2 * kDiagTile)));
+  // stripe tiles of 128 k rows where the staged rows fit, else 64; lag span up to 192 blocks (64 for fp32)
+  const int span_cap = elem == 2 ? 192 : 64;
+  const int dtile = room / int64_t(st) - 2 * kDiagTileMax >= span_cap ? kDiagTileMax : kDiagTileMin;
+  const int span = int(std::max<int64_t>(0, std::min<int64_t>(span_cap, room / int64_t(st) - 2 * dtile)));
   const DiagGroups gr = make_diag_groups(p, gmax, span);
   const int nDG = (p.corr_on && !p.stripe_all_diffuse) ? gr.n * int(BH) : 0;
   size_t smem1 = colrow_smem(N, int(D), elem);
-  if (nDG) smem1 = std::max(smem1, size_t(2 * kDiagTile + span) * st + size_t(gmax) * N * 4 + size_t(gmax) * kLanes * 8 + 64);
+  if (nDG) smem1 = std::max(smem1, size_t(2 * dtile + span) * st + size_t(gmax) * N * 4 + size_t(gmax) * kLanes * 8 + 64);
   if (nF) smem1 = std::max(smem1, R ? fft_warp_smem_rt(R, N, elem) : fft_partial_smem(M, nf));
   const unsigned grid1 = unsigned(nF + nDG + int(BH));
 #define FFTS_STAGE1(RR)                                                                                          \
@@ -1305,7 +1323,7 @@ static int run_block_mask(const T *qb, const T *kb, int64_t B, int64_t H, int64_
       if (rc1) return rc1;                                                                                       \
     }                                                                                                            \
     select_stage1_kernel<T, RR><<<grid1, 256, smem1, stream>>>(qb, kb, int(H), int(Hkv), int(D), p, M, nf, nchunk, \
-                                                               int(BH), nDG, gr, gmax, ws.partial, ws.nv,         \
+                                                               int(BH), nDG, gr, gmax, dtile, ws.partial, ws.nv,  \
                                                                ws.colsel, ws.lastsel, safe_q, safe_k);           \
     break;                                                                                                       \
   }
