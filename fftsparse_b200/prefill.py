@@ -526,7 +526,7 @@ def _host_streams(device: torch.device):
     return _HOST_STREAMS[idx]
 
 
-def myattn_prefill_host(query_states, key_states, value_states, layer_idx, chunk_heads: int = 4,
+def myattn_prefill_host(query_states, key_states, value_states, layer_idx, chunk_heads: int = 1,
                         out: Optional[torch.Tensor] = None, device=None, **kwargs):
     """``myattn_prefill`` on host buffers, with the copies overlapped with the work.
 
@@ -535,11 +535,13 @@ def myattn_prefill_host(query_states, key_states, value_states, layer_idx, chunk
     myattn_prefill's.  Returns ``out``, a pinned CPU [B, L, H*D] bf16 tensor
     (allocated when None), equal bit for bit to myattn_prefill on the same inputs
     on the device: the selection and the attention of a head read only that head
-    (and its KV head).  Heads go in chunks of ``chunk_heads`` (a multiple of the
-    group size H / Hkv): chunk c+1 is copied in on one stream while chunk c is
+    (and its KV head).  Heads go in chunks of ``chunk_heads``, rounded to a
+    multiple of the group size H / Hkv (default: one head, or one KV group of
+    un-expanded K/V): chunk c+1 is copied in on one stream while chunk c is
     selected and attended on the current stream and chunk c-1's output columns
-    are copied back on a third, so the layer takes about as long as its input
-    copy.  The call returns once the work is queued; the result is complete when
+    are copied back on a third, so the layer takes about as long as its copies
+    (small chunks keep the last chunk's work and read-back, which nothing
+    overlaps, short).  The call returns once the work is queued; the result is complete when
     the current stream's work is (``torch.cuda.current_stream().synchronize()``).
     The calibration collector, when installed, records one entry per chunk.
     """
