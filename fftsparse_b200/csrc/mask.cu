@@ -384,14 +384,36 @@ __device__ uint32_t block_select_rank(const uint32_t *keys, int n, int rank, int
       if ((kk & mask) == prefix) atomicAdd(&hist[(kk >> shift) & 255], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int c = 0, dsel = 255;
-      for (int d = 0; d < 256; ++d) {
-        if (c + hist[d] > rank) { dsel = d; break; }
-        c += hist[d];
+    if (threadIdx.x < 32) {
+      // the first digit d whose running count passes `rank`, and the count below it
+      // (the total when none does): lane l scans bins [8l, 8l + 8) after a warp
+      // prefix sum of the lanes' totals
+      const int lane = threadIdx.x;
+      int c[8], tot = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[e] = hist[lane * 8 + e];
+        tot += c[e];
       }
-      bc[0] = dsel;
-      bc[1] = c;
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int excl = incl - tot;
+      const unsigned ball = __ballot_sync(0xffffffffu, rank >= excl && rank < incl);
+      const int src = ball ? __ffs(ball) - 1 : 31;
+      if (lane == src) {
+        int cc = excl, dsel = 255;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (cc + c[e] > rank) { dsel = lane * 8 + e; break; }
+          cc += c[e];
+        }
+        bc[0] = dsel;
+        bc[1] = cc;
+      }
     }
     __syncthreads();
     rank -= bc[1];
