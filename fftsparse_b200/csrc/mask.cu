@@ -1145,6 +1145,20 @@ __device__ void warp_topk_bits(const uint32_t *keys, int n, int k, uint32_t *wor
 }
 
 // ------------------------------------------------------------ mask build
+// bits t < x of a word (x clipped to [0, 32])
+__device__ __forceinline__ uint32_t bits_below(int x) {
+  return x <= 0 ? 0u : (x >= 32 ? 0xffffffffu : ((1u << x) - 1u));
+}
+
+// bits [base, base + 32) of the bit array words[0..W) as one word (bit k = bit
+// base + k); positions outside the array (base may be negative) read as 0
+__device__ __forceinline__ uint32_t lag_window(const uint32_t *words, int W, int base) {
+  const int wlo = base >> 5, sh = base & 31;  // floor division, also for base < 0
+  const uint32_t a = (wlo >= 0 && wlo < W) ? words[FFTS_INDEX(wlo, W)] : 0u;
+  const uint32_t b = (wlo + 1 >= 0 && wlo + 1 < W) ? words[FFTS_INDEX(wlo + 1, W)] : 0u;
+  return sh ? (a >> sh) | (b << (32 - sh)) : a;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) mask_build_kernel(const T *__restrict__ qb,
                                                          const T *__restrict__ kb, int H, int Hkv,
@@ -1218,25 +1232,27 @@ __global__ void __launch_bounds__(256) mask_build_kernel(const T *__restrict__ q
   const uint32_t *ts = tausel + int64_t(bh) * W;
   const uint32_t *cs = colsel + int64_t(bh) * W;
   const uint32_t *ls = lastsel + int64_t(bh) * W;
+  const bool lag_on = p.corr_on && stripe;
   for (int e = threadIdx.x; e < rows * W; e += blockDim.x) {
     const int r = e / W, w = e - r * W;
     const int i = i0 + r;
-    uint32_t word = 0;
-    const uint32_t cw = col_apply ? cs[w] : 0u;
-    const uint32_t lw = (p.last_on && i == N - 1) ? ls[w] : 0u;
-    const uint32_t dw = diffuse ? rowbits[r * W + w] : 0u;
-    for (int t = 0; t < 32; ++t) {
-      const int j = w * 32 + t;
-      if (j > i) break;
-      const int tau = i - j;
-      bool on = j < p.keep_sink || j >= N - p.keep_recent || tau <= p.local_window;
-      if (p.corr_on && stripe)
-        on |= tau >= p.remote_start && ((ts[FFTS_INDEX(tau >> 5, W)] >> (tau & 31)) & 1u) && j >= p.keep_sink;
-      on |= (dw >> t) & 1u;
-      on |= (cw >> t) & 1u;
-      on |= (lw >> t) & 1u;
-      word |= uint32_t(on) << t;
+    const int j0 = w * 32;  // bit t of the word is key block j = j0 + t, lag tau = i - j
+    // kept: j < keep_sink, j >= N - keep_recent, tau <= local_window (j >= i - local_window),
+    // and for a stripe head with the lag mask the selected lags tau >= remote_start
+    // (j <= i - remote_start) among j >= keep_sink; then the diffuse, column and
+    // last-row selections; nothing above the diagonal (j <= i)
+    uint32_t word = bits_below(p.keep_sink - j0) | ~bits_below(N - p.keep_recent - j0) |
+                    ~bits_below(i - p.local_window - j0);
+    if (lag_on) {
+      // bit t <- selected-lag bit tau = i - j0 - t: the 32 lag bits from tau = i - j0 - 31
+      // up, reversed
+      const uint32_t lagw = __brev(lag_window(ts, W, i - j0 - 31));
+      word |= lagw & bits_below(i - p.remote_start + 1 - j0) & ~bits_below(p.keep_sink - j0);
     }
+    if (diffuse) word |= rowbits[r * W + w];
+    if (col_apply) word |= cs[w];
+    if (p.last_on && i == N - 1) word |= ls[w];
+    word &= bits_below(i + 1 - j0);
     bits[(int64_t(bh) * N + i) * W + w] = word;
     atomicAdd(&cnt[r], __popc(word));
   }
