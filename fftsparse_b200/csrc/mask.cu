@@ -491,18 +491,24 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
   __shared__ int hist[256];
   __shared__ int bc[4];
   __shared__ float red[32];
+  __shared__ double nvs[FFTS_MAX_DIAG_SAMPLES];
   const int bh = blockIdx.x;
   const int F = M / 2 + 1;
   const int bits = ilog2_ceil(M);
   const int W = (N + 31) / 32;
   const int stride = kMaxFFT / M;
+  // the per-lag statistics are loaded side by side, then summed in sample order by one thread
+  const bool stripe_test = p.corr_on && !p.stripe_all_diffuse;
+  if (stripe_test)
+    for (int s = threadIdx.x; s < p.n_diag_samples; s += blockDim.x)
+      nvs[FFTS_INDEX(s, FFTS_MAX_DIAG_SAMPLES)] = nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + s];
+  __syncthreads();
   if (threadIdx.x == 0) {
     float svar = INFINITY;
     int stripe = 0;
-    if (p.corr_on && !p.stripe_all_diffuse) {
+    if (stripe_test) {
       double total = 0.0;
-      for (int s = 0; s < p.n_diag_samples; ++s)
-        total = __dadd_rn(total, nv[int64_t(bh) * FFTS_MAX_DIAG_SAMPLES + FFTS_INDEX(s, FFTS_MAX_DIAG_SAMPLES)]);
+      for (int s = 0; s < p.n_diag_samples; ++s) total = __dadd_rn(total, nvs[FFTS_INDEX(s, FFTS_MAX_DIAG_SAMPLES)]);
       svar = __double2float_rn(__ddiv_rn(total, (double)p.n_diag_samples));
       stripe = svar <= p.stripe_threshold;
     }
@@ -522,10 +528,17 @@ __global__ void __launch_bounds__(512) corr_select_kernel(const float2 *__restri
   const float2 *part = partial + int64_t(bh) * nchunk * F;
   for (int f = threadIdx.x; f < F; f += blockDim.x) {
     float2 s = make_float2(0.0f, 0.0f);
-    for (int c = 0; c < nchunk; ++c) {
-      const float2 v = part[int64_t(c) * F + f];
-      s.x = __fadd_rn(s.x, v.x);
-      s.y = __fadd_rn(s.y, v.y);
+    for (int c0 = 0; c0 < nchunk; c0 += 8) {  // eight chunks' loads in flight, added in chunk order
+      float2 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = c0 + u < nchunk ? part[int64_t(c0 + u) * F + f] : make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (c0 + u < nchunk) {
+          s.x = __fadd_rn(s.x, v[u].x);
+          s.y = __fadd_rn(s.y, v[u].y);
+        }
+      }
     }
     X[bitrev(f, bits)] = s;
     if (f > 0 && f < M / 2) X[bitrev(M - f, bits)] = make_float2(s.x, -s.y);
